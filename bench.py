@@ -1,0 +1,365 @@
+"""SGSA layer forward benchmark (the driver's contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one SGSA layer forward (chunked delta stage, causal top-k
+indexer, sparse attention over the selected rows, gate) over the
+``b200_bf16`` configuration: B=4, T=8192, H=16, d=128, top-k 512, indexer dim
+64, bf16 inputs with fp32 accumulation.  Multi-GPU runs are (batch x head)
+shards with no communication (weak scaling): rank r processes its own
+configuration-sized shard drawn with seed r.
+
+``value`` is whole-job tokens/s with inputs resident in HBM (CUDA events on
+the launching stream, max over ranks).  ``e2e`` is the same metric through the
+public op with host (pinned) inputs: the host->device copies of all inputs and
+the device->host copy of the output are inside its timed region.  The inputs
+(q, k, v, iq, ik, mix: 470 MB per step) are larger than the 126 MB L2, so no
+extra flush is done between steps.
+
+``--impl reference`` times the CPU restatement of the reference's algorithm
+(oracle/, float64, OpenMP over all host threads) on a bounded sample of the
+same workload, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "SGSA layer fwd tokens/s"
+UNIT = "tokens/s"
+CONFIG_NAME = "b200_bf16"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def algorithmic_counts(cfg):
+    """Per-layer-forward FLOPs and bytes of each stage (formulas in DESIGN.md)."""
+    B, T, H, D, K, DI = cfg.B, cfg.T, cfg.H, cfg.D, cfg.top_k, cfg.d_idx
+    C = cfg.chunk
+    f_delta = B * T * H * (6 * D * D + 2 * C * (3 * D + 2 * D))
+    f_idx = B * H * T * (T + 1) * DI  # 2 * DI per causal pair, T(T+1)/2 pairs
+    sel = sum(min(K, t + 1) for t in range(T))
+    f_sp = B * H * sel * 4 * D
+    bytes_gather = B * H * sel * (2 * D) * 2
+    bytes_io = B * T * H * (2 * 3 * D + 2 * 2 * DI + 2 * D + 2 * D + 2 * 2) + 2 * B * H * D * D * 4
+    return dict(f_delta=f_delta, f_idx=f_idx, f_sp=f_sp, bytes_gather=bytes_gather,
+                bytes_io=bytes_io, selected=B * H * sel)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out = ""
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def setup_dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return ws, rank, local
+
+
+def max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws):
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def cpu_reference(cfg, cores: int, budget_s: float = 20.0):
+    """Time the oracle port on a bounded sample; returns (tokens/s, sample text, seconds)."""
+    from oracle import oracle
+    from sgsa_b200.inputs import make_inputs
+
+    oracle.set_num_threads(cores)
+    small = cfg.scaled(B=1)
+    x = make_inputs(small, seed=0)
+    hs = min(cfg.H, max(1, cores))
+    t0 = time.perf_counter()
+    oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], heads=(0, hs))
+    t_delta = (time.perf_counter() - t0) / hs * cores  # core-seconds per (b,h)
+    nq = 64
+    mid = cfg.T // 2
+    tr = (mid - nq // 2, mid + nq // 2)
+    t0 = time.perf_counter()
+    idx = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k, t_range=tr)
+    od = torch.zeros(1, cfg.T, cfg.H, cfg.D)
+    oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx, od, x["mix"], t_range=tr)
+    t_sel = time.perf_counter() - t0  # all H heads, nq queries, in parallel
+    # queries around T/2 have the mean causal prefix, so work scales by T/nq
+    per_bh_sel = t_sel * cores / cfg.H * (cfg.T / nq)
+    total_core_s = cfg.B * cfg.H * (t_delta + per_bh_sel)
+    wall = total_core_s / cores
+    sample = (f"delta: b0 heads 0..{hs - 1} full T={cfg.T}; indexer+attention+gate: b0 all "
+              f"{cfg.H} heads, queries [{tr[0]},{tr[1]}) (mean causal prefix) scaled by T/{nq}; "
+              f"extrapolated to B={cfg.B} H={cfg.H} at {cores} threads")
+    return cfg.tokens / wall, sample, t_delta * hs / cores + t_sel
+
+
+def run_reference(args, ws, rank):
+    from sgsa_b200.inputs import CONFIGS
+
+    if rank != 0:
+        return
+    cfg = CONFIGS[CONFIG_NAME]
+    cores = os.cpu_count() or 1
+    vals, sample = [], ""
+    for _ in range(max(args.warmup, 0)):
+        pass  # the CPU port has no warm-up effects worth a full step
+    for _ in range(max(args.steps, 1)):
+        v, sample, _ = cpu_reference(cfg, cores)
+        vals.append(v)
+    v = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cfg.tokens / v * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded, configs[1] shapes/distributions)",
+        "config": {"workload": CONFIG_NAME, "B": cfg.B, "T": cfg.T, "H": cfg.H, "d": cfg.D,
+                   "top_k": cfg.top_k, "d_idx": cfg.d_idx, "chunk": cfg.chunk},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def stage_times(cfg, d, reps=3):
+    """Per-stage device time (ms) of the layer, each stage called through the C ABI."""
+    from sgsa_b200 import _lib, ops
+
+    lib = _lib.load()
+    st = torch.cuda.current_stream()
+    B, T, H, D = cfg.B, cfg.T, cfg.H, cfg.D
+    od = torch.empty(B, T, H, D, device="cuda", dtype=torch.float32)
+    ix = torch.empty(B, H, T, cfg.top_k, device="cuda", dtype=torch.int32)
+    flags = _lib.FLAG_OUT_F32
+    ws = torch.empty(lib.sgsa_chunk_fwd_workspace_size(B, T, H, D, flags), device="cuda",
+                     dtype=torch.uint8)
+    out = torch.empty_like(d["q"])
+    P = lambda t: t.data_ptr()
+
+    def delta():
+        _lib.check(lib.sgsa_chunk_fwd(P(d["q"]), P(d["k"]), P(d["v"]), P(d["beta"]), P(d["gamma"]),
+                                      None, None, None, None, P(od), None, B, T, H, D,
+                                      _lib.DTYPE_BF16, 64, flags, P(ws), ws.numel(), st.cuda_stream),
+                   "chunk")
+
+    def index():
+        _lib.check(lib.sgsa_indexer_topk(P(d["iq"]), P(d["ik"]), P(ix), B, T, H, cfg.d_idx,
+                                         cfg.top_k, _lib.DTYPE_BF16, st.cuda_stream), "indexer")
+
+    def attn():
+        _lib.check(lib.sgsa_sparse_attn_mix(P(d["q"]), P(d["k"]), P(d["v"]), P(ix), P(od),
+                                            P(d["mix"]), P(out), B, T, H, D, cfg.top_k,
+                                            1.0 / math.sqrt(D), 1, _lib.DTYPE_BF16,
+                                            st.cuda_stream), "attn")
+
+    res = {}
+    for name, fn in (("delta", delta), ("indexer_topk", index), ("sparse_attn_mix", attn)):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / reps
+    del ops
+    return res
+
+
+def run_ours(args, ws, rank, local):
+    from sgsa_b200 import ops
+    from sgsa_b200.inputs import CONFIGS, make_inputs
+
+    cfg = CONFIGS[CONFIG_NAME]
+    host = make_inputs(cfg, seed=rank)
+    d = {n: t.cuda() for n, t in host.items()}
+    names = ["q", "k", "v", "beta", "gamma", "iq", "ik", "mix"]
+
+    def step():
+        return ops.sgsa_layer_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"], d["ik"],
+                                  d["mix"], cfg.top_k)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier(ws)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        barrier(ws)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws)
+    value = ws * cfg.tokens / (ms / 1e3)
+
+    # end to end: pinned host inputs -> device -> layer -> host output
+    pinned = {n: host[n].pin_memory() for n in names}
+    out_host = torch.empty(cfg.B, cfg.T, cfg.H, cfg.D, dtype=cfg.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        g = {n: pinned[n].to("cuda", non_blocking=True) for n in names}
+        o = ops.sgsa_layer_fwd(g["q"], g["k"], g["v"], g["beta"], g["gamma"], g["iq"], g["ik"],
+                               g["mix"], cfg.top_k)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier(ws)
+    e2e_steps = max(1, min(args.steps, 5))
+    e0.record(st)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(st)
+    barrier(ws)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws)
+
+    stages = stage_times(cfg, d)
+    cnt = algorithmic_counts(cfg)
+    hbm, tfl, src = peaks()
+    # the dominant kernel and its roofline
+    dom = max(stages, key=stages.get)
+    if dom == "sparse_attn_mix":
+        ach = cnt["bytes_gather"] / (stages[dom] / 1e3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s"}
+    elif dom == "indexer_topk":
+        ach = cnt["f_idx"] / (stages[dom] / 1e3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tfl, "unit": "TFLOP/s"}
+    else:
+        ach = cnt["f_delta"] / (stages[dom] / 1e3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tfl, "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = src
+    roof["traffic"] = None
+    roof["stage_ms"] = stages
+
+    if rank == 0:
+        cores = os.cpu_count() or 1
+        cpu_v, sample, secs = cpu_reference(cfg, cores)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, configs[1] shapes/distributions; rank r uses seed r)",
+            "config": {"workload": CONFIG_NAME, "B": cfg.B, "T": cfg.T, "H": cfg.H, "d": cfg.D,
+                       "top_k": cfg.top_k, "d_idx": cfg.d_idx, "chunk": cfg.chunk,
+                       "parallelism": f"bh-shard x{ws}", "l2": "inputs 470 MB > L2, no flush"},
+            "e2e": {"value": ws * cfg.tokens / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": 4 * args.steps,
+            "roofline": roof,
+            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": sample, "seconds": secs},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, ws, rank)
+        return
+    ws, rank, local = setup_dist()
+    try:
+        run_ours(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

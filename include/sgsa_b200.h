@@ -1,0 +1,124 @@
+/*
+ * sgsa_b200 -- C ABI of the B200 (sm_100a) SGSA layer forward.
+ *
+ * Every entry point takes raw device pointers, plain integer shapes and a
+ * cudaStream_t (passed as void*), returns an int status (SGSA_OK == 0, a
+ * negative SGSA_ERR_* otherwise) and never aborts or traps.  The library keeps
+ * no pointers between calls and allocates nothing: outputs and workspaces are
+ * owned by the caller, sized with the *_workspace_size queries.
+ *
+ * Tensor layouts follow the reference (row-major, contiguous):
+ *   q, k, v, sparse_k, sparse_v, o     [B, T, H, D]          dtype
+ *   beta, gamma, alpha                 [B, T, H]             dtype
+ *   initial_state, final_state         [B, H, D, D]          float32, S[d_k][d_v]
+ *   iq, ik (indexer)                   [B, T, H, DI]         dtype
+ *   mix                                [B, T, H, D] or [B, T, H]   dtype
+ *   top-k indices                      [B, H, T, K]          int32, ascending, -1 padded
+ * dtype is SGSA_DTYPE_F32 or SGSA_DTYPE_BF16 for all floating inputs of a call.
+ */
+#ifndef SGSA_B200_H_
+#define SGSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SGSA_OK = 0,
+    SGSA_ERR_SHAPE = -1,       /* bad or unsupported shape */
+    SGSA_ERR_DTYPE = -2,       /* unsupported dtype */
+    SGSA_ERR_NULL = -3,        /* required pointer is NULL */
+    SGSA_ERR_WORKSPACE = -4,   /* workspace too small or misaligned */
+    SGSA_ERR_LAUNCH = -5,      /* CUDA launch / runtime error */
+    SGSA_ERR_UNSUPPORTED = -6, /* valid request this build does not implement */
+    SGSA_ERR_DEVICE = -7       /* current device is not sm_100 */
+};
+
+enum { SGSA_DTYPE_F32 = 0, SGSA_DTYPE_BF16 = 1 };
+
+/* Flags of sgsa_chunk_fwd. */
+enum {
+    SGSA_FLAG_HAS_SPARSE = 1,   /* sparse_k/sparse_v/alpha given: 2 virtual samples per token */
+    SGSA_FLAG_HAS_INIT = 2,     /* initial_state given */
+    SGSA_FLAG_STORE_FINAL = 4,  /* write final_state */
+    SGSA_FLAG_OUT_F32 = 8       /* o is float32 regardless of dtype */
+};
+
+/* Human-readable text of a status code (static storage). */
+const char *sgsa_status_string(int status);
+
+/* Last CUDA error text seen by this thread (static storage, "" if none). */
+const char *sgsa_last_error(void);
+
+/* Library version, e.g. 1000 for 0.1.0. */
+int sgsa_version(void);
+
+/*
+ * Chunked SGSA / gated-delta-rule forward.
+ * Replaces chunk_sgsa (modelings/sgsa_ops/chunk.py:104-148) and its forward
+ * chunk_sgsa_fwd (modelings/sgsa_ops/chunk_fwd.py:12-131), with the semantics of
+ * naive_recurrent_sgsa (modelings/sgsa_ops/naive.py:39-55): no query scale,
+ * o_t = S_t^T q_t.  d_k == d_v == D, D in {32, 64, 128}; chunk_size == 64.
+ * sparse_k/sparse_v/alpha may be NULL unless SGSA_FLAG_HAS_SPARSE is set.
+ */
+size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags);
+int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta,
+                   const void *gamma, const void *sparse_k, const void *sparse_v,
+                   const void *alpha, const float *initial_state, void *o,
+                   float *final_state, int B, int T, int H, int D, int dtype, int chunk_size,
+                   int flags, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Causal per-head top-k indexer: s_tj = iq_t . ik_j for j <= t; row t keeps the
+ * min(top_k, t+1) largest, ties to the lowest j, written ascending and padded
+ * with -1.  Replaces the selection of TopKSparseKVReuseAttention.forward
+ * (modelings/hybrid_dense_delta_topk.py:344-349) and
+ * SparseRetriever._masked_topk (modelings/modeling_sgsa.py:144-165).
+ * DI in {32, 64, 128}; bf16 scores run on tcgen05 when DI % 64 == 0.
+ */
+int sgsa_indexer_topk(const void *iq, const void *ik, int32_t *indices, int B, int T, int H,
+                      int DI, int top_k, int dtype, void *stream);
+
+/*
+ * Row-wise top-k of a float32 score matrix [R, S] where row r considers
+ * columns [0, valid[r]).  Same selection rule and output format as
+ * sgsa_indexer_topk; it exists so that the select can be checked bit-exactly
+ * on identical scores (the rule of modelings/modeling_sgsa.py:155-164).
+ */
+int sgsa_topk_select(const float *scores, const int32_t *valid, int32_t *indices, int R, int S,
+                     int top_k, void *stream);
+
+/*
+ * Sparse attention over selected rows plus the gate:
+ *   o_s = sum_{j in I_t} softmax_j(q_t . k_j * scale) v_j     (fp32)
+ *   out = mix * o_s + (1 - mix) * o_delta
+ * Replaces modelings/hybrid_dense_delta_topk.py:350-356 and :389-390.
+ * o_delta is float32 [B,T,H,D] (NULL: out = o_s).  mix_per_channel selects
+ * the [B,T,H,D] (1) or [B,T,H] (0) mix layout; mix may be NULL with o_delta.
+ * out has the call's dtype.
+ */
+int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int32_t *indices,
+                         const float *o_delta, const void *mix, void *out, int B, int T, int H,
+                         int D, int top_k, float scale, int mix_per_channel, int dtype,
+                         void *stream);
+
+/*
+ * The composite layer forward: chunked delta stage (no sparse write),
+ * indexer top-k, sparse attention and gate, in one stream-ordered call.
+ * indices may be NULL (kept in the workspace).  final_state may be NULL.
+ */
+size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top_k);
+int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta,
+                   const void *gamma, const void *iq, const void *ik, const void *mix,
+                   const float *initial_state, void *out, float *final_state, int32_t *indices,
+                   int B, int T, int H, int D, int DI, int top_k, int mix_per_channel,
+                   int dtype, void *workspace, size_t workspace_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SGSA_B200_H_ */

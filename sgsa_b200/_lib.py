@@ -1,0 +1,69 @@
+"""ctypes binding of libsgsa_b200.so (the C ABI declared in include/sgsa_b200.h).
+
+There is no fallback: if the library is missing or the device is not an
+sm_100 part, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libsgsa_b200.so")
+
+SGSA_OK = 0
+DTYPE_F32, DTYPE_BF16 = 0, 1
+FLAG_HAS_SPARSE, FLAG_HAS_INIT, FLAG_STORE_FINAL, FLAG_OUT_F32 = 1, 2, 4, 8
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/sgsa_b200.h
+SIGNATURES = {
+    "sgsa_status_string": (ctypes.c_char_p, [_i]),
+    "sgsa_last_error": (ctypes.c_char_p, []),
+    "sgsa_version": (_i, []),
+    "sgsa_chunk_fwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
+    "sgsa_chunk_fwd": (_i, [_vp] * 11 + [_i] * 7 + [_vp, _sz, _vp]),
+    "sgsa_indexer_topk": (_i, [_vp, _vp, _vp] + [_i] * 6 + [_vp]),
+    "sgsa_topk_select": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
+    "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
+    "sgsa_layer_fwd_workspace_size": (_sz, [_i] * 6),
+    "sgsa_layer_fwd": (_i, [_vp] * 12 + [_i] * 9 + [_vp, _sz, _vp]),
+}
+
+_lib = None
+
+
+class SGSAError(RuntimeError):
+    pass
+
+
+def load():
+    """Load the library once (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m sgsa_b200.build` "
+                "(there is no CPU or Python fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status == SGSA_OK:
+        return
+    lib = load()
+    msg = lib.sgsa_status_string(status).decode()
+    extra = lib.sgsa_last_error().decode()
+    text = f"{what}: {msg}" + (f" ({extra})" if extra else "")
+    if status in (-1, -2, -3, -4, -6):
+        raise ValueError(text)
+    raise SGSAError(text)

@@ -1,0 +1,171 @@
+// extern "C" boundary of libsgsa_b200.so: argument checks, workspace carving,
+// status codes.  No entry point allocates, frees, aborts or traps.
+#include <stdio.h>
+#include <string.h>
+
+#include "common.cuh"
+
+namespace {
+
+thread_local char g_last_error[256] = "";
+
+int fail_cuda(cudaError_t e) {
+    snprintf(g_last_error, sizeof(g_last_error), "%s: %s", cudaGetErrorName(e),
+             cudaGetErrorString(e));
+    return SGSA_ERR_LAUNCH;
+}
+
+int check_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return SGSA_ERR_DEVICE;
+    int major = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+        return SGSA_ERR_DEVICE;
+    return major == 10 ? SGSA_OK : SGSA_ERR_DEVICE;
+}
+
+bool head_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
+bool dtype_ok(int dt) { return dt == SGSA_DTYPE_F32 || dt == SGSA_DTYPE_BF16; }
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+extern "C" {
+
+const char *sgsa_status_string(int s) {
+    switch (s) {
+        case SGSA_OK: return "ok";
+        case SGSA_ERR_SHAPE: return "bad or unsupported shape";
+        case SGSA_ERR_DTYPE: return "unsupported dtype";
+        case SGSA_ERR_NULL: return "required pointer is NULL";
+        case SGSA_ERR_WORKSPACE: return "workspace too small or misaligned";
+        case SGSA_ERR_LAUNCH: return "CUDA launch or runtime error";
+        case SGSA_ERR_UNSUPPORTED: return "unsupported request";
+        case SGSA_ERR_DEVICE: return "current CUDA device is not an sm_100 (B200) part";
+        default: return "unknown status";
+    }
+}
+
+const char *sgsa_last_error(void) { return g_last_error; }
+
+int sgsa_version(void) { return 1000; }
+
+size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags) {
+    if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D)) return 0;
+    return sgsa::chunk_delta_ws_bytes(B, T, H, D, flags);
+}
+
+int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta,
+                   const void *gamma, const void *sparse_k, const void *sparse_v,
+                   const void *alpha, const float *initial_state, void *o, float *final_state,
+                   int B, int T, int H, int D, int dtype, int chunk_size, int flags,
+                   void *workspace, size_t workspace_bytes, void *stream) {
+    if (B < 0 || T < 0 || H < 0) return SGSA_ERR_SHAPE;
+    if (!head_dim_ok(D) || chunk_size != 64) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (B == 0 || T == 0 || H == 0) {
+        // Empty sequence: the final state is the initial state (or zero).
+        if ((flags & SGSA_FLAG_STORE_FINAL) && final_state && B > 0 && H > 0) {
+            const size_t n = (size_t)B * H * D * D * sizeof(float);
+            cudaError_t e = (flags & SGSA_FLAG_HAS_INIT) && initial_state
+                                ? cudaMemcpyAsync(final_state, initial_state, n,
+                                                  cudaMemcpyDeviceToDevice, (cudaStream_t)stream)
+                                : cudaMemsetAsync(final_state, 0, n, (cudaStream_t)stream);
+            if (e != cudaSuccess) return fail_cuda(e);
+        }
+        return SGSA_OK;
+    }
+    if (!q || !k || !v || !beta || !gamma || !o) return SGSA_ERR_NULL;
+    if ((flags & SGSA_FLAG_HAS_SPARSE) && (!sparse_k || !sparse_v || !alpha)) return SGSA_ERR_NULL;
+    if ((flags & SGSA_FLAG_HAS_INIT) && !initial_state) return SGSA_ERR_NULL;
+    if ((flags & SGSA_FLAG_STORE_FINAL) && !final_state) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    const size_t need = sgsa::chunk_delta_ws_bytes(B, T, H, D, flags);
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255)) return SGSA_ERR_WORKSPACE;
+    cudaError_t e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, sparse_k, sparse_v, alpha,
+                                             initial_state, o, final_state, B, T, H, D, dtype,
+                                             flags, workspace, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_indexer_topk(const void *iq, const void *ik, int32_t *indices, int B, int T, int H,
+                      int DI, int top_k, int dtype, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || top_k <= 0) return SGSA_ERR_SHAPE;
+    if (DI != 32 && DI != 64 && DI != 128) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!iq || !ik || !indices) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_indexer_topk(iq, ik, indices, B, T, H, DI, top_k, dtype,
+                                              (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_topk_select(const float *scores, const int32_t *valid, int32_t *indices, int R, int S,
+                     int top_k, void *stream) {
+    if (R < 0 || S < 0 || top_k <= 0) return SGSA_ERR_SHAPE;
+    if (R == 0) return SGSA_OK;
+    if (!scores || !valid || !indices) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_topk_select(scores, valid, indices, R, S, top_k,
+                                             (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int32_t *indices,
+                         const float *o_delta, const void *mix, void *out, int B, int T, int H,
+                         int D, int top_k, float scale, int mix_per_channel, int dtype,
+                         void *stream) {
+    if (B < 0 || T < 0 || H < 0 || top_k <= 0 || !head_dim_ok(D)) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!q || !k || !v || !indices || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_sparse_attn_mix(q, k, v, indices, o_delta, mix, out, B, T, H, D,
+                                                 top_k, scale, mix_per_channel, dtype,
+                                                 (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top_k) {
+    if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D) || top_k <= 0) return 0;
+    (void)DI;
+    size_t n = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
+    n += align256((size_t)B * T * H * D * sizeof(float));       // o_delta
+    n += align256((size_t)B * H * T * top_k * sizeof(int32_t));  // indices
+    return n;
+}
+
+int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta,
+                   const void *gamma, const void *iq, const void *ik, const void *mix,
+                   const float *initial_state, void *out, float *final_state, int32_t *indices,
+                   int B, int T, int H, int D, int DI, int top_k, int mix_per_channel,
+                   int dtype, void *workspace, size_t workspace_bytes, void *stream) {
+    if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D) || top_k <= 0) return SGSA_ERR_SHAPE;
+    if (DI != 32 && DI != 64 && DI != 128) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (!q || !k || !v || !beta || !gamma || !iq || !ik || !mix || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    const size_t need = sgsa_layer_fwd_workspace_size(B, T, H, D, DI, top_k);
+    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255)) return SGSA_ERR_WORKSPACE;
+    cudaStream_t st = (cudaStream_t)stream;
+    char *w = (char *)workspace;
+    const size_t cws = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
+    float *od = (float *)(w + cws);
+    int32_t *ix = (int32_t *)(w + cws + align256((size_t)B * T * H * D * sizeof(float)));
+    if (indices) ix = indices;
+    int flags = SGSA_FLAG_OUT_F32 | (initial_state ? SGSA_FLAG_HAS_INIT : 0) |
+                (final_state ? SGSA_FLAG_STORE_FINAL : 0);
+    cudaError_t e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
+                                             initial_state, od, final_state, B, T, H, D, dtype,
+                                             flags, w, st);
+    if (e != cudaSuccess) return fail_cuda(e);
+    e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, H, DI, top_k, dtype, st);
+    if (e != cudaSuccess) return fail_cuda(e);
+    const float scale = 1.0f / sqrtf((float)D);
+    e = sgsa::launch_sparse_attn_mix(q, k, v, ix, od, mix, out, B, T, H, D, top_k, scale,
+                                     mix_per_channel, dtype, st);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+}  // extern "C"

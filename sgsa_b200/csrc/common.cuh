@@ -1,0 +1,51 @@
+// Shared helpers of the sgsa_b200 kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/sgsa_b200.h"
+
+namespace sgsa {
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+    return __float2bfloat16_rn(x);
+}
+
+// Orderable 32-bit key of a float: a > b  <=>  key(a) > key(b) (no NaNs).
+__device__ __forceinline__ uint32_t float_key(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace sgsa
+
+// Launch wrappers implemented in the .cu files (all return cudaError_t of the launch).
+namespace sgsa {
+cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, const void *beta,
+                               const void *gamma, const void *sk, const void *sv,
+                               const void *alpha, const float *s0, void *o, float *sT, int B,
+                               int T, int H, int D, int dtype, int flags, void *ws,
+                               cudaStream_t st);
+size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags);
+
+cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T,
+                                int H, int DI, int K, int dtype, cudaStream_t st);
+cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,
+                               int S, int K, cudaStream_t st);
+cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
+                                   const int32_t *idx, const float *od, const void *mix,
+                                   void *out, int B, int T, int H, int D, int K, float scale,
+                                   int mix_pc, int dtype, cudaStream_t st);
+}  // namespace sgsa

@@ -1,0 +1,216 @@
+// Sparse attention over the top-k rows of each query, fused with the gate.
+//
+//   o_s,t = sum_{j in I_t} softmax_j(q_t . k_j * scale) v_j        (fp32)
+//   out_t = m_t * o_s,t + (1 - m_t) * o_delta,t
+// as in modelings/hybrid_dense_delta_topk.py:343-356 (top-k softmax in fp32,
+// row gather, weighted sum) and :389-390 (sigmoid gate mix), without
+// materialising the [B,H,T,K,D] gather of the reference.
+//
+// One warp per (b, h, t).  Each half-warp gathers one selected row per step
+// with 16-byte vector loads (a 128-wide bf16 row is 16 lanes x 16 B), so one
+// warp keeps 2 x kUnroll rows in flight; the score is reduced over the
+// half-warp with shuffles, and each half keeps its own online-softmax state
+// (running max, sum, accumulator) that the two halves merge at the end.
+#include "common.cuh"
+
+namespace sgsa {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kUnroll = 4;
+
+template <typename T, int N>
+struct VecLoad;
+template <int N>
+struct VecLoad<__nv_bfloat16, N> {  // N bf16 values (N in {2,4,8})
+    __device__ __forceinline__ static void load(const __nv_bfloat16 *p, float *x) {
+        if constexpr (N == 8) {
+            uint4 r = __ldg(reinterpret_cast<const uint4 *>(p));
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&r);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float2 f = __bfloat1622float2(h[i]);
+                x[2 * i] = f.x;
+                x[2 * i + 1] = f.y;
+            }
+        } else if constexpr (N == 4) {
+            uint2 r = __ldg(reinterpret_cast<const uint2 *>(p));
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&r);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                float2 f = __bfloat1622float2(h[i]);
+                x[2 * i] = f.x;
+                x[2 * i + 1] = f.y;
+            }
+        } else {
+            uint32_t r = __ldg(reinterpret_cast<const unsigned int *>(p));
+            float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&r));
+            x[0] = f.x;
+            x[1] = f.y;
+        }
+    }
+};
+template <int N>
+struct VecLoad<float, N> {  // N floats (N in {2,4,8})
+    __device__ __forceinline__ static void load(const float *p, float *x) {
+        if constexpr (N % 4 == 0) {
+#pragma unroll
+            for (int i = 0; i < N / 4; ++i) {
+                float4 r = __ldg(reinterpret_cast<const float4 *>(p) + i);
+                x[4 * i] = r.x; x[4 * i + 1] = r.y; x[4 * i + 2] = r.z; x[4 * i + 3] = r.w;
+            }
+        } else {
+            float2 r = __ldg(reinterpret_cast<const float2 *>(p));
+            x[0] = r.x;
+            x[1] = r.y;
+        }
+    }
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
+    const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
+    const int32_t *__restrict__ idx, const float *__restrict__ od, const T *__restrict__ mix,
+    T *__restrict__ out, int B, int T_, int H, int K, float scale_log2, int mix_pc) {
+    constexpr int EPL = D / 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int half = lane >> 4, hl = lane & 15;
+    const long long qi = (long long)blockIdx.x * kWarps + warp;  // over [B*H*T]
+    if (qi >= (long long)B * H * T_) return;
+    const int t = (int)(qi % T_);
+    const int bh = (int)(qi / T_);
+    const int b = bh / H, h = bh % H;
+    const size_t rowq = ((size_t)b * T_ + t) * H + h;
+    const size_t kvstride = (size_t)H * D;
+    const T *kb = k + ((size_t)b * T_ * H + h) * D + hl * EPL;
+    const T *vb = v + ((size_t)b * T_ * H + h) * D + hl * EPL;
+
+    float qv[EPL];
+    VecLoad<T, EPL>::load(q + rowq * D + hl * EPL, qv);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) qv[e] *= scale_log2;
+
+    const int32_t *ix = idx + (size_t)qi * K;
+    const int nsel = min(K, t + 1);
+    float m = -INFINITY, l = 0.f, acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+
+    for (int base = 0; base < nsel; base += 32) {
+        const int cnt = min(32, nsel - base);
+        const int my = (lane < cnt) ? __ldg(ix + base + lane) : 0;
+        for (int p = 0; p < cnt; p += 2 * kUnroll) {
+            float kr[kUnroll][EPL], s[kUnroll];
+            int jr[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int slot = p + 2 * u + half;
+                jr[u] = __shfl_sync(0xffffffffu, my, slot & 31);
+                if (slot >= cnt) jr[u] = -1;
+                if (jr[u] >= 0) VecLoad<T, EPL>::load(kb + (size_t)jr[u] * kvstride, kr[u]);
+                else {
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) kr[u][e] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                float d0 = 0.f;
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) d0 = fmaf(qv[e], kr[u][e], d0);
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) d0 += __shfl_xor_sync(0xffffffffu, d0, off);
+                s[u] = (jr[u] >= 0) ? d0 : -INFINITY;
+            }
+            float vr[kUnroll][EPL];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                if (jr[u] >= 0) VecLoad<T, EPL>::load(vb + (size_t)jr[u] * kvstride, vr[u]);
+                else {
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) vr[u][e] = 0.f;
+                }
+            }
+            float mn = m;
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) mn = fmaxf(mn, s[u]);
+            if (mn != -INFINITY) {
+                const float corr = exp2f(m - mn);  // m == -inf gives 0
+                l *= corr;
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) acc[e] *= corr;
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    const float pu = exp2f(s[u] - mn);
+                    l += pu;
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pu, vr[u][e], acc[e]);
+                }
+                m = mn;
+            }
+        }
+    }
+    // merge the two half-warp states
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, 16);
+    const float l2 = __shfl_xor_sync(0xffffffffu, l, 16);
+    const float mt = fmaxf(m, m2);
+    const float c1 = (m == -INFINITY) ? 0.f : exp2f(m - mt);
+    const float c2 = (m2 == -INFINITY) ? 0.f : exp2f(m2 - mt);
+    const float lt = l * c1 + l2 * c2;
+    const float inv = (lt > 0.f) ? 1.f / lt : 0.f;
+    float o[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const float a2 = __shfl_xor_sync(0xffffffffu, acc[e], 16);
+        o[e] = (acc[e] * c1 + a2 * c2) * inv;
+    }
+    if (half == 0) {
+        T *dst = out + rowq * D + hl * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) {
+            float r = o[e];
+            if (od) {
+                const float mm = mix ? to_f32(mix_pc ? mix[rowq * D + hl * EPL + e] : mix[rowq]) : 1.f;
+                r = mm * r + (1.f - mm) * od[rowq * D + hl * EPL + e];
+            }
+            dst[e] = from_f32<T>(r);
+        }
+    }
+}
+
+template <typename T, int D>
+cudaError_t run(const void *q, const void *k, const void *v, const int32_t *idx, const float *od,
+                const void *mix, void *out, int B, int T_, int H, int K, float scale, int mix_pc,
+                cudaStream_t st) {
+    const long long nq = (long long)B * H * T_;
+    const unsigned grid = (unsigned)((nq + kWarps - 1) / kWarps);
+    sparse_attn_mix_kernel<T, D><<<grid, kWarps * 32, 0, st>>>(
+        (const T *)q, (const T *)k, (const T *)v, idx, od, (const T *)mix, (T *)out, B, T_, H, K,
+        scale * 1.4426950408889634f, mix_pc);
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t run_d(int D, const void *q, const void *k, const void *v, const int32_t *idx,
+                  const float *od, const void *mix, void *out, int B, int T_, int H, int K,
+                  float scale, int mix_pc, cudaStream_t st) {
+    switch (D) {
+        case 32: return run<T, 32>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, st);
+        case 64: return run<T, 64>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, st);
+        case 128: return run<T, 128>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
+                                   const int32_t *idx, const float *od, const void *mix,
+                                   void *out, int B, int T, int H, int D, int K, float scale,
+                                   int mix_pc, int dtype, cudaStream_t st) {
+    if (dtype == SGSA_DTYPE_F32)
+        return run_d<float>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, st);
+    return run_d<__nv_bfloat16>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, st);
+}
+
+}  // namespace sgsa

@@ -1,0 +1,259 @@
+"""Host-side operators of the SGSA layer forward on B200.
+
+``chunk_sgsa`` keeps the signature, argument meaning and return of the
+reference's public op (modelings/sgsa_ops/chunk.py:104-148), so a caller can
+swap the import.  The other functions expose the rest of the layer's hot path
+(indexer top-k, sparse attention + gate, the fused composite) at op level.
+
+Every op runs the CUDA kernels of libsgsa_b200.so on the tensors' device and
+current stream.  There is no CPU or Python fallback: CPU tensors, unsupported
+dtypes or shapes raise.  The forward pass only is implemented; asking for a
+gradient through these ops raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+Tensor = torch.Tensor
+
+_DT = {torch.float32: _lib.DTYPE_F32, torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def _dtype_code(t: Tensor) -> int:
+    if t.dtype not in _DT:
+        raise TypeError(f"sgsa_b200 supports float32 and bfloat16 inputs, got {t.dtype}")
+    return _DT[t.dtype]
+
+
+def _dev(t: Tensor, name: str) -> Tensor:
+    if not isinstance(t, Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (sgsa_b200 has no CPU path)")
+    return t
+
+
+def _ptr(t: Optional[Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _no_grad_check(*ts):
+    if torch.is_grad_enabled() and any(isinstance(t, Tensor) and t.requires_grad for t in ts):
+        raise NotImplementedError("sgsa_b200 implements the SGSA forward only (no backward)")
+
+
+def _workspace(nbytes: int, device) -> Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def chunk_sgsa(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    beta: Tensor,
+    gamma: Tensor,
+    sparse_k: Optional[Tensor] = None,
+    sparse_v: Optional[Tensor] = None,
+    alpha: Optional[Tensor] = None,
+    initial_state: Optional[Tensor] = None,
+    chunk_size: int = 64,
+    output_final_state: bool = False,
+    use_triton: bool = True,
+) -> Tuple[Tensor, Optional[Tensor]]:
+    """Chunked Sparse-Guided State Attention core (forward).
+
+    Same contract as the reference ``chunk_sgsa`` (modelings/sgsa_ops/chunk.py:104-148):
+    q, k, v, sparse_k, sparse_v are ``[B, T, H, D]``; beta, gamma, alpha are
+    ``[B, T, H]``; initial_state is ``[B, H, D, D]``; returns ``o`` in q.dtype
+    and the final state in q.dtype (or None).  The sparse write is active when
+    all three of sparse_k, sparse_v and alpha are given.  The device path
+    always tiles by 64 tokens: ``chunk_size`` only has to be positive (the
+    result does not depend on it beyond rounding), and ``use_triton`` is
+    accepted for signature compatibility -- there is no other backend.
+    """
+    del use_triton
+    if chunk_size <= 0:
+        raise ValueError("chunk_size must be positive")
+    for n, t in (("q", q), ("k", k), ("v", v), ("beta", beta), ("gamma", gamma)):
+        _dev(t, n)
+    _no_grad_check(q, k, v, beta, gamma, sparse_k, sparse_v, alpha, initial_state)
+    if q.dim() != 4 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must share the shape [B, T, H, D]")
+    B, T, H, D = q.shape
+    if beta.shape != (B, T, H) or gamma.shape != (B, T, H):
+        raise ValueError("beta and gamma must be [B, T, H]")
+    dt = _dtype_code(q)
+    has_sparse = sparse_k is not None and sparse_v is not None and alpha is not None
+    flags = 0
+    if has_sparse:
+        if sparse_k.shape != q.shape or sparse_v.shape != q.shape or alpha.shape != (B, T, H):
+            raise ValueError("sparse_k/sparse_v must be [B, T, H, D] and alpha [B, T, H]")
+        flags |= _lib.FLAG_HAS_SPARSE
+    cast = lambda t: None if t is None else t.to(device=q.device, dtype=q.dtype).contiguous()
+    q_, k_, v_ = q.contiguous(), cast(k), cast(v)
+    beta_, gamma_ = cast(beta), cast(gamma)
+    sk_, sv_, al_ = (cast(sparse_k), cast(sparse_v), cast(alpha)) if has_sparse else (None,) * 3
+    s0 = None
+    if initial_state is not None:
+        if initial_state.shape != (B, H, D, D):
+            raise ValueError("initial_state must be [B, H, D, D]")
+        s0 = initial_state.to(device=q.device, dtype=torch.float32).contiguous()
+        flags |= _lib.FLAG_HAS_INIT
+    o = torch.empty_like(q_)
+    sT = None
+    if output_final_state:
+        sT = torch.empty(B, H, D, D, device=q.device, dtype=torch.float32)
+        flags |= _lib.FLAG_STORE_FINAL
+    lib = _lib.load()
+    wsb = lib.sgsa_chunk_fwd_workspace_size(B, T, H, D, flags)
+    ws = _workspace(wsb, q.device)
+    st = lib.sgsa_chunk_fwd(_ptr(q_), _ptr(k_), _ptr(v_), _ptr(beta_), _ptr(gamma_), _ptr(sk_),
+                            _ptr(sv_), _ptr(al_), _ptr(s0), _ptr(o), _ptr(sT), B, T, H, D, dt, 64,
+                            flags, _ptr(ws), ws.numel(), _stream(q))
+    _lib.check(st, "sgsa_chunk_fwd")
+    if sT is not None:
+        sT = sT.to(q.dtype)
+    return o, sT
+
+
+def chunk_sgsa_fp32_state(q, k, v, beta, gamma, initial_state=None, sparse_k=None,
+                          sparse_v=None, alpha=None, out_f32: bool = False):
+    """Like ``chunk_sgsa`` but returns the final state in float32 (for hand-off
+    between sequence shards) and optionally a float32 ``o``."""
+    B, T, H, D = q.shape
+    _dev(q, "q")
+    dt = _dtype_code(q)
+    has_sparse = sparse_k is not None and sparse_v is not None and alpha is not None
+    flags = _lib.FLAG_STORE_FINAL | (_lib.FLAG_OUT_F32 if out_f32 else 0)
+    flags |= _lib.FLAG_HAS_SPARSE if has_sparse else 0
+    cast = lambda t: None if t is None else t.to(dtype=q.dtype).contiguous()
+    s0 = None
+    if initial_state is not None:
+        s0 = initial_state.to(dtype=torch.float32).contiguous()
+        flags |= _lib.FLAG_HAS_INIT
+    o = torch.empty(q.shape, device=q.device, dtype=torch.float32 if out_f32 else q.dtype)
+    sT = torch.empty(B, H, D, D, device=q.device, dtype=torch.float32)
+    lib = _lib.load()
+    ws = _workspace(lib.sgsa_chunk_fwd_workspace_size(B, T, H, D, flags), q.device)
+    args = [cast(t) for t in (q, k, v, beta, gamma)]
+    sp = [cast(t) for t in (sparse_k, sparse_v, alpha)] if has_sparse else [None] * 3
+    st = lib.sgsa_chunk_fwd(*[_ptr(t) for t in args], *[_ptr(t) for t in sp], _ptr(s0), _ptr(o),
+                            _ptr(sT), B, T, H, D, dt, 64, flags, _ptr(ws), ws.numel(),
+                            _stream(q))
+    _lib.check(st, "sgsa_chunk_fwd")
+    return o, sT
+
+
+def indexer_topk(iq: Tensor, ik: Tensor, top_k: int) -> Tensor:
+    """Causal per-head top-k of ``iq . ik`` -> int32 ``[B, H, T, top_k]``.
+
+    Row t holds the min(top_k, t+1) selected key positions in ascending order,
+    ties broken toward the lower position, padded with -1 (the selection of
+    modelings/hybrid_dense_delta_topk.py:344-349 / modeling_sgsa.py:144-165).
+    """
+    _dev(iq, "iq"), _dev(ik, "ik")
+    if iq.dim() != 4 or ik.shape != iq.shape:
+        raise ValueError("iq and ik must share the shape [B, T, H, DI]")
+    if top_k <= 0:
+        raise ValueError("top_k must be positive")
+    B, T, H, DI = iq.shape
+    dt = _dtype_code(iq)
+    iq_, ik_ = iq.contiguous(), ik.to(iq.dtype).contiguous()
+    out = torch.empty(B, H, T, top_k, device=iq.device, dtype=torch.int32)
+    st = _lib.load().sgsa_indexer_topk(_ptr(iq_), _ptr(ik_), _ptr(out), B, T, H, DI, top_k, dt,
+                                        _stream(iq))
+    _lib.check(st, "sgsa_indexer_topk")
+    return out
+
+
+def topk_select(scores: Tensor, valid: Tensor, top_k: int) -> Tensor:
+    """Row top-k of float32 ``scores [R, S]`` over columns ``[0, valid[r])``."""
+    _dev(scores, "scores")
+    if scores.dim() != 2:
+        raise ValueError("scores must be [R, S]")
+    R, S = scores.shape
+    sc = scores.to(torch.float32).contiguous()
+    val = valid.to(device=scores.device, dtype=torch.int32).contiguous()
+    if val.shape != (R,):
+        raise ValueError("valid must be [R]")
+    out = torch.empty(R, top_k, device=scores.device, dtype=torch.int32)
+    st = _lib.load().sgsa_topk_select(_ptr(sc), _ptr(val), _ptr(out), R, S, top_k,
+                                       _stream(scores))
+    _lib.check(st, "sgsa_topk_select")
+    return out
+
+
+def sparse_attn_mix(q: Tensor, k: Tensor, v: Tensor, indices: Tensor,
+                    o_delta: Optional[Tensor] = None, mix: Optional[Tensor] = None,
+                    scale: Optional[float] = None) -> Tensor:
+    """Softmax attention of each query over its selected rows, then the gate
+    ``mix * o_s + (1 - mix) * o_delta`` (modelings/hybrid_dense_delta_topk.py:350-356,389-390).
+
+    ``indices`` is int32 ``[B, H, T, K]`` as produced by ``indexer_topk``;
+    ``mix`` is ``[B, T, H, D]`` or ``[B, T, H]``; ``o_delta`` ``[B, T, H, D]``.
+    """
+    for n, t in (("q", q), ("k", k), ("v", v), ("indices", indices)):
+        _dev(t, n)
+    B, T, H, D = q.shape
+    if indices.dim() != 4 or indices.shape[:3] != (B, H, T):
+        raise ValueError("indices must be [B, H, T, K]")
+    K = indices.shape[-1]
+    dt = _dtype_code(q)
+    cast = lambda t: None if t is None else t.to(q.dtype).contiguous()
+    q_, k_, v_ = q.contiguous(), cast(k), cast(v)
+    ix = indices.to(torch.int32).contiguous()
+    od = None if o_delta is None else o_delta.to(torch.float32).contiguous()
+    mx = cast(mix) if o_delta is not None else None
+    per_channel = int(mx is not None and mx.dim() == 4)
+    out = torch.empty_like(q_)
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    st = _lib.load().sgsa_sparse_attn_mix(_ptr(q_), _ptr(k_), _ptr(v_), _ptr(ix), _ptr(od),
+                                           _ptr(mx), _ptr(out), B, T, H, D, K, sc, per_channel,
+                                           dt, _stream(q))
+    _lib.check(st, "sgsa_sparse_attn_mix")
+    return out
+
+
+def sgsa_layer_fwd(q: Tensor, k: Tensor, v: Tensor, beta: Tensor, gamma: Tensor, iq: Tensor,
+                   ik: Tensor, mix: Tensor, top_k: int, initial_state: Optional[Tensor] = None,
+                   output_final_state: bool = False, return_indices: bool = False):
+    """Fused SGSA layer core: delta stage + indexer top-k + sparse attention + gate.
+
+    Returns ``out`` (q.dtype), then the float32 final state if requested and
+    the int32 indices if requested.
+    """
+    for n, t in (("q", q), ("k", k), ("v", v), ("beta", beta), ("gamma", gamma), ("iq", iq),
+                 ("ik", ik), ("mix", mix)):
+        _dev(t, n)
+    _no_grad_check(q, k, v, beta, gamma, iq, ik, mix, initial_state)
+    B, T, H, D = q.shape
+    DI = iq.shape[-1]
+    dt = _dtype_code(q)
+    cast = lambda t: t.to(q.dtype).contiguous()
+    args = [q.contiguous()] + [cast(t) for t in (k, v, beta, gamma, iq, ik, mix)]
+    per_channel = int(mix.dim() == 4)
+    s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    out = torch.empty_like(args[0])
+    sT = torch.empty(B, H, D, D, device=q.device, dtype=torch.float32) if output_final_state else None
+    ix = torch.empty(B, H, T, top_k, device=q.device, dtype=torch.int32) if return_indices else None
+    lib = _lib.load()
+    ws = _workspace(lib.sgsa_layer_fwd_workspace_size(B, T, H, D, DI, top_k), q.device)
+    st = lib.sgsa_layer_fwd(*[_ptr(t) for t in args], _ptr(s0), _ptr(out), _ptr(sT), _ptr(ix),
+                            B, T, H, D, DI, top_k, per_channel, dt, _ptr(ws), ws.numel(),
+                            _stream(q))
+    _lib.check(st, "sgsa_layer_fwd")
+    res = [out]
+    if output_final_state:
+        res.append(sT)
+    if return_indices:
+        res.append(ix)
+    return res[0] if len(res) == 1 else tuple(res)

@@ -1,0 +1,62 @@
+"""The C-ABI library loads and exports every entry point include/sgsa_b200.h declares."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from sgsa_b200 import _lib, build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "sgsa_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sgsa_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    names = header_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), f"{n} missing from libsgsa_b200.so"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_host_only_entry_points(lib):
+    assert lib.sgsa_version() >= 1000
+    assert lib.sgsa_status_string(0) == b"ok"
+    assert b"shape" in lib.sgsa_status_string(-1)
+    n = lib.sgsa_chunk_fwd_workspace_size(4, 8192, 16, 128, 0)
+    assert n == 4 * 16 * 128 * (2 * 64 * 128 + 64 * 64 + 64) * 4
+    assert lib.sgsa_chunk_fwd_workspace_size(1, 64, 1, 96, 0) == 0  # unsupported head dim
+    assert lib.sgsa_layer_fwd_workspace_size(1, 1024, 4, 64, 32, 128) > 0
+
+
+def test_bad_arguments_rejected_before_any_launch(lib):
+    # shape / dtype checks run before the device is touched
+    assert lib.sgsa_chunk_fwd(*([None] * 11), 1, 64, 1, 96, 0, 64, 0, None, 0, None) == -1
+    assert lib.sgsa_chunk_fwd(*([None] * 11), 1, 64, 1, 64, 0, 32, 0, None, 0, None) == -1
+    assert lib.sgsa_chunk_fwd(*([None] * 11), 1, 64, 1, 64, 7, 64, 0, None, 0, None) == -2
+    assert lib.sgsa_indexer_topk(None, None, None, 1, 64, 1, 48, 8, 0, None) == -1
+    assert lib.sgsa_sparse_attn_mix(*([None] * 7), 1, 64, 1, 64, 0, 1.0, 0, 1, None) == -1
+    # empty problems are a no-op
+    assert lib.sgsa_indexer_topk(None, None, None, 0, 64, 1, 64, 8, 1, None) == 0
+
+
+def test_ops_refuse_cpu_tensors():
+    import sgsa_b200 as sg
+    x = torch.zeros(1, 8, 1, 32)
+    g = torch.ones(1, 8, 1)
+    with pytest.raises(ValueError, match="CUDA"):
+        sg.chunk_sgsa(x, x, x, g, g)
+    with pytest.raises(ValueError, match="CUDA"):
+        sg.indexer_topk(x, x, 4)

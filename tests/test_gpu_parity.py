@@ -1,0 +1,209 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle.
+
+Tolerances (relative L2 against the float64 oracle run on the same,
+already-rounded inputs): 1e-5 for float32 inputs, 2e-3 for bfloat16 inputs.
+Top-k index sets must be identical; where the device and the oracle compute
+scores with different rounding, a differing index is accepted only if its
+score lies within a small band around the row's k-th score (a near tie).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from sgsa_b200 import ops
+from sgsa_b200.inputs import CONFIGS, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-3}
+
+
+def dev(x):
+    return {n: t.cuda() for n, t in x.items()}
+
+
+def rand_case(B, T, H, D, dtype, seed=0, sparse=False, init=False, decay="softplus"):
+    g = torch.Generator().manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g)
+    x = dict(q=torch.nn.functional.normalize(r(B, T, H, D), dim=-1),
+             k=torch.nn.functional.normalize(r(B, T, H, D), dim=-1),
+             v=r(B, T, H, D), beta=torch.sigmoid(r(B, T, H)))
+    x["gamma"] = torch.exp(-torch.nn.functional.softplus(r(B, T, H))) if decay == "softplus" \
+        else 0.9 + 0.1 * torch.rand(B, T, H, generator=g)
+    if sparse:
+        x["sparse_k"] = torch.nn.functional.normalize(r(B, T, H, D), dim=-1)
+        x["sparse_v"] = r(B, T, H, D)
+        x["alpha"] = 0.25 * torch.sigmoid(r(B, T, H))
+    if init:
+        x["initial_state"] = 0.1 * r(B, H, D, D)
+    return {n: (t.to(dtype) if n != "initial_state" else t) for n, t in x.items()}
+
+
+def run_chunk(x):
+    d = dev(x)
+    o, s = ops.chunk_sgsa(**d, output_final_state=True)
+    torch.cuda.synchronize()
+    return o.float().cpu().numpy(), s.float().cpu().numpy()
+
+
+def oracle_chunk(x):
+    return oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], x.get("sparse_k"),
+                                 x.get("sparse_v"), x.get("alpha"), x.get("initial_state"))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("sparse,init", [(False, False), (True, True)])
+def test_chunk_matches_oracle(dtype, D, sparse, init):
+    x = rand_case(2, 200, 3, D, dtype, seed=D, sparse=sparse, init=init)
+    o, s = run_chunk(x)
+    ro, rs = oracle_chunk(x)
+    assert oracle.rel_l2(o, ro) < TOL[dtype]
+    assert oracle.rel_l2(s, rs) < TOL[dtype]
+
+
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 130])
+def test_chunk_ragged_lengths(T):
+    x = rand_case(1, T, 2, 64, torch.float32, seed=T, sparse=True, init=True)
+    o, s = run_chunk(x)
+    ro, rs = oracle_chunk(x)
+    assert oracle.rel_l2(o, ro) < 1e-5
+    assert oracle.rel_l2(s, rs) < 1e-5
+
+
+def test_chunk_mild_decay_long():
+    # mild decay keeps the state large across many chunks (the regime the
+    # reference's chunk path handles well); errors must not accumulate.
+    x = rand_case(1, 2048, 2, 128, torch.float32, seed=5, decay="mild")
+    o, s = run_chunk(x)
+    ro, rs = oracle_chunk(x)
+    assert oracle.rel_l2(o, ro) < 1e-5
+    assert oracle.rel_l2(s, rs) < 1e-5
+
+
+def test_chunk_cpu_config_fp32():
+    cfg = CONFIGS["cpu_fp32"]
+    x = make_inputs(cfg)
+    d = dev(x)
+    o, s = ops.chunk_sgsa(d["q"], d["k"], d["v"], d["beta"], d["gamma"], output_final_state=True)
+    z = np.load("tests/golden/recurrent_cfg0.npz")
+    assert oracle.rel_l2(o.cpu().numpy(), z["o"]) < 1e-5
+    assert oracle.rel_l2(s.cpu().numpy(), z["state"]) < 1e-5
+
+
+def test_chunk_empty_sequence_returns_initial_state():
+    x = rand_case(1, 4, 2, 64, torch.float32, init=True)
+    d = {n: t[:, :0].cuda() if t.dim() >= 3 and n != "initial_state" else t.cuda() for n, t in x.items()}
+    o, s = ops.chunk_sgsa(**d, output_final_state=True)
+    assert o.shape[1] == 0
+    torch.testing.assert_close(s.cpu(), x["initial_state"])
+
+
+def check_index_sets(got, want, iq, ik, kth, tol):
+    """Exact equality, except that differing entries must be near-ties."""
+    if np.array_equal(got, want):
+        return 0
+    B, H, T, K = got.shape
+    bad = np.argwhere((got != want).any(-1))
+    iqd = iq.double().numpy()
+    ikd = ik.double().numpy()
+    for b, h, t in bad:
+        a = set(got[b, h, t][got[b, h, t] >= 0].tolist())
+        w = set(want[b, h, t][want[b, h, t] >= 0].tolist())
+        assert len(a) == len(w)
+        for j in a ^ w:
+            s = float(iqd[b, t, h] @ ikd[b, j, h])
+            assert abs(s - kth[b, h, t]) <= tol * max(1.0, abs(kth[b, h, t])), (b, h, t, j)
+    return len(bad)
+
+
+def test_indexer_cpu_config_fp32_matches_reference_fixture():
+    cfg = CONFIGS["cpu_fp32"]
+    x = make_inputs(cfg)
+    got = ops.indexer_topk(x["iq"].cuda(), x["ik"].cuda(), cfg.top_k).cpu().numpy()
+    want, kth = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k, return_kth=True)
+    z = np.load("tests/golden/indexer_cfg0.npz")
+    np.testing.assert_array_equal(want, z["idx"].astype(np.int32))
+    check_index_sets(got, want, x["iq"], x["ik"], kth, 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T,DI,K", [(300, 64, 32), (1000, 128, 256), (129, 32, 128), (70, 64, 512)])
+def test_indexer_matches_oracle(dtype, T, DI, K):
+    g = torch.Generator().manual_seed(T + DI)
+    iq = torch.randn(2, T, 3, DI, generator=g).to(dtype)
+    ik = torch.randn(2, T, 3, DI, generator=g).to(dtype)
+    got = ops.indexer_topk(iq.cuda(), ik.cuda(), K).cpu().numpy()
+    want, kth = oracle.indexer_topk(iq, ik, K, return_kth=True)
+    check_index_sets(got, want, iq.float(), ik.float(), kth, 1e-5)
+
+
+def test_indexer_exact_ties_lowest_index():
+    # integer-valued indexer vectors produce many exactly equal scores
+    g = torch.Generator().manual_seed(3)
+    iq = torch.randint(-2, 3, (1, 257, 2, 32), generator=g).float()
+    ik = torch.randint(-2, 3, (1, 257, 2, 32), generator=g).float()
+    for dtype in (torch.float32, torch.bfloat16):
+        got = ops.indexer_topk(iq.to(dtype).cuda(), ik.to(dtype).cuda(), 16).cpu().numpy()
+        want = oracle.indexer_topk(iq, ik, 16)
+        np.testing.assert_array_equal(got, want)
+
+
+def test_topk_select_bit_exact_on_identical_scores():
+    g = torch.Generator().manual_seed(7)
+    R, S, K = 300, 700, 64
+    sc = torch.randn(R, S, generator=g)
+    sc[::3] = torch.round(sc[::3] * 2)  # heavy ties on every third row
+    sc[5] = 1.0                         # a row that is all ties
+    sc[6] = -0.0
+    valid = torch.randint(0, S + 1, (R,), generator=g).int()
+    valid[:4] = torch.tensor([0, 1, K, K + 1])
+    got = ops.topk_select(sc.cuda(), valid.cuda(), K).cpu().numpy()
+    want = oracle.topk_select(sc.numpy(), valid.numpy(), K)
+    np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_sparse_attn_mix_matches_oracle(dtype, D):
+    T, K = 300, 48
+    x = rand_case(2, T, 3, D, dtype, seed=11)
+    g = torch.Generator().manual_seed(12)
+    iq = torch.randn(2, T, 3, 32, generator=g)
+    idx = oracle.indexer_topk(iq, iq.roll(1, 1), K)
+    od = torch.randn(2, T, 3, D, generator=g)
+    for mix in (torch.sigmoid(torch.randn(2, T, 3, D, generator=g)).to(dtype),
+                torch.sigmoid(torch.randn(2, T, 3, generator=g)).to(dtype)):
+        got = ops.sparse_attn_mix(x["q"].cuda(), x["k"].cuda(), x["v"].cuda(),
+                                  torch.from_numpy(idx).cuda(), od.cuda(), mix.cuda())
+        want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx, od, mix)
+        assert oracle.rel_l2(got.float().cpu().numpy(), want) < TOL[dtype]
+
+
+def test_sparse_attention_reference_fixture():
+    z = np.load("tests/golden/sparse_attn_ref.npz")
+    t = lambda a: torch.from_numpy(a).float().cuda()
+    idx = ops.indexer_topk(t(z["q"]), t(z["k"]), int(z["top_k"]))
+    got = ops.sparse_attn_mix(t(z["q"]), t(z["k"]), t(z["v"]), idx, t(z["o_delta"]), t(z["mix"]))
+    assert oracle.rel_l2(got.cpu().numpy(), z["out"]) < 1e-5
+
+
+@pytest.mark.parametrize("dtype,cfgname", [(torch.float32, "cpu_fp32"), (torch.bfloat16, "small_bf16")])
+def test_layer_fwd_matches_oracle(dtype, cfgname):
+    cfg = CONFIGS["cpu_fp32"] if cfgname == "cpu_fp32" else CONFIGS["b200_bf16"].scaled(
+        name="small_bf16", B=1, T=1024, H=4)
+    x = make_inputs(cfg)
+    d = dev(x)
+    out, st, idx = ops.sgsa_layer_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"],
+                                      d["ik"], d["mix"], cfg.top_k, output_final_state=True,
+                                      return_indices=True)
+    ro, rs = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"])
+    want_idx, kth = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k, return_kth=True)
+    got_idx = idx.cpu().numpy()
+    check_index_sets(got_idx, want_idx, x["iq"].float(), x["ik"].float(), kth, 1e-5)
+    # score the composite on the device's own index sets so a near-tie swap
+    # does not leak into the output comparison
+    want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], got_idx, ro, x["mix"])
+    assert oracle.rel_l2(out.float().cpu().numpy(), want) < TOL[dtype]
+    assert oracle.rel_l2(st.cpu().numpy(), rs) < TOL[dtype]
