@@ -57,6 +57,14 @@ const char *sgsa_last_error(void);
 int sgsa_version(void);
 
 /*
+ * Synchronises `stream`, returns and clears the device watchdog word: 0 when
+ * every bounded wait inside the tensor-core kernels completed, else a bitmask
+ * of the waits that gave up (their results are then invalid).  No reference
+ * counterpart: the reference's Triton kernels have no device-side waits.
+ */
+int sgsa_watchdog_status(void *stream);
+
+/*
  * Chunked SGSA / gated-delta-rule forward.
  * Replaces chunk_sgsa (modelings/sgsa_ops/chunk.py:104-148) and its forward
  * chunk_sgsa_fwd (modelings/sgsa_ops/chunk_fwd.py:12-131), with the semantics of

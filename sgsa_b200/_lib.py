@@ -24,6 +24,7 @@ SIGNATURES = {
     "sgsa_status_string": (ctypes.c_char_p, [_i]),
     "sgsa_last_error": (ctypes.c_char_p, []),
     "sgsa_version": (_i, []),
+    "sgsa_watchdog_status": (_i, [_vp]),
     "sgsa_chunk_fwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "sgsa_chunk_fwd": (_i, [_vp] * 11 + [_i] * 7 + [_vp, _sz, _vp]),
     "sgsa_indexer_topk": (_i, [_vp, _vp, _vp] + [_i] * 6 + [_vp]),

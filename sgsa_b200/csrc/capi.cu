@@ -50,6 +50,10 @@ const char *sgsa_last_error(void) { return g_last_error; }
 
 int sgsa_version(void) { return 1000; }
 
+int sgsa_watchdog_status(void *stream) {
+    return (int)sgsa::read_index_watchdog((cudaStream_t)stream);
+}
+
 size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags) {
     if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D)) return 0;
     return sgsa::chunk_delta_ws_bytes(B, T, H, D, flags);

@@ -44,6 +44,7 @@ size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags);
 
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T,
                                 int H, int DI, int K, int dtype, cudaStream_t st);
+unsigned int read_index_watchdog(cudaStream_t st);
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,
                                int S, int K, cudaStream_t st);
 cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,

@@ -16,9 +16,20 @@
 // key is above the prefix plus the first `need` columns equal to it -- which
 // is exactly the lowest-index tie-break.  Scores are recomputed in every pass
 // (bit-identical, same code and order), so nothing of size T^2 is stored.
+#include <stdlib.h>
+
 #include "common.cuh"
+#include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace sgsa {
+
+// SGSA_INDEXER_SIMT=1 forces the CUDA-core score path for bf16 (A/B checks).
+static bool indexer_use_tc() {
+    const char *e = getenv("SGSA_INDEXER_SIMT");
+    return !(e && e[0] == '1');
+}
+
 namespace {
 
 constexpr int kRows = 128;       // query rows per CTA (one per thread)
@@ -176,6 +187,212 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
     select_rows(tiles, nvalid, K, (r < R) ? idx + (size_t)r * K : nullptr, hist, maxv);
 }
 
+
+// ---- tcgen05 indexer: bf16 scores on the tensor cores, fp32 in TMEM. --------
+//
+// Warp roles of the 192-thread CTA (one CTA per 128-query tile of one (b, h)):
+//   warp 0  TMA producer: the query tile once, then key tiles of 128 rows
+//           into a ring of shared-memory stages;
+//   warp 1  TMEM owner and MMA issuer: S_tile = Q K^T, M=128 (queries) x
+//           N=128 (keys) x K=DI, into one of two TMEM accumulators;
+//   warps 2-5  one thread per query row: tcgen05.ld of its row of the tile,
+//           radix histogram / collect, as in select_rows above.
+// The key stream is replayed once per radix pass; the tensor cores recompute
+// the identical fp32 scores each time.
+static __device__ unsigned int g_index_watchdog;
+
+template <int DI>
+struct TcCfg {
+    static constexpr int kKB = DI / 64;                // 128-byte K blocks
+    static constexpr int kN = 128;                     // keys per tile
+    static constexpr int kStages = (DI == 64) ? 4 : 2;
+    static constexpr int kQBytes = 128 * DI * 2;
+    static constexpr int kKBytes = kN * DI * 2;
+    static constexpr int kHistBytes = 256 * kRows * 4;
+    static constexpr int kBars = 2 * kStages + 5;
+    static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
+};
+
+template <int DI>
+__global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    int32_t *__restrict__ idx, int B, int T, int H, int K, int nqt) {
+    using C = TcCfg<DI>;
+    using namespace sm100;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char *sQ = base;
+    unsigned char *sK = sQ + C::kQBytes;
+    uint32_t *hist = (uint32_t *)(sK + C::kStages * C::kKBytes);
+    uint64_t *bars = (uint64_t *)(hist + 256 * kRows);
+    uint64_t *full = bars, *empty = bars + C::kStages, *tfull = bars + 2 * C::kStages,
+             *tempty = tfull + 2, *qbar = tempty + 2;
+    __shared__ uint32_t s_tmem;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int BH = B * H;
+    const int qt = nqt - 1 - (int)(blockIdx.x / BH);
+    const int bh = (int)(blockIdx.x % BH), b = bh / H, h = bh % H;
+    const int q0 = qt * kRows;
+    const int q_last = min(T - 1, q0 + kRows - 1);
+    const int nkt = q_last / C::kN + 1;
+    unsigned int *wd = &g_index_watchdog;
+
+    // epilogue-thread row state
+    const bool epi = warp >= 2;
+    const int quad = warp & 3;               // TMEM lane quarter this warp may access
+    const int row = quad * 32 + lane;
+    const int t = q0 + row;
+    const int nvalid = (epi && t < T) ? t + 1 : 0;
+    int32_t *out_row = (epi && t < T) ? idx + ((size_t)bh * T + t) * K : nullptr;
+    SelState s{0u, 0u, K, true};
+    if (epi && nvalid > K) s.done = false;
+    if (epi && out_row && nvalid <= K)
+        for (int i = 0; i < K; ++i) out_row[i] = (i < nvalid) ? i : -1;
+    if (q_last + 1 <= K) return;  // every row of the tile keeps all its columns
+
+    if (warp == 0 && lane == 0) {
+        for (int i = 0; i < C::kStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 4);
+        }
+        mbar_init(qbar, 1);
+        fence_barrier_init();
+        prefetch_tmap(&tm_q);
+        prefetch_tmap(&tm_k);
+    }
+    if (warp == 1) tmem_alloc(&s_tmem, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    uint32_t it_p = 0, it_m = 0, it_e = 0;
+    int mode = 0;  // 0..3: radix digit passes (shift 24 - 8 mode); 4: collect
+    while (mode <= 4) {
+        const int shift = 24 - 8 * mode;
+        if (warp == 0) {
+            if (lane == 0) {
+                if (mode == 0) {
+                    mbar_arrive_expect_tx(qbar, C::kQBytes);
+                    for (int kb = 0; kb < C::kKB; ++kb)
+                        tma_load_3d(sQ + kb * (128 * 128), &tm_q, qbar, kb * 64, h, b * T + q0);
+                }
+                for (int kt = 0; kt < nkt; ++kt, ++it_p) {
+                    const uint32_t st = it_p % C::kStages, ph = (it_p / C::kStages) & 1;
+                    mbar_wait(&empty[st], ph ^ 1, wd, 1u);
+                    mbar_arrive_expect_tx(&full[st], C::kKBytes);
+                    unsigned char *dst = sK + st * C::kKBytes;
+                    for (int kb = 0; kb < C::kKB; ++kb)
+                        tma_load_3d(dst + kb * (C::kN * 128), &tm_k, &full[st], kb * 64, h,
+                                    b * T + kt * C::kN);
+                }
+            }
+            __syncwarp();
+        } else if (warp == 1) {
+            if (lane == 0) {
+                if (mode == 0) mbar_wait(qbar, 0, wd, 2u);
+                constexpr uint32_t idesc = idesc_bf16_f32(128, C::kN);
+                const uint32_t qa = smem_u32(sQ);
+                for (int kt = 0; kt < nkt; ++kt, ++it_m) {
+                    const uint32_t st = it_m % C::kStages, ph = (it_m / C::kStages) & 1;
+                    const uint32_t buf = it_m & 1, bph = (it_m >> 1) & 1;
+                    mbar_wait(&tempty[buf], bph ^ 1, wd, 4u);
+                    mbar_wait(&full[st], ph, wd, 8u);
+                    tc_fence_after();
+                    const uint32_t ka = smem_u32(sK + st * C::kKBytes);
+#pragma unroll
+                    for (int kb = 0; kb < C::kKB; ++kb) {
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint64_t ad = sdesc_kmajor_sw128(qa + kb * (128 * 128) + kk * 32);
+                            const uint64_t bd = sdesc_kmajor_sw128(ka + kb * (C::kN * 128) + kk * 32);
+                            mma_bf16(tmem + buf * C::kN, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                        }
+                    }
+                    mma_commit(&empty[st]);
+                    mma_commit(&tfull[buf]);
+                }
+            }
+            __syncwarp();
+        } else {
+            const bool active = !s.done;
+            const bool collect = (mode == 4) && out_row && nvalid > K;
+            if (mode < 4 && active)
+                for (int bin = 0; bin < 256; ++bin) hist[bin * kRows + row] = 0u;
+            int pos = 0, taken = 0;
+            for (int kt = 0; kt < nkt; ++kt, ++it_e) {
+                const uint32_t buf = it_e & 1, bph = (it_e >> 1) & 1;
+                mbar_wait(&tfull[buf], bph, wd, 16u);
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < C::kN / 32; ++c) {
+                    float v[32];
+                    tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN + c * 32, v);
+                    const int jb = kt * C::kN + c * 32;
+                    if (mode < 4) {
+                        if (active && jb < nvalid) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                if (jb + i < nvalid) {
+                                    const uint32_t u = float_key(v[i]);
+                                    if ((u & s.mask) == s.prefix)
+                                        ++hist[((u >> shift) & 0xffu) * kRows + row];
+                                }
+                            }
+                        }
+                    } else if (collect && jb < nvalid) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (jb + i < nvalid) {
+                                const uint32_t m = float_key(v[i]) & s.mask;
+                                if (m > s.prefix || (m == s.prefix && taken < s.need)) {
+                                    if (m == s.prefix) ++taken;
+                                    if (pos < K) out_row[pos] = jb + i;
+                                    ++pos;
+                                }
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);
+            }
+            if (mode < 4 && active) sel_choose(s, hist, row, shift);
+            if (collect)
+                for (int i = pos; i < K; ++i) out_row[i] = -1;
+        }
+        const int more = __syncthreads_or(epi && !s.done);
+        mode = (mode < 4) ? (more ? mode + 1 : 4) : 5;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+template <int DI>
+cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, int B, int T, int H, int K,
+                   cudaStream_t st) {
+    using C = TcCfg<DI>;
+    CUtensorMap mq, mk;
+    if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
+        !make_tmap_rows_bf16(&mk, ik, B, T, H, DI, C::kN))
+        return cudaErrorInvalidValue;
+    auto kern = indexer_topk_tc_kernel<DI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::kSmem);
+    if (e != cudaSuccess) return e;
+    const int nqt = ceil_div(T, kRows);
+    kern<<<nqt * B * H, 192, C::kSmem, st>>>(mq, mk, idx, B, T, H, K, nqt);
+    return cudaGetLastError();
+}
+
 template <typename Tin, int DI>
 cudaError_t run_simt(const void *iq, const void *ik, int32_t *idx, int B, int T, int H, int K,
                      cudaStream_t st) {
@@ -205,7 +422,19 @@ cudaError_t run_simt_d(int DI, const void *iq, const void *ik, int32_t *idx, int
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T, int H,
                                 int DI, int K, int dtype, cudaStream_t st) {
     if (dtype == SGSA_DTYPE_F32) return run_simt_d<float>(DI, iq, ik, idx, B, T, H, K, st);
+    if (indexer_use_tc()) {
+        if (DI == 64) return run_tc<64>(iq, ik, idx, B, T, H, K, st);
+        if (DI == 128) return run_tc<128>(iq, ik, idx, B, T, H, K, st);
+    }
     return run_simt_d<__nv_bfloat16>(DI, iq, ik, idx, B, T, H, K, st);
+}
+
+unsigned int read_index_watchdog(cudaStream_t st) {
+    unsigned int v = 0, z = 0;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_index_watchdog, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (v) cudaMemcpyToSymbol(g_index_watchdog, &z, sizeof(z));
+    return v;
 }
 
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,

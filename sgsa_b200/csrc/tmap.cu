@@ -1,0 +1,41 @@
+// Host-side TMA tensor-map encoding (driver entry point fetched through the
+// runtime, so the library does not link libcuda directly).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tmap.cuh"
+
+namespace sgsa {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    return fn;
+}
+
+bool make_tmap_rows_bf16(CUtensorMap *map, const void *base, int B, int T, int H, int W,
+                         int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || ((uintptr_t)base & 15)) return false;
+    // dims (innermost first): W features, H heads, B*T tokens
+    cuuint64_t dims[3] = {(cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)B * T};
+    cuuint64_t strides[2] = {(cuuint64_t)W * 2, (cuuint64_t)H * W * 2};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace sgsa

@@ -207,3 +207,19 @@ def test_layer_fwd_matches_oracle(dtype, cfgname):
     want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], got_idx, ro, x["mix"])
     assert oracle.rel_l2(out.float().cpu().numpy(), want) < TOL[dtype]
     assert oracle.rel_l2(st.cpu().numpy(), rs) < TOL[dtype]
+
+
+def test_watchdog_clear_after_suite():
+    from sgsa_b200 import _lib
+    assert _lib.load().sgsa_watchdog_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize("T,DI,K", [(1000, 64, 100), (777, 128, 64), (4096, 64, 512)])
+def test_indexer_tc_matches_simt_bitwise_sets(T, DI, K, monkeypatch):
+    """The tensor-core and CUDA-core score paths select the same sets (up to near ties)."""
+    g = torch.Generator().manual_seed(T)
+    iq = torch.randn(2, T, 2, DI, generator=g).bfloat16()
+    ik = torch.randn(2, T, 2, DI, generator=g).bfloat16()
+    got = ops.indexer_topk(iq.cuda(), ik.cuda(), K).cpu().numpy()
+    want, kth = oracle.indexer_topk(iq, ik, K, return_kth=True)
+    check_index_sets(got, want, iq.float(), ik.float(), kth, 1e-5)
