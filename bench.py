@@ -203,7 +203,7 @@ def run_reference(args, ws, rank):
     print(json.dumps(line), flush=True)
 
 
-def stage_times(cfg, d, reps=3):
+def stage_times(cfg, d, reps=3, only=None):
     """Per-stage device time (ms) of the layer, each stage called through the C ABI."""
     from sgsa_b200 import _lib, ops
 
@@ -235,7 +235,12 @@ def stage_times(cfg, d, reps=3):
                                             st.cuda_stream), "attn")
 
     res = {}
-    for name, fn in (("delta", delta), ("indexer_topk", index), ("sparse_attn_mix", attn)):
+    stages = (("delta", delta), ("indexer_topk", index), ("sparse_attn_mix", attn))
+    if only == "sparse_attn_mix":
+        index()  # the attention stage reads the indexer's output
+    for name, fn in stages:
+        if only and name != only:
+            continue
         fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -247,6 +252,20 @@ def stage_times(cfg, d, reps=3):
         res[name] = e0.elapsed_time(e1) / reps
     del ops
     return res
+
+
+def run_only(args):
+    """Run a single stage on a scaled configuration (for ncu captures)."""
+    from sgsa_b200.inputs import CONFIGS, make_inputs
+
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[CONFIG_NAME]
+    kw = {n: getattr(args, n) for n in ("B", "T", "H") if getattr(args, n)}
+    cfg = cfg.scaled(**kw) if kw else cfg
+    d = {n: t.cuda() for n, t in make_inputs(cfg, seed=0).items()}
+    res = stage_times(cfg, d, reps=args.steps, only=args.only)
+    print(json.dumps({"stage": args.only, "ms": res[args.only],
+                      "config": {"B": cfg.B, "T": cfg.T, "H": cfg.H}}))
 
 
 def run_ours(args, ws, rank, local):
@@ -347,7 +366,15 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--only", default=None, choices=["delta", "indexer_topk", "sparse_attn_mix"],
+                    help="profiling aid: run one stage --steps times on a (scaled) config, no JSON")
+    ap.add_argument("--B", type=int, default=None)
+    ap.add_argument("--T", type=int, default=None)
+    ap.add_argument("--H", type=int, default=None)
     args = ap.parse_args()
+    if args.only:
+        run_only(args)
+        return
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

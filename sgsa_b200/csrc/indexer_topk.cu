@@ -191,40 +191,111 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 // ---- tcgen05 indexer: bf16 scores on the tensor cores, fp32 in TMEM. --------
 //
 // Warp roles of the 192-thread CTA (one CTA per 128-query tile of one (b, h)):
-//   warp 0  TMA producer: the query tile once, then key tiles of 128 rows
-//           into a ring of shared-memory stages;
+//   warp 0  TMA producer: the query tile once, then key tiles into a ring of
+//           shared-memory stages;
 //   warp 1  TMEM owner and MMA issuer: S_tile = Q K^T, M=128 (queries) x
-//           N=128 (keys) x K=DI, into one of two TMEM accumulators;
+//           N=kN (keys) x K=DI, into one of two TMEM accumulators;
 //   warps 2-5  one thread per query row: tcgen05.ld of its row of the tile,
 //           radix histogram / collect, as in select_rows above.
 // The key stream is replayed once per radix pass; the tensor cores recompute
-// the identical fp32 scores each time.
+// the identical fp32 scores each time.  For rows shorter than 65536 the
+// histogram packs two 16-bit counters per 32-bit word (64 KB), so the CTA
+// needs ~105 KB and two CTAs share an SM; their epilogues hide each other's
+// latencies.  Counters are bumped with shared-memory atomics that return
+// nothing, so consecutive increments do not wait on each other.
 static __device__ unsigned int g_index_watchdog;
 
-template <int DI>
+template <bool PACKED>
+__device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, int col) {
+    if (PACKED) return (hist[(bin >> 1) * kRows + col] >> ((bin & 1) << 4)) & 0xffffu;
+    return hist[bin * kRows + col];
+}
+
+template <bool PACKED>
+__device__ __forceinline__ void sel_choose_p(SelState &s, const uint32_t *hist, int col,
+                                             int shift) {
+    int cum = 0, chosen = 0, cnt = 0;
+    for (int bin = 255; bin >= 0; --bin) {
+        cnt = (int)hist_count<PACKED>(hist, bin, col);
+        if (cum + cnt >= s.need) { chosen = bin; break; }
+        cum += cnt;
+    }
+    s.need -= cum;
+    s.prefix |= (uint32_t)chosen << shift;
+    s.mask |= 0xffu << shift;
+    if (cnt == s.need || shift == 0) s.done = true;
+}
+
+template <int DI, bool PACKED>
 struct TcCfg {
     static constexpr int kKB = DI / 64;                // 128-byte K blocks
-    static constexpr int kN = 128;                     // keys per tile
-    static constexpr int kStages = (DI == 64) ? 4 : 2;
+    static constexpr int kN = PACKED ? 64 : 128;       // keys per tile
+    static constexpr int kStages = PACKED ? 3 : 2;
     static constexpr int kQBytes = 128 * DI * 2;
     static constexpr int kKBytes = kN * DI * 2;
-    static constexpr int kHistBytes = 256 * kRows * 4;
+    static constexpr int kHistBytes = (PACKED ? 128 : 256) * kRows * 4;
     static constexpr int kBars = 2 * kStages + 5;
     static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
+    static constexpr int kMinBlocks = (kSmem * 2 + 2048 <= 233472) ? 2 : 1;
+    static constexpr int kTmemCols = 2 * kN;
 };
 
-template <int DI>
-__global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
-    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-    int32_t *__restrict__ idx, int B, int T, int H, int K, int nqt) {
-    using C = TcCfg<DI>;
+// Histogram update of one 32-column chunk; FULL skips the causal bound check.
+template <bool PASS0, bool FULL, bool PACKED>
+__device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol, int jb,
+                                           int nvalid, uint32_t mask, uint32_t prefix,
+                                           int shift) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        if (FULL || jb + i < nvalid) {
+            const uint32_t u = float_key(v[i]);
+            if (PASS0 || (u & mask) == prefix) {
+                const uint32_t d = (u >> shift) & 0xffu;
+                if (PACKED) atomicAdd(hcol + (d >> 1) * kRows, 1u << ((d & 1u) << 4));
+                else atomicAdd(hcol + d * kRows, 1u);
+            }
+        }
+    }
+}
+
+// Output row writer: indices are staged four at a time and stored as one
+// 16-byte vector when the row is 16-byte aligned (K % 4 == 0).
+struct RowWriter {
+    int32_t *row;
+    int pos, K;
+    int a0, a1, a2;
+    bool vec;
+    __device__ __forceinline__ void put(int j) {
+        if (!vec) {
+            if (pos < K) row[pos] = j;
+            ++pos;
+            return;
+        }
+        const int slot = pos & 3;
+        if (slot == 0) a0 = j;
+        else if (slot == 1) a1 = j;
+        else if (slot == 2) a2 = j;
+        else if (pos < K) reinterpret_cast<int4 *>(row)[pos >> 2] = make_int4(a0, a1, a2, j);
+        ++pos;
+    }
+    __device__ __forceinline__ void finish() {
+        while (pos < K) put(-1);
+    }
+};
+
+template <int DI, bool PACKED>
+__global__ void __launch_bounds__(192, (TcCfg<DI, PACKED>::kMinBlocks))
+indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx, int B,
+                       int T, int H, int K, int nqt) {
+    using C = TcCfg<DI, PACKED>;
     using namespace sm100;
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     unsigned char *sQ = base;
     unsigned char *sK = sQ + C::kQBytes;
     uint32_t *hist = (uint32_t *)(sK + C::kStages * C::kKBytes);
-    uint64_t *bars = (uint64_t *)(hist + 256 * kRows);
+    uint64_t *bars = (uint64_t *)((unsigned char *)hist + C::kHistBytes);
     uint64_t *full = bars, *empty = bars + C::kStages, *tfull = bars + 2 * C::kStages,
              *tempty = tfull + 2, *qbar = tempty + 2;
     __shared__ uint32_t s_tmem;
@@ -238,7 +309,6 @@ __global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
     const int nkt = q_last / C::kN + 1;
     unsigned int *wd = &g_index_watchdog;
 
-    // epilogue-thread row state
     const bool epi = warp >= 2;
     const int quad = warp & 3;               // TMEM lane quarter this warp may access
     const int row = quad * 32 + lane;
@@ -265,7 +335,7 @@ __global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
         prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
     }
-    if (warp == 1) tmem_alloc(&s_tmem, 256);
+    if (warp == 1) tmem_alloc(&s_tmem, C::kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -322,28 +392,30 @@ __global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
         } else {
             const bool active = !s.done;
             const bool collect = (mode == 4) && out_row && nvalid > K;
+            uint32_t *hcol = hist + row;
             if (mode < 4 && active)
-                for (int bin = 0; bin < 256; ++bin) hist[bin * kRows + row] = 0u;
-            int pos = 0, taken = 0;
+                for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
+            RowWriter wr{out_row, 0, K, 0, 0, 0, (K & 3) == 0};
+            int taken = 0;
             for (int kt = 0; kt < nkt; ++kt, ++it_e) {
                 const uint32_t buf = it_e & 1, bph = (it_e >> 1) & 1;
                 mbar_wait(&tfull[buf], bph, wd, 16u);
                 tc_fence_after();
+                const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN;
+                const bool full_tile = (kt + 1) * C::kN <= nvalid;
 #pragma unroll 1
                 for (int c = 0; c < C::kN / 32; ++c) {
                     float v[32];
-                    tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN + c * 32, v);
+                    tmem_ld32(taddr + c * 32, v);
                     const int jb = kt * C::kN + c * 32;
                     if (mode < 4) {
-                        if (active && jb < nvalid) {
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                if (jb + i < nvalid) {
-                                    const uint32_t u = float_key(v[i]);
-                                    if ((u & s.mask) == s.prefix)
-                                        ++hist[((u >> shift) & 0xffu) * kRows + row];
-                                }
-                            }
+                        if (!active || jb >= nvalid) continue;
+                        if (mode == 0) {
+                            if (full_tile) hist_chunk<true, true, PACKED>(v, hcol, jb, nvalid, 0u, 0u, 24);
+                            else hist_chunk<true, false, PACKED>(v, hcol, jb, nvalid, 0u, 0u, 24);
+                        } else {
+                            if (full_tile) hist_chunk<false, true, PACKED>(v, hcol, jb, nvalid, s.mask, s.prefix, shift);
+                            else hist_chunk<false, false, PACKED>(v, hcol, jb, nvalid, s.mask, s.prefix, shift);
                         }
                     } else if (collect && jb < nvalid) {
 #pragma unroll
@@ -352,8 +424,7 @@ __global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
                                 const uint32_t m = float_key(v[i]) & s.mask;
                                 if (m > s.prefix || (m == s.prefix && taken < s.need)) {
                                     if (m == s.prefix) ++taken;
-                                    if (pos < K) out_row[pos] = jb + i;
-                                    ++pos;
+                                    wr.put(jb + i);
                                 }
                             }
                         }
@@ -363,9 +434,8 @@ __global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
-            if (mode < 4 && active) sel_choose(s, hist, row, shift);
-            if (collect)
-                for (int i = pos; i < K; ++i) out_row[i] = -1;
+            if (mode < 4 && active) sel_choose_p<PACKED>(s, hist, row, shift);
+            if (collect) wr.finish();
         }
         const int more = __syncthreads_or(epi && !s.done);
         mode = (mode < 4) ? (more ? mode + 1 : 4) : 5;
@@ -373,24 +443,32 @@ __global__ void __launch_bounds__(192, 1) indexer_topk_tc_kernel(
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 256);
+    if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
-template <int DI>
+template <int DI, bool PACKED>
 cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, int B, int T, int H, int K,
                    cudaStream_t st) {
-    using C = TcCfg<DI>;
+    using C = TcCfg<DI, PACKED>;
     CUtensorMap mq, mk;
     if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
         !make_tmap_rows_bf16(&mk, ik, B, T, H, DI, C::kN))
         return cudaErrorInvalidValue;
-    auto kern = indexer_topk_tc_kernel<DI>;
+    auto kern = indexer_topk_tc_kernel<DI, PACKED>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)C::kSmem);
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRows);
     kern<<<nqt * B * H, 192, C::kSmem, st>>>(mq, mk, idx, B, T, H, K, nqt);
     return cudaGetLastError();
+}
+
+template <int DI>
+cudaError_t run_tc_t(const void *iq, const void *ik, int32_t *idx, int B, int T, int H, int K,
+                     cudaStream_t st) {
+    // 16-bit counters hold any count below 65536, the longest row they can see.
+    if (T < 65536) return run_tc<DI, true>(iq, ik, idx, B, T, H, K, st);
+    return run_tc<DI, false>(iq, ik, idx, B, T, H, K, st);
 }
 
 template <typename Tin, int DI>
@@ -423,8 +501,8 @@ cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, in
                                 int DI, int K, int dtype, cudaStream_t st) {
     if (dtype == SGSA_DTYPE_F32) return run_simt_d<float>(DI, iq, ik, idx, B, T, H, K, st);
     if (indexer_use_tc()) {
-        if (DI == 64) return run_tc<64>(iq, ik, idx, B, T, H, K, st);
-        if (DI == 128) return run_tc<128>(iq, ik, idx, B, T, H, K, st);
+        if (DI == 64) return run_tc_t<64>(iq, ik, idx, B, T, H, K, st);
+        if (DI == 128) return run_tc_t<128>(iq, ik, idx, B, T, H, K, st);
     }
     return run_simt_d<__nv_bfloat16>(DI, iq, ik, idx, B, T, H, K, st);
 }

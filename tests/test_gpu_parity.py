@@ -223,3 +223,24 @@ def test_indexer_tc_matches_simt_bitwise_sets(T, DI, K, monkeypatch):
     got = ops.indexer_topk(iq.cuda(), ik.cuda(), K).cpu().numpy()
     want, kth = oracle.indexer_topk(iq, ik, K, return_kth=True)
     check_index_sets(got, want, iq.float(), ik.float(), kth, 1e-5)
+
+
+def test_indexer_max_length_rows():
+    """T = 65536 (the long-context length; 32-bit histogram path): the heaviest
+    rows and a few early ones against the oracle."""
+    T, DI, K = 65536, 64, 2048
+    g = torch.Generator().manual_seed(99)
+    iq = torch.randn(1, T, 1, DI, generator=g).bfloat16()
+    ik = torch.randn(1, T, 1, DI, generator=g).bfloat16()
+    got = ops.indexer_topk(iq.cuda(), ik.cuda(), K).cpu().numpy()
+    for t0, t1 in ((T - 48, T), (2040, 2060), (30000, 30016)):
+        want, kth = oracle.indexer_topk(iq, ik, K, t_range=(t0, t1), return_kth=True)
+        sub = got[:, :, t0:t1]
+        iqd, ikd = iq.double().numpy(), ik.double().numpy()
+        for b, h, tt in np.argwhere((sub != want).any(-1)):
+            a = set(sub[b, h, tt].tolist()) - {-1}
+            w = set(want[b, h, tt].tolist()) - {-1}
+            assert len(a) == len(w)
+            for j in a ^ w:
+                s = float(iqd[b, t0 + tt, h] @ ikd[b, j, h])
+                assert abs(s - kth[b, h, tt]) <= 1e-5 * max(1.0, abs(kth[b, h, tt]))
