@@ -240,48 +240,47 @@ struct TcCfg {
     static constexpr int kTmemCols = 2 * kN;
 };
 
+__device__ __forceinline__ void red_shared_if(uint32_t *addr, uint32_t inc, bool pred) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p red.shared.add.u32 [%0], %1;\n\t}" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(addr)),
+                 "r"(inc), "r"((uint32_t)pred)
+                 : "memory");
+}
+
 // Histogram update of one 32-column chunk; FULL skips the causal bound check.
+// Predicated shared-memory reductions (no branch, no returned value).
 template <bool PASS0, bool FULL, bool PACKED>
 __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol, int jb,
                                            int nvalid, uint32_t mask, uint32_t prefix,
                                            int shift) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        if (FULL || jb + i < nvalid) {
-            const uint32_t u = float_key(v[i]);
-            if (PASS0 || (u & mask) == prefix) {
-                const uint32_t d = (u >> shift) & 0xffu;
-                if (PACKED) atomicAdd(hcol + (d >> 1) * kRows, 1u << ((d & 1u) << 4));
-                else atomicAdd(hcol + d * kRows, 1u);
-            }
-        }
+        const uint32_t u = float_key(v[i]);
+        const bool in = (FULL || jb + i < nvalid) && (PASS0 || (u & mask) == prefix);
+        const uint32_t d = (u >> shift) & 0xffu;
+        if (PACKED) red_shared_if(hcol + (d >> 1) * kRows, 1u << ((d & 1u) << 4), in);
+        else red_shared_if(hcol + d * kRows, 1u, in);
     }
 }
 
-// Output row writer: indices are staged four at a time and stored as one
-// 16-byte vector when the row is 16-byte aligned (K % 4 == 0).
-struct RowWriter {
-    int32_t *row;
-    int pos, K;
-    int a0, a1, a2;
-    bool vec;
-    __device__ __forceinline__ void put(int j) {
-        if (!vec) {
-            if (pos < K) row[pos] = j;
-            ++pos;
-            return;
-        }
-        const int slot = pos & 3;
-        if (slot == 0) a0 = j;
-        else if (slot == 1) a1 = j;
-        else if (slot == 2) a2 = j;
-        else if (pos < K) reinterpret_cast<int4 *>(row)[pos >> 2] = make_int4(a0, a1, a2, j);
-        ++pos;
+// Collect of one 32-column chunk: selected column indices go, branch-free,
+// into this row's 32-slot ring in shared memory (ring[slot * kRows + row]),
+// which is then flushed in order to the output row.
+template <bool FULL>
+__device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ring, int jb,
+                                              int nvalid, const SelState &s, int &pos,
+                                              int &taken) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t m = float_key(v[i]) & s.mask;
+        const bool ok = FULL || jb + i < nvalid;
+        const bool eq = ok && m == s.prefix && taken < s.need;
+        const bool sel = eq || (ok && m > s.prefix);
+        ring[(pos & 31) * kRows] = (uint32_t)(jb + i);
+        pos += sel;
+        taken += eq;
     }
-    __device__ __forceinline__ void finish() {
-        while (pos < K) put(-1);
-    }
-};
+}
 
 template <int DI, bool PACKED>
 __global__ void __launch_bounds__(192, (TcCfg<DI, PACKED>::kMinBlocks))
@@ -395,8 +394,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             uint32_t *hcol = hist + row;
             if (mode < 4 && active)
                 for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
-            RowWriter wr{out_row, 0, K, 0, 0, 0, (K & 3) == 0};
-            int taken = 0;
+            uint32_t *ring = hist + row;  // the histogram is idle during the collect pass
+            int pos = 0, taken = 0, flushed = 0;
             for (int kt = 0; kt < nkt; ++kt, ++it_e) {
                 const uint32_t buf = it_e & 1, bph = (it_e >> 1) & 1;
                 mbar_wait(&tfull[buf], bph, wd, 16u);
@@ -418,16 +417,10 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                             else hist_chunk<false, false, PACKED>(v, hcol, jb, nvalid, s.mask, s.prefix, shift);
                         }
                     } else if (collect && jb < nvalid) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            if (jb + i < nvalid) {
-                                const uint32_t m = float_key(v[i]) & s.mask;
-                                if (m > s.prefix || (m == s.prefix && taken < s.need)) {
-                                    if (m == s.prefix) ++taken;
-                                    wr.put(jb + i);
-                                }
-                            }
-                        }
+                        if (full_tile) collect_chunk<true>(v, ring, jb, nvalid, s, pos, taken);
+                        else collect_chunk<false>(v, ring, jb, nvalid, s, pos, taken);
+                        for (; flushed < pos; ++flushed)
+                            if (flushed < K) out_row[flushed] = (int32_t)ring[(flushed & 31) * kRows];
                     }
                 }
                 tc_fence_before();
@@ -435,7 +428,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
             if (mode < 4 && active) sel_choose_p<PACKED>(s, hist, row, shift);
-            if (collect) wr.finish();
+            if (collect)
+                for (int i = flushed; i < K; ++i) out_row[i] = -1;
         }
         const int more = __syncthreads_or(epi && !s.done);
         mode = (mode < 4) ? (more ? mode + 1 : 4) : 5;
