@@ -190,20 +190,39 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 
 // ---- tcgen05 indexer: bf16 scores on the tensor cores, fp32 in TMEM. --------
 //
-// Warp roles of the 192-thread CTA (one CTA per 128-query tile of one (b, h)):
+// Warp roles of the 320-thread CTA (one CTA per 128-query tile of one (b, h)):
 //   warp 0  TMA producer: the query tile once, then key tiles into a ring of
 //           shared-memory stages;
 //   warp 1  TMEM owner and MMA issuer: S_tile = Q K^T, M=128 (queries) x
 //           N=kN (keys) x K=DI, into one of two TMEM accumulators;
-//   warps 2-5  one thread per query row: tcgen05.ld of its row of the tile,
-//           radix histogram / collect, as in select_rows above.
-// The key stream is replayed once per radix pass; the tensor cores recompute
-// the identical fp32 scores each time.  For rows shorter than 65536 the
-// histogram packs two 16-bit counters per 32-bit word (64 KB), so the CTA
-// needs ~105 KB and two CTAs share an SM; their epilogues hide each other's
-// latencies.  Counters are bumped with shared-memory atomics that return
-// nothing, so consecutive increments do not wait on each other.
+//   warps 2-9  two threads per query row (warps w and w+4 read the same TMEM
+//           lane quarter and split the tile's columns): tcgen05.ld of their
+//           part of the row, radix histogram; the first thread of each row
+//           also runs the collect pass, which must walk the row in order.
+// The key stream is replayed once per pass; the tensor cores recompute the
+// identical fp32 scores each time.
+//
+// Digits.  The first pass bins the top 12 bits of the order-preserving key
+// (sign, exponent, 3 mantissa bits: 1/8-octave bins) of positive scores in
+// [2^-16, 2^16), clamping the rest into bins 0 and 255.  If a row's k-th score
+// falls in an interior bin, its 12-bit prefix is known after one pass and the
+// remaining 20 bits follow as 8-, 8- and 4-bit digits; if it falls in a clamp
+// bin, the row restarts with plain 8-bit digits from the top.  Either way the
+// selection is exact.  Rows shorter than 65536 use 16-bit counters packed two
+// per 32-bit word (64 KB), so the CTA needs ~105 KB and two CTAs share an SM.
+// Counters are bumped with predicated shared-memory reductions: no branches,
+// no returned values, and the two threads of a row may share a counter.
 static __device__ unsigned int g_index_watchdog;
+
+constexpr int kFastBase = 0x800 + (111 << 3);  // key>>20 of 2^-16
+constexpr int kEpiThreads = 256;
+
+struct RowSel {
+    uint32_t prefix, mask;
+    int need;
+    int top;    // bits [top-1 : 0] of the k-th key are still unknown
+    bool done;
+};
 
 template <bool PACKED>
 __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, int col) {
@@ -211,19 +230,34 @@ __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, in
     return hist[bin * kRows + col];
 }
 
-template <bool PACKED>
-__device__ __forceinline__ void sel_choose_p(SelState &s, const uint32_t *hist, int col,
-                                             int shift) {
+// Choose the bin holding the need-th largest remaining key.  FAST: the
+// first-pass clamped 12-bit digit.
+template <bool PACKED, bool FAST>
+__device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int col, int K) {
+    const int w = FAST ? 8 : min(8, s.top);
     int cum = 0, chosen = 0, cnt = 0;
-    for (int bin = 255; bin >= 0; --bin) {
+    for (int bin = (1 << w) - 1; bin >= 0; --bin) {
         cnt = (int)hist_count<PACKED>(hist, bin, col);
         if (cum + cnt >= s.need) { chosen = bin; break; }
         cum += cnt;
     }
-    s.need -= cum;
-    s.prefix |= (uint32_t)chosen << shift;
-    s.mask |= 0xffu << shift;
-    if (cnt == s.need || shift == 0) s.done = true;
+    if (FAST) {
+        if (chosen == 0 || chosen == 255) {  // outside the fast window: plain radix
+            s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32;
+            return;
+        }
+        s.need -= cum;
+        s.prefix = (uint32_t)(kFastBase + chosen) << 20;
+        s.mask = 0xfff00000u;
+        s.top = 20;
+    } else {
+        const int shift = s.top - w;
+        s.need -= cum;
+        s.prefix |= (uint32_t)chosen << shift;
+        s.mask |= ((1u << w) - 1u) << shift;
+        s.top = shift;
+    }
+    if (cnt == s.need || s.top == 0) s.done = true;
 }
 
 template <int DI, bool PACKED>
@@ -234,10 +268,12 @@ struct TcCfg {
     static constexpr int kQBytes = 128 * DI * 2;
     static constexpr int kKBytes = kN * DI * 2;
     static constexpr int kHistBytes = (PACKED ? 128 : 256) * kRows * 4;
-    static constexpr int kBars = 2 * kStages + 5;
+    static constexpr int kAcc = PACKED ? 4 : 2;        // TMEM accumulator buffers
+    static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
     static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
     static constexpr int kMinBlocks = (kSmem * 2 + 2048 <= 233472) ? 2 : 1;
-    static constexpr int kTmemCols = 2 * kN;
+    static constexpr int kTmemCols = kAcc * kN;
+    static constexpr int kThreads = 64 + kEpiThreads;
 };
 
 __device__ __forceinline__ void red_shared_if(uint32_t *addr, uint32_t inc, bool pred) {
@@ -247,17 +283,32 @@ __device__ __forceinline__ void red_shared_if(uint32_t *addr, uint32_t inc, bool
                  : "memory");
 }
 
-// Histogram update of one 32-column chunk; FULL skips the causal bound check.
-// Predicated shared-memory reductions (no branch, no returned value).
-template <bool PASS0, bool FULL, bool PACKED>
+__device__ __forceinline__ void epi_bar() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
+}
+
+// Histogram update of one 32-column chunk.  FAST: clamped 12-bit first digit;
+// else the row's next digit among keys matching its prefix.  FULL skips the
+// causal bound check.
+template <bool FAST, bool FULL, bool PACKED>
 __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol, int jb,
-                                           int nvalid, uint32_t mask, uint32_t prefix,
-                                           int shift) {
+                                           int nvalid, const RowSel &s) {
+    const int w = min(8, s.top);
+    const int shift = s.top - w;
+    const uint32_t dmask = (1u << w) - 1u;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
         const uint32_t u = float_key(v[i]);
-        const bool in = (FULL || jb + i < nvalid) && (PASS0 || (u & mask) == prefix);
-        const uint32_t d = (u >> shift) & 0xffu;
+        const bool ok = FULL || jb + i < nvalid;
+        uint32_t d;
+        bool in;
+        if (FAST) {
+            d = (uint32_t)min(max((int)(u >> 20) - kFastBase, 0), 255);
+            in = ok;
+        } else {
+            d = (u >> shift) & dmask;
+            in = ok && (u & s.mask) == s.prefix;
+        }
         if (PACKED) red_shared_if(hcol + (d >> 1) * kRows, 1u << ((d & 1u) << 4), in);
         else red_shared_if(hcol + d * kRows, 1u, in);
     }
@@ -265,10 +316,10 @@ __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol,
 
 // Collect of one 32-column chunk: selected column indices go, branch-free,
 // into this row's 32-slot ring in shared memory (ring[slot * kRows + row]),
-// which is then flushed in order to the output row.
+// which the caller then flushes in order to the output row.
 template <bool FULL>
 __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ring, int jb,
-                                              int nvalid, const SelState &s, int &pos,
+                                              int nvalid, const RowSel &s, int &pos,
                                               int &taken) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -283,7 +334,7 @@ __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ri
 }
 
 template <int DI, bool PACKED>
-__global__ void __launch_bounds__(192, (TcCfg<DI, PACKED>::kMinBlocks))
+__global__ void __launch_bounds__(TcCfg<DI, PACKED>::kThreads, (TcCfg<DI, PACKED>::kMinBlocks))
 indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx, int B,
                        int T, int H, int K, int nqt) {
@@ -296,7 +347,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     uint32_t *hist = (uint32_t *)(sK + C::kStages * C::kKBytes);
     uint64_t *bars = (uint64_t *)((unsigned char *)hist + C::kHistBytes);
     uint64_t *full = bars, *empty = bars + C::kStages, *tfull = bars + 2 * C::kStages,
-             *tempty = tfull + 2, *qbar = tempty + 2;
+             *tempty = tfull + C::kAcc, *qbar = tempty + C::kAcc;
     __shared__ uint32_t s_tmem;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -309,14 +360,15 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     unsigned int *wd = &g_index_watchdog;
 
     const bool epi = warp >= 2;
-    const int quad = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = epi ? (warp - 2) >> 2 : 0;  // which half of the tile's columns
+    const int quad = warp & 3;                    // TMEM lane quarter this warp may access
     const int row = quad * 32 + lane;
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
     int32_t *out_row = (epi && t < T) ? idx + ((size_t)bh * T + t) * K : nullptr;
-    SelState s{0u, 0u, K, true};
+    RowSel s{0u, 0u, K, 32, true};
     if (epi && nvalid > K) s.done = false;
-    if (epi && out_row && nvalid <= K)
+    if (epi && half == 0 && out_row && nvalid <= K)
         for (int i = 0; i < K; ++i) out_row[i] = (i < nvalid) ? i : -1;
     if (q_last + 1 <= K) return;  // every row of the tile keeps all its columns
 
@@ -325,9 +377,9 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < C::kAcc; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 4);
+            mbar_init(&tempty[i], kEpiThreads / 32);
         }
         mbar_init(qbar, 1);
         fence_barrier_init();
@@ -340,13 +392,14 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
+    constexpr int kMaxDigitPasses = 5;  // fast digit + 4 plain digits after a fallback
+    constexpr int kChunksPerHalf = C::kN / 64;
     uint32_t it_p = 0, it_m = 0, it_e = 0;
-    int mode = 0;  // 0..3: radix digit passes (shift 24 - 8 mode); 4: collect
-    while (mode <= 4) {
-        const int shift = 24 - 8 * mode;
+    bool collecting = false;
+    for (int pass = 0;; ++pass) {
         if (warp == 0) {
             if (lane == 0) {
-                if (mode == 0) {
+                if (pass == 0) {
                     mbar_arrive_expect_tx(qbar, C::kQBytes);
                     for (int kb = 0; kb < C::kKB; ++kb)
                         tma_load_3d(sQ + kb * (128 * 128), &tm_q, qbar, kb * 64, h, b * T + q0);
@@ -364,12 +417,12 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
         } else if (warp == 1) {
             if (lane == 0) {
-                if (mode == 0) mbar_wait(qbar, 0, wd, 2u);
+                if (pass == 0) mbar_wait(qbar, 0, wd, 2u);
                 constexpr uint32_t idesc = idesc_bf16_f32(128, C::kN);
                 const uint32_t qa = smem_u32(sQ);
                 for (int kt = 0; kt < nkt; ++kt, ++it_m) {
                     const uint32_t st = it_m % C::kStages, ph = (it_m / C::kStages) & 1;
-                    const uint32_t buf = it_m & 1, bph = (it_m >> 1) & 1;
+                    const uint32_t buf = it_m % C::kAcc, bph = (it_m / C::kAcc) & 1;
                     mbar_wait(&tempty[buf], bph ^ 1, wd, 4u);
                     mbar_wait(&full[st], ph, wd, 8u);
                     tc_fence_after();
@@ -390,33 +443,43 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
         } else {
             const bool active = !s.done;
-            const bool collect = (mode == 4) && out_row && nvalid > K;
             uint32_t *hcol = hist + row;
-            if (mode < 4 && active)
-                for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
+            const bool collect = collecting && half == 0 && out_row && nvalid > K;
+            if (!collecting) {
+                if (half == 0 && active)
+                    for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
+                epi_bar();
+            }
             uint32_t *ring = hist + row;  // the histogram is idle during the collect pass
             int pos = 0, taken = 0, flushed = 0;
             for (int kt = 0; kt < nkt; ++kt, ++it_e) {
-                const uint32_t buf = it_e & 1, bph = (it_e >> 1) & 1;
+                const uint32_t buf = it_e % C::kAcc, bph = (it_e / C::kAcc) & 1;
                 mbar_wait(&tfull[buf], bph, wd, 16u);
                 tc_fence_after();
                 const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN;
                 const bool full_tile = (kt + 1) * C::kN <= nvalid;
+                if (!collecting) {
 #pragma unroll 1
-                for (int c = 0; c < C::kN / 32; ++c) {
-                    float v[32];
-                    tmem_ld32(taddr + c * 32, v);
-                    const int jb = kt * C::kN + c * 32;
-                    if (mode < 4) {
+                    for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
+                        float v[32];
+                        tmem_ld32(taddr + c * 32, v);
+                        const int jb = kt * C::kN + c * 32;
                         if (!active || jb >= nvalid) continue;
-                        if (mode == 0) {
-                            if (full_tile) hist_chunk<true, true, PACKED>(v, hcol, jb, nvalid, 0u, 0u, 24);
-                            else hist_chunk<true, false, PACKED>(v, hcol, jb, nvalid, 0u, 0u, 24);
+                        if (pass == 0) {
+                            if (full_tile) hist_chunk<true, true, PACKED>(v, hcol, jb, nvalid, s);
+                            else hist_chunk<true, false, PACKED>(v, hcol, jb, nvalid, s);
                         } else {
-                            if (full_tile) hist_chunk<false, true, PACKED>(v, hcol, jb, nvalid, s.mask, s.prefix, shift);
-                            else hist_chunk<false, false, PACKED>(v, hcol, jb, nvalid, s.mask, s.prefix, shift);
+                            if (full_tile) hist_chunk<false, true, PACKED>(v, hcol, jb, nvalid, s);
+                            else hist_chunk<false, false, PACKED>(v, hcol, jb, nvalid, s);
                         }
-                    } else if (collect && jb < nvalid) {
+                    }
+                } else if (half == 0) {
+#pragma unroll 1
+                    for (int c = 0; c < C::kN / 32; ++c) {
+                        float v[32];
+                        tmem_ld32(taddr + c * 32, v);
+                        const int jb = kt * C::kN + c * 32;
+                        if (!collect || jb >= nvalid) continue;
                         if (full_tile) collect_chunk<true>(v, ring, jb, nvalid, s, pos, taken);
                         else collect_chunk<false>(v, ring, jb, nvalid, s, pos, taken);
                         for (; flushed < pos; ++flushed)
@@ -427,12 +490,19 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
-            if (mode < 4 && active) sel_choose_p<PACKED>(s, hist, row, shift);
-            if (collect)
+            if (!collecting) {
+                epi_bar();  // every reduction of the pass has landed
+                if (active) {
+                    if (pass == 0) row_choose<PACKED, true>(s, hist, row, K);
+                    else row_choose<PACKED, false>(s, hist, row, K);
+                }
+            } else if (collect) {
                 for (int i = flushed; i < K; ++i) out_row[i] = -1;
+            }
         }
         const int more = __syncthreads_or(epi && !s.done);
-        mode = (mode < 4) ? (more ? mode + 1 : 4) : 5;
+        if (collecting) break;
+        if (!more || pass + 1 >= kMaxDigitPasses) collecting = true;
     }
     tc_fence_before();
     __syncthreads();
@@ -453,7 +523,7 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, int B, int T, i
                                          (int)C::kSmem);
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRows);
-    kern<<<nqt * B * H, 192, C::kSmem, st>>>(mq, mk, idx, B, T, H, K, nqt);
+    kern<<<nqt * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, B, T, H, K, nqt);
     return cudaGetLastError();
 }
 

@@ -244,3 +244,25 @@ def test_indexer_max_length_rows():
             for j in a ^ w:
                 s = float(iqd[b, t0 + tt, h] @ ikd[b, j, h])
                 assert abs(s - kth[b, h, tt]) <= 1e-5 * max(1.0, abs(kth[b, h, tt]))
+
+
+@pytest.mark.parametrize("kind", ["negative", "huge", "tiny", "mixed"])
+def test_indexer_tc_score_ranges(kind):
+    """Scores outside the fast first-digit window (all negative, > 2^16, < 2^-16)
+    take the plain radix path; results stay exact."""
+    g = torch.Generator().manual_seed(17)
+    T, DI, K = 600, 64, 64
+    iq = torch.randn(1, T, 2, DI, generator=g)
+    ik = torch.randn(1, T, 2, DI, generator=g)
+    if kind == "negative":
+        iq, ik = -iq.abs(), ik.abs()
+    elif kind == "huge":
+        iq, ik = iq * 1e3, ik * 1e3
+    elif kind == "tiny":
+        iq, ik = iq * 1e-4, ik * 1e-4
+    else:
+        iq[:, ::2] *= 1e3
+    iq, ik = iq.bfloat16(), ik.bfloat16()
+    got = ops.indexer_topk(iq.cuda(), ik.cuda(), K).cpu().numpy()
+    want, kth = oracle.indexer_topk(iq, ik, K, return_kth=True)
+    check_index_sets(got, want, iq.float(), ik.float(), kth, 1e-5)
