@@ -220,9 +220,16 @@ constexpr int kEpiThreads = 256;
 struct RowSel {
     uint32_t prefix, mask;
     int need;
-    int top;    // bits [top-1 : 0] of the k-th key are still unknown
+    int top;     // bits [top-1 : 0] of the k-th key are still unknown
     bool done;
+    bool plain;  // the row left the fast window: full order-preserving keys
 };
+
+// Key of a score for a row whose k-th score is a positive float: the raw bits
+// with the sign flipped order every positive score correctly and put every
+// negative one (and -0.0) below any positive prefix, which is all the
+// comparisons against such a prefix need.
+__device__ __forceinline__ uint32_t fast_key(float f) { return __float_as_uint(f) ^ 0x80000000u; }
 
 template <bool PACKED>
 __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, int col) {
@@ -243,7 +250,7 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
     }
     if (FAST) {
         if (chosen == 0 || chosen == 255) {  // outside the fast window: plain radix
-            s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32;
+            s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32; s.plain = true;
             return;
         }
         s.need -= cum;
@@ -287,29 +294,32 @@ __device__ __forceinline__ void epi_bar() {
     asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
 }
 
-// Histogram update of one 32-column chunk.  FAST: clamped 12-bit first digit;
-// else the row's next digit among keys matching its prefix.  FULL skips the
-// causal bound check.
-template <bool FAST, bool FULL, bool PACKED>
+// Histogram update of one 32-column chunk.  FAST: clamped 12-bit first digit
+// (taken from the arithmetic shift of the raw bits: negative scores land in
+// bin 0); else the row's next digit among keys matching its prefix, with keys
+// from float_key (PLAIN) or fast_key.  FULL skips the causal bound check.
+template <bool FAST, bool PLAIN, bool FULL, bool PACKED>
 __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol, int jb,
                                            int nvalid, const RowSel &s) {
+    // u >> shift as a high multiply (no variable-amount shift in the loop)
     const int w = min(8, s.top);
     const int shift = s.top - w;
+    const uint32_t mul = shift ? (1u << (32 - shift)) : 0u;
     const uint32_t dmask = (1u << w) - 1u;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const uint32_t u = float_key(v[i]);
         const bool ok = FULL || jb + i < nvalid;
         uint32_t d;
         bool in;
         if (FAST) {
-            d = (uint32_t)min(max((int)(u >> 20) - kFastBase, 0), 255);
+            d = (uint32_t)min(max((__float_as_int(v[i]) >> 20) - (kFastBase - 0x800), 0), 255);
             in = ok;
         } else {
-            d = (u >> shift) & dmask;
+            const uint32_t u = PLAIN ? float_key(v[i]) : fast_key(v[i]);
+            d = (shift ? __umulhi(u, mul) : u) & dmask;
             in = ok && (u & s.mask) == s.prefix;
         }
-        if (PACKED) red_shared_if(hcol + (d >> 1) * kRows, 1u << ((d & 1u) << 4), in);
+        if (PACKED) red_shared_if(hcol + (d >> 1) * kRows, (d & 1u) * 0xffffu + 1u, in);
         else red_shared_if(hcol + d * kRows, 1u, in);
     }
 }
@@ -317,13 +327,13 @@ __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol,
 // Collect of one 32-column chunk: selected column indices go, branch-free,
 // into this row's 32-slot ring in shared memory (ring[slot * kRows + row]),
 // which the caller then flushes in order to the output row.
-template <bool FULL>
+template <bool PLAIN, bool FULL>
 __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ring, int jb,
                                               int nvalid, const RowSel &s, int &pos,
                                               int &taken) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const uint32_t m = float_key(v[i]) & s.mask;
+        const uint32_t m = (PLAIN ? float_key(v[i]) : fast_key(v[i])) & s.mask;
         const bool ok = FULL || jb + i < nvalid;
         const bool eq = ok && m == s.prefix && taken < s.need;
         const bool sel = eq || (ok && m > s.prefix);
@@ -366,7 +376,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
     int32_t *out_row = (epi && t < T) ? idx + ((size_t)bh * T + t) * K : nullptr;
-    RowSel s{0u, 0u, K, 32, true};
+    RowSel s{0u, 0u, K, 32, true, false};
     if (epi && nvalid > K) s.done = false;
     if (epi && half == 0 && out_row && nvalid <= K)
         for (int i = 0; i < K; ++i) out_row[i] = (i < nvalid) ? i : -1;
@@ -466,11 +476,14 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const int jb = kt * C::kN + c * 32;
                         if (!active || jb >= nvalid) continue;
                         if (pass == 0) {
-                            if (full_tile) hist_chunk<true, true, PACKED>(v, hcol, jb, nvalid, s);
-                            else hist_chunk<true, false, PACKED>(v, hcol, jb, nvalid, s);
+                            if (full_tile) hist_chunk<true, false, true, PACKED>(v, hcol, jb, nvalid, s);
+                            else hist_chunk<true, false, false, PACKED>(v, hcol, jb, nvalid, s);
+                        } else if (!s.plain) {
+                            if (full_tile) hist_chunk<false, false, true, PACKED>(v, hcol, jb, nvalid, s);
+                            else hist_chunk<false, false, false, PACKED>(v, hcol, jb, nvalid, s);
                         } else {
-                            if (full_tile) hist_chunk<false, true, PACKED>(v, hcol, jb, nvalid, s);
-                            else hist_chunk<false, false, PACKED>(v, hcol, jb, nvalid, s);
+                            if (full_tile) hist_chunk<false, true, true, PACKED>(v, hcol, jb, nvalid, s);
+                            else hist_chunk<false, true, false, PACKED>(v, hcol, jb, nvalid, s);
                         }
                     }
                 } else if (half == 0) {
@@ -480,8 +493,13 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         tmem_ld32(taddr + c * 32, v);
                         const int jb = kt * C::kN + c * 32;
                         if (!collect || jb >= nvalid) continue;
-                        if (full_tile) collect_chunk<true>(v, ring, jb, nvalid, s, pos, taken);
-                        else collect_chunk<false>(v, ring, jb, nvalid, s, pos, taken);
+                        if (!s.plain) {
+                            if (full_tile) collect_chunk<false, true>(v, ring, jb, nvalid, s, pos, taken);
+                            else collect_chunk<false, false>(v, ring, jb, nvalid, s, pos, taken);
+                        } else {
+                            if (full_tile) collect_chunk<true, true>(v, ring, jb, nvalid, s, pos, taken);
+                            else collect_chunk<true, false>(v, ring, jb, nvalid, s, pos, taken);
+                        }
                         for (; flushed < pos; ++flushed)
                             if (flushed < K) out_row[flushed] = (int32_t)ring[(flushed & 31) * kRows];
                     }
