@@ -80,6 +80,24 @@ int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta
                    int flags, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * Same as sgsa_chunk_fwd, but for callers that cannot allocate device memory
+ * when they run (a fixed memory plan, a locked allocator, a plugin that only
+ * receives its inputs and outputs).  No reference counterpart: the
+ * reference's op allocates its temporaries through torch.  The workspace is a
+ * 64 MiB scratch array built into the library and held on every GPU that
+ * loads it; a problem whose sgsa_chunk_fwd_workspace_size exceeds 64 MiB is
+ * rejected with SGSA_ERR_WORKSPACE.  The first call on each device looks up
+ * the array's device address, so make it before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  The call allocates and frees nothing.
+ */
+int sgsa_chunk_fwd_noalloc(const void *q, const void *k, const void *v, const void *beta,
+                           const void *gamma, const void *sparse_k, const void *sparse_v,
+                           const void *alpha, const float *initial_state, void *o,
+                           float *final_state, int B, int T, int H, int D, int dtype,
+                           int chunk_size, int flags, void *stream);
+
+/*
  * Causal per-head top-k indexer: s_tj = iq_t . ik_j for j <= t; row t keeps the
  * min(top_k, t+1) largest, ties to the lowest j, written ascending and padded
  * with -1.  Replaces the selection of TopKSparseKVReuseAttention.forward
