@@ -157,7 +157,7 @@ def cpu_reference(cfg, cores: int, budget_s: float = 20.0):
     t0 = time.perf_counter()
     oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], heads=(0, hs))
     t_delta = (time.perf_counter() - t0) / hs * cores  # core-seconds per (b,h)
-    nq = 64
+    nq = 512
     mid = cfg.T // 2
     tr = (mid - nq // 2, mid + nq // 2)
     t0 = time.perf_counter()
