@@ -22,7 +22,11 @@
 // to the workspace; kernel 2 (chunk_scan) walks the chunks of one (b, h) in
 // order, one CTA per 32-column slice of the state, the slice held in shared
 // memory in fp32.
+#include <stdlib.h>
+
 #include "common.cuh"
+#include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace sgsa {
 namespace {
@@ -38,6 +42,7 @@ struct ChunkArgs {
     float *sT;
     int B, T, H, NC;
     float *W, *U, *Aqk, *G;
+    float *Qt, *KtT;  // tensor-core scan only: exp(G_t) q_t [C x D] and Kap~^T [D x C]
 };
 
 template <int D, bool SPARSE>
@@ -103,6 +108,19 @@ __global__ void __launch_bounds__(kThreads) chunk_prep_kernel(ChunkArgs a) {
     }
     __syncthreads();
 
+    if (!SPARSE && a.Qt) {  // operands of the tensor-core scan, in fp32
+        const size_t cix = (size_t)bh * a.NC + c;
+        float *qt = a.Qt + cix * kC * D, *kt = a.KtT + cix * D * kC;
+        const float gl = sG[kC - 1];
+        for (int e = tid; e < kC * D; e += kThreads) {
+            const int t = e / D, d = e % D;
+            qt[e] = __expf(sG[t]) * VU[t * LD + d];
+        }
+        for (int e = tid; e < kC * D; e += kThreads) {
+            const int d = e / kC, m = e % kC;
+            kt[e] = __expf(gl - sG[m]) * KW[m * LD + d];
+        }
+    }
     const int ti = tid & 15, tj = tid >> 4;
     {   // A = strictly-earlier-token transition
         constexpr int R = M / 16;
@@ -300,6 +318,247 @@ cudaError_t run(const ChunkArgs &a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// ---- tensor-core scan (bf16 inputs, D = 128, no sparse write) ---------------
+//
+// One CTA per (b, h); the 128x128 fp32 state is kept transposed (S^T[v][dk]) in
+// shared memory as a K-major, 128-byte-swizzled tf32 operand, and every
+// contraction of a chunk runs as tcgen05.mma.kind::tf32 with M = 128 (state
+// rows), fp32 accumulation in TMEM:
+//   D1 = S^T W^T            (U^T = Uh^T - D1)       [v x tok]
+//   D2 = S^T Qt^T + U^T Aqk^T                        [v x t]   -> o^T
+//   D3 = U^T Kt             (S^T <- e^{G_last} S^T + D3)  [v x dk]
+// W, Qt, Aqk and Kt^T come from the prep kernel's workspace through TMA.
+// Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; warps 2-5: one
+// thread per state row v (TMEM lane), the two epilogues.
+static __device__ unsigned int g_scan_watchdog;
+
+namespace tc {
+constexpr int kD = 128;
+constexpr int kSt = 0;                       // S^T  [128 v][128 dk]   64 KB
+constexpr int kW = kSt + 65536;              // W    [64 tok][128 dk]  32 KB
+constexpr int kQ = kW + 32768;               // Qt   [64 t][128 dk]    32 KB
+constexpr int kA = kQ + 32768;               // Aqk  [64 t][64 tok]    16 KB
+constexpr int kK = kA + 16384;               // Kt^T [128 dk][64 tok]  32 KB
+constexpr int kU = kK + 32768;               // U^T  [128 v][64 tok]   32 KB
+constexpr int kBar = kU + 32768;
+constexpr int kBytes = kBar + 64;
+constexpr size_t kSmem = 1024 + kBytes;
+constexpr uint32_t kOpBytes = 32768 * 3 + 16384;
+}  // namespace tc
+
+// Byte offset of fp32 element (r, k) in a K-major 128-byte-swizzled operand of
+// `rows` rows (32 k per 128-byte row, blocks of 32 k stacked).
+__device__ __forceinline__ uint32_t sw128_f32(int rows, int r, int k) {
+    return (uint32_t)((k >> 5) * rows * 128 + r * 128 + ((((k & 31) >> 2) ^ (r & 7)) << 4) +
+                      ((k & 3) << 2));
+}
+
+template <typename Tout>
+__global__ void __launch_bounds__(192, 1)
+chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
+                     const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_a,
+                     const __grid_constant__ CUtensorMap tm_k) {
+    using namespace sm100;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(sm + tc::kBar);
+    uint64_t *opfull = bars + 0, *d1done = bars + 1, *utready = bars + 2, *d23done = bars + 3,
+             *stready = bars + 4;
+    __shared__ uint32_t s_tmem;
+    unsigned int *wd = &g_scan_watchdog;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+    const int NC = a.NC;
+
+    if (threadIdx.x == 0) {
+        mbar_init(opfull, 1);
+        mbar_init(d1done, 1);
+        mbar_init(utready, 4);
+        mbar_init(d23done, 1);
+        mbar_init(stready, 4);
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(&s_tmem, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int c = 0; c < NC; ++c) {
+                if (c > 0) mbar_wait(d23done, (c - 1) & 1, wd, 1u);
+                const int cix = bh * NC + c;
+                mbar_arrive_expect_tx(opfull, tc::kOpBytes);
+                for (int kb = 0; kb < 4; ++kb) {
+                    tma_load_2d(sm + tc::kW + kb * 8192, &tm_w, opfull, kb * 32, cix * 64);
+                    tma_load_2d(sm + tc::kQ + kb * 8192, &tm_q, opfull, kb * 32, cix * 64);
+                }
+                for (int kb = 0; kb < 2; ++kb) {
+                    tma_load_2d(sm + tc::kA + kb * 8192, &tm_a, opfull, kb * 32, cix * 64);
+                    tma_load_2d(sm + tc::kK + kb * 16384, &tm_k, opfull, kb * 32, cix * 128);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t st = smem_u32(sm + tc::kSt), wq = smem_u32(sm + tc::kW),
+                           qq = smem_u32(sm + tc::kQ), aq = smem_u32(sm + tc::kA),
+                           kq = smem_u32(sm + tc::kK), uq = smem_u32(sm + tc::kU);
+            constexpr uint32_t id64 = idesc_tf32_f32(128, 64), id128 = idesc_tf32_f32(128, 128);
+            const uint32_t tD1 = tmem, tD2 = tmem + 64, tD3 = tmem + 128;
+            for (int c = 0; c < NC; ++c) {
+                const uint32_t ph = c & 1;
+                mbar_wait(stready, ph, wd, 2u);
+                mbar_wait(opfull, ph, wd, 4u);
+                tc_fence_after();
+                // D1 = S^T W^T, D2 = S^T Qt^T   (K = dk = 128: 4 blocks x 4 steps)
+                for (int kb = 0; kb < 4; ++kb)
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t ad = sdesc_kmajor_sw128(st + kb * 16384 + kk * 32);
+                        const uint32_t acc = (kb | kk) ? 1u : 0u;
+                        mma_tf32(tD1, ad, sdesc_kmajor_sw128(wq + kb * 8192 + kk * 32), id64, acc);
+                        mma_tf32(tD2, ad, sdesc_kmajor_sw128(qq + kb * 8192 + kk * 32), id64, acc);
+                    }
+                mma_commit(d1done);
+                mbar_wait(utready, ph, wd, 8u);
+                tc_fence_after();
+                // D2 += U^T Aqk^T, D3 = U^T Kt   (K = tok = 64: 2 blocks x 4 steps)
+                for (int kb = 0; kb < 2; ++kb)
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t ad = sdesc_kmajor_sw128(uq + kb * 16384 + kk * 32);
+                        mma_tf32(tD2, ad, sdesc_kmajor_sw128(aq + kb * 8192 + kk * 32), id64, 1u);
+                        mma_tf32(tD3, ad, sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32), id128,
+                                 (kb | kk) ? 1u : 0u);
+                    }
+                mma_commit(d23done);
+            }
+        }
+        __syncwarp();
+    } else {
+        const int quad = warp & 3, v = quad * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+        float *ST = (float *)(sm + tc::kSt);
+        unsigned char *UT = sm + tc::kU;
+        // initial state, transposed: S^T[v][dk] = S0[dk][v]
+        for (int k4 = 0; k4 < tc::kD; k4 += 4) {
+            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (a.s0) {
+                const float *s0 = a.s0 + (size_t)bh * tc::kD * tc::kD + v;
+                x = make_float4(s0[(k4 + 0) * tc::kD], s0[(k4 + 1) * tc::kD],
+                                s0[(k4 + 2) * tc::kD], s0[(k4 + 3) * tc::kD]);
+            }
+            *(float4 *)((unsigned char *)ST + sw128_f32(128, v, k4)) = x;
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(stready);
+        Tout *o = (Tout *)a.o;
+        for (int c = 0; c < NC; ++c) {
+            const uint32_t ph = c & 1;
+            const int t0 = c * kC, L = min(kC, a.T - t0);
+            const size_t cix = (size_t)bh * NC + c;
+            // ---- E1: U^T = Uh^T - S^T W^T
+            const float *Uh = a.U + cix * kC * tc::kD + v;
+            float uh[kC];
+#pragma unroll
+            for (int t = 0; t < kC; ++t) uh[t] = Uh[t * tc::kD];
+            mbar_wait(d1done, ph, wd, 16u);
+            tc_fence_after();
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float d[32];
+                tmem_ld32(trow + half * 32, d);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    const int t = half * 32 + j;
+                    *(float4 *)(UT + sw128_f32(128, v, t)) =
+                        make_float4(uh[t] - d[j], uh[t + 1] - d[j + 1], uh[t + 2] - d[j + 2],
+                                    uh[t + 3] - d[j + 3]);
+                }
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(utready);
+            // ---- E2: o^T = D2, S^T = e^{G_last} S^T + D3
+            const float gl = __expf(a.G[cix * kC + kC - 1]);
+            mbar_wait(d23done, ph, wd, 32u);
+            tc_fence_after();
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float d[32];
+                tmem_ld32(trow + 64 + half * 32, d);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = half * 32 + j;
+                    if (t < L) o[(((size_t)b * a.T + t0 + t) * a.H + h) * tc::kD + v] = from_f32<Tout>(d[j]);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float d[32];
+                tmem_ld32(trow + 128 + q * 32, d);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float4 *p = (float4 *)((unsigned char *)ST + sw128_f32(128, v, q * 32 + j));
+                    float4 x = *p;
+                    x.x = fmaf(gl, x.x, d[j]);
+                    x.y = fmaf(gl, x.y, d[j + 1]);
+                    x.z = fmaf(gl, x.z, d[j + 2]);
+                    x.w = fmaf(gl, x.w, d[j + 3]);
+                    *p = x;
+                }
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(stready);
+        }
+        if (a.sT) {
+            float *sT = a.sT + (size_t)bh * tc::kD * tc::kD + v;
+            for (int k = 0; k < tc::kD; ++k)
+                sT[(size_t)k * tc::kD] = *(float *)((unsigned char *)ST + sw128_f32(128, v, k));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+static bool scan_use_tc() {
+    const char *e = getenv("SGSA_SCAN_SIMT");
+    return !(e && e[0] == '1');
+}
+
+template <typename Tout>
+cudaError_t run_tc_scan(const ChunkArgs &a, cudaStream_t st) {
+    using Dm = Dims<128, false>;
+    auto prep = chunk_prep_kernel<__nv_bfloat16, 128, false>;
+    cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Dm::prep_smem);
+    if (e != cudaSuccess) return e;
+    const long long nch = (long long)a.B * a.H * a.NC;
+    CUtensorMap mw, mq, ma, mk;
+    if (!make_tmap_2d_f32(&mw, a.W, 128, nch * 64, 64) ||
+        !make_tmap_2d_f32(&mq, a.Qt, 128, nch * 64, 64) ||
+        !make_tmap_2d_f32(&ma, a.Aqk, 64, nch * 64, 64) ||
+        !make_tmap_2d_f32(&mk, a.KtT, 64, nch * 128, 128))
+        return cudaErrorInvalidValue;
+    auto scan = chunk_scan_tc_kernel<Tout>;
+    e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmem);
+    if (e != cudaSuccess) return e;
+    prep<<<dim3(a.NC, a.B * a.H), kThreads, Dm::prep_smem, st>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    scan<<<a.B * a.H, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
+    return cudaGetLastError();
+}
+
 template <typename Tin, typename Tout, bool SPARSE>
 cudaError_t run_d(int D, const ChunkArgs &a, cudaStream_t st) {
     switch (D) {
@@ -315,8 +574,13 @@ cudaError_t run_d(int D, const ChunkArgs &a, cudaStream_t st) {
 size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags) {
     const int M = (flags & SGSA_FLAG_HAS_SPARSE) ? 2 * kC : kC;
     const size_t NC = (size_t)ceil_div(T, kC);
-    const size_t per = (size_t)2 * M * D + (size_t)kC * M + kC;
-    return (size_t)B * H * NC * per * sizeof(float);
+    size_t per = (size_t)2 * M * D + (size_t)kC * M + kC;
+    size_t extra = 0;
+    if (D == 128 && M == kC) {  // Qt and Kt^T of the tensor-core scan (+ alignment pad)
+        per += (size_t)2 * kC * D;
+        extra = 256;
+    }
+    return (size_t)B * H * NC * per * sizeof(float) + extra;
 }
 
 cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, const void *beta,
@@ -338,6 +602,21 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
     a.U = a.W + nchunk * M * D;
     a.Aqk = a.U + nchunk * M * D;
     a.G = a.Aqk + nchunk * kC * M;
+    a.Qt = nullptr;
+    a.KtT = nullptr;
+    if (D == 128 && !sparse) {
+        float *tail = a.G + nchunk * kC;
+        // keep the fp32 operand arrays 16-byte aligned for TMA
+        tail = (float *)(((uintptr_t)tail + 255) & ~(uintptr_t)255);
+        a.Qt = tail;
+        a.KtT = a.Qt + nchunk * kC * D;
+    }
+    if (dtype == SGSA_DTYPE_BF16 && D == 128 && !sparse && scan_use_tc()) {
+        const bool of32b = (flags & SGSA_FLAG_OUT_F32);
+        return of32b ? run_tc_scan<float>(a, st) : run_tc_scan<__nv_bfloat16>(a, st);
+    }
+    a.Qt = nullptr;
+    a.KtT = nullptr;
     const bool of32 = (flags & SGSA_FLAG_OUT_F32) || dtype == SGSA_DTYPE_F32;
     if (dtype == SGSA_DTYPE_F32) {
         return sparse ? run_d<float, float, true>(D, a, st) : run_d<float, float, false>(D, a, st);

@@ -38,4 +38,19 @@ bool make_tmap_rows_bf16(CUtensorMap *map, const void *base, int B, int T, int H
     return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_2d_f32(CUtensorMap *map, const void *base, int inner, long long rows,
+                      int box_rows) {
+    auto fn = encode_fn();
+    if (!fn || ((uintptr_t)base & 15)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)inner * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace sgsa

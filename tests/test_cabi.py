@@ -36,7 +36,7 @@ def test_host_only_entry_points(lib):
     assert lib.sgsa_status_string(0) == b"ok"
     assert b"shape" in lib.sgsa_status_string(-1)
     n = lib.sgsa_chunk_fwd_workspace_size(4, 8192, 16, 128, 0)
-    assert n == 4 * 16 * 128 * (2 * 64 * 128 + 64 * 64 + 64) * 4
+    assert n == 4 * 16 * 128 * (4 * 64 * 128 + 64 * 64 + 64) * 4 + 256
     assert lib.sgsa_chunk_fwd_workspace_size(1, 64, 1, 96, 0) == 0  # unsupported head dim
     assert lib.sgsa_layer_fwd_workspace_size(1, 1024, 4, 64, 32, 128) > 0
 
