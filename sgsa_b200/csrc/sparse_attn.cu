@@ -8,7 +8,7 @@
 //
 // One warp per (b, h, t).  Each half-warp gathers one selected row per step
 // with 16-byte vector loads (a 128-wide bf16 row is 16 lanes x 16 B), so one
-// warp keeps 2 x kUnroll rows in flight; the score is reduced over the
+// warp keeps up to 16 k rows and 16 v rows in flight; the score is reduced over the
 // half-warp with shuffles, and each half keeps its own online-softmax state
 // (running max, sum, accumulator) that the two halves merge at the end.
 #include "common.cuh"
@@ -17,7 +17,6 @@ namespace sgsa {
 namespace {
 
 constexpr int kWarps = 8;
-constexpr int kUnroll = 4;
 
 template <typename T, int N>
 struct VecLoad;
@@ -67,12 +66,48 @@ struct VecLoad<float, N> {  // N floats (N in {2,4,8})
     }
 };
 
+// A row segment of one lane kept packed (as loaded) until it is used.
+template <typename T, int EPL>
+struct RawSeg {
+    static constexpr int W = EPL * (int)sizeof(T) / 4;  // 32-bit words
+    uint32_t w[W];
+    __device__ __forceinline__ void load(const T *p) {
+        if constexpr (W % 4 == 0) {
+#pragma unroll
+            for (int i = 0; i < W / 4; ++i) {
+                const uint4 r = __ldg(reinterpret_cast<const uint4 *>(p) + i);
+                w[4 * i] = r.x; w[4 * i + 1] = r.y; w[4 * i + 2] = r.z; w[4 * i + 3] = r.w;
+            }
+        } else if constexpr (W == 2) {
+            const uint2 r = __ldg(reinterpret_cast<const uint2 *>(p));
+            w[0] = r.x; w[1] = r.y;
+        } else {
+            w[0] = __ldg(reinterpret_cast<const unsigned int *>(p));
+        }
+    }
+    __device__ __forceinline__ void zero() {
+#pragma unroll
+        for (int i = 0; i < W; ++i) w[i] = 0u;
+    }
+    __device__ __forceinline__ float get(int e) const {
+        if constexpr (sizeof(T) == 4) {
+            return __uint_as_float(w[e]);
+        } else {
+            const uint32_t x = w[e >> 1];
+            return __uint_as_float((e & 1) ? (x & 0xffff0000u) : (x << 16));
+        }
+    }
+};
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
     const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
     const int32_t *__restrict__ idx, const float *__restrict__ od, const T *__restrict__ mix,
     T *__restrict__ out, int B, int T_, int H, int K, float scale_log2, int mix_pc) {
     constexpr int EPL = D / 16;
+    // rows per half-warp in flight: up to 8, bounded by ~64 registers of packed rows
+    constexpr int kWords = EPL * (int)sizeof(T) / 4;
+    constexpr int kU = (32 / kWords) < 8 ? (32 / kWords < 2 ? 2 : 32 / kWords) : 8;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int half = lane >> 4, hl = lane & 15;
     const long long qi = (long long)blockIdx.x * kWarps + warp;  // over [B*H*T]
@@ -99,52 +134,47 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
     for (int base = 0; base < nsel; base += 32) {
         const int cnt = min(32, nsel - base);
         const int my = (lane < cnt) ? __ldg(ix + base + lane) : 0;
-        for (int p = 0; p < cnt; p += 2 * kUnroll) {
-            float kr[kUnroll][EPL], s[kUnroll];
-            int jr[kUnroll];
+        for (int p = 0; p < cnt; p += 2 * kU) {
+            // issue every k and v row load of the group before any use
+            RawSeg<T, EPL> kr[kU], vr[kU];
+            int jr[kU];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
+            for (int u = 0; u < kU; ++u) {
                 const int slot = p + 2 * u + half;
                 jr[u] = __shfl_sync(0xffffffffu, my, slot & 31);
                 if (slot >= cnt) jr[u] = -1;
-                if (jr[u] >= 0) VecLoad<T, EPL>::load(kb + (size_t)jr[u] * kvstride, kr[u]);
-                else {
-#pragma unroll
-                    for (int e = 0; e < EPL; ++e) kr[u][e] = 0.f;
+                if (jr[u] >= 0) {
+                    kr[u].load(kb + (size_t)jr[u] * kvstride);
+                    vr[u].load(vb + (size_t)jr[u] * kvstride);
+                } else {
+                    kr[u].zero();
+                    vr[u].zero();
                 }
             }
+            float s[kU];
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
+            for (int u = 0; u < kU; ++u) {
                 float d0 = 0.f;
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) d0 = fmaf(qv[e], kr[u][e], d0);
+                for (int e = 0; e < EPL; ++e) d0 = fmaf(qv[e], kr[u].get(e), d0);
 #pragma unroll
                 for (int off = 8; off > 0; off >>= 1) d0 += __shfl_xor_sync(0xffffffffu, d0, off);
                 s[u] = (jr[u] >= 0) ? d0 : -INFINITY;
             }
-            float vr[kUnroll][EPL];
-#pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                if (jr[u] >= 0) VecLoad<T, EPL>::load(vb + (size_t)jr[u] * kvstride, vr[u]);
-                else {
-#pragma unroll
-                    for (int e = 0; e < EPL; ++e) vr[u][e] = 0.f;
-                }
-            }
             float mn = m;
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) mn = fmaxf(mn, s[u]);
+            for (int u = 0; u < kU; ++u) mn = fmaxf(mn, s[u]);
             if (mn != -INFINITY) {
                 const float corr = exp2f(m - mn);  // m == -inf gives 0
                 l *= corr;
 #pragma unroll
                 for (int e = 0; e < EPL; ++e) acc[e] *= corr;
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
+                for (int u = 0; u < kU; ++u) {
                     const float pu = exp2f(s[u] - mn);
                     l += pu;
 #pragma unroll
-                    for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pu, vr[u][e], acc[e]);
+                    for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pu, vr[u].get(e), acc[e]);
                 }
                 m = mn;
             }
