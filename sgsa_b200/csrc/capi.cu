@@ -1,6 +1,7 @@
 // extern "C" boundary of libsgsa_b200.so: argument checks, workspace carving,
 // status codes.  No entry point allocates, frees, aborts or traps.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -28,6 +29,12 @@ bool head_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
 bool dtype_ok(int dt) { return dt == SGSA_DTYPE_F32 || dt == SGSA_DTYPE_BF16; }
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// SGSA_ATTN_GATHER=1 makes the layer use the row-gather attention (A/B checks).
+bool fused_attn_enabled() {
+    const char *e = getenv("SGSA_ATTN_GATHER");
+    return !(e && e[0] == '1');
+}
+
 }  // namespace
 
 extern "C" {
@@ -51,7 +58,11 @@ const char *sgsa_last_error(void) { return g_last_error; }
 int sgsa_version(void) { return 1000; }
 
 int sgsa_watchdog_status(void *stream) {
-    return (int)sgsa::read_index_watchdog((cudaStream_t)stream);
+    const cudaStream_t st = (cudaStream_t)stream;
+    const unsigned int a = sgsa::read_index_watchdog(st), b = sgsa::read_scan_watchdog(st),
+                       c = sgsa::read_attn_watchdog(st);
+    if (a == 0xffffffffu || b == 0xffffffffu || c == 0xffffffffu) return -1;
+    return (int)(a | (b << 8) | (c << 16));
 }
 
 size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags) {
@@ -137,6 +148,7 @@ size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top
     size_t n = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
     n += align256((size_t)B * T * H * D * sizeof(float));       // o_delta
     n += align256((size_t)B * H * T * top_k * sizeof(int32_t));  // indices
+    n += align256((size_t)B * H * T * 16);                       // per-row selection thresholds
     return n;
 }
 
@@ -157,6 +169,9 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     const size_t cws = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
     float *od = (float *)(w + cws);
     int32_t *ix = (int32_t *)(w + cws + align256((size_t)B * T * H * D * sizeof(float)));
+    uint32_t *thr = (uint32_t *)((char *)ix + align256((size_t)B * H * T * top_k * sizeof(int32_t)));
+    const bool fused = sgsa::indexer_tc_eligible(DI, dtype) &&
+                       sgsa::sparse_attn_tc_eligible(T, D, DI, dtype) && fused_attn_enabled();
     if (indices) ix = indices;
     int flags = SGSA_FLAG_OUT_F32 | (initial_state ? SGSA_FLAG_HAS_INIT : 0) |
                 (final_state ? SGSA_FLAG_STORE_FINAL : 0);
@@ -164,9 +179,17 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
                                              initial_state, od, final_state, B, T, H, D, dtype,
                                              flags, w, st);
     if (e != cudaSuccess) return fail_cuda(e);
+    const float scale = 1.0f / sqrtf((float)D);
+    if (fused) {
+        // selection exported as per-row thresholds; indices written only if asked for
+        e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, H, DI, top_k, st);
+        if (e != cudaSuccess) return fail_cuda(e);
+        e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
+                                        mix_per_channel, st);
+        return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+    }
     e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, H, DI, top_k, dtype, st);
     if (e != cudaSuccess) return fail_cuda(e);
-    const float scale = 1.0f / sqrtf((float)D);
     e = sgsa::launch_sparse_attn_mix(q, k, v, ix, od, mix, out, B, T, H, D, top_k, scale,
                                      mix_per_channel, dtype, st);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);

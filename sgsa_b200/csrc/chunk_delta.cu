@@ -571,6 +571,14 @@ cudaError_t run_d(int D, const ChunkArgs &a, cudaStream_t st) {
 
 }  // namespace
 
+unsigned int read_scan_watchdog(cudaStream_t st) {
+    unsigned int v = 0, z = 0;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_scan_watchdog, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (v) cudaMemcpyToSymbol(g_scan_watchdog, &z, sizeof(z));
+    return v;
+}
+
 size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags) {
     const int M = (flags & SGSA_FLAG_HAS_SPARSE) ? 2 * kC : kC;
     const size_t NC = (size_t)ceil_div(T, kC);

@@ -31,6 +31,13 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
+bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype);
+cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
+                                  const void *ik, const uint32_t *thr, const float *od,
+                                  const void *mix, void *out, int B, int T, int H, float scale,
+                                  int mix_pc, cudaStream_t st);
+unsigned int read_attn_watchdog(cudaStream_t st);
+unsigned int read_scan_watchdog(cudaStream_t st);
 }  // namespace sgsa
 
 // Launch wrappers implemented in the .cu files (all return cudaError_t of the launch).
@@ -45,10 +52,23 @@ size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags);
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T,
                                 int H, int DI, int K, int dtype, cudaStream_t st);
 unsigned int read_index_watchdog(cudaStream_t st);
+// Tensor-core indexer that also writes, per query row, the exact selection as a
+// threshold {prefix, mask, cut, 1}: column j <= t is selected iff
+// (key(s_tj) & mask) > prefix, or == prefix and j <= cut.  idx may be NULL.
+bool indexer_tc_eligible(int DI, int dtype);
+cudaError_t launch_indexer_topk_thr(const void *iq, const void *ik, int32_t *idx, uint32_t *thr,
+                                    int B, int T, int H, int DI, int K, cudaStream_t st);
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,
                                int S, int K, cudaStream_t st);
 cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
                                    const int32_t *idx, const float *od, const void *mix,
                                    void *out, int B, int T, int H, int D, int K, float scale,
                                    int mix_pc, int dtype, cudaStream_t st);
+bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype);
+cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
+                                  const void *ik, const uint32_t *thr, const float *od,
+                                  const void *mix, void *out, int B, int T, int H, float scale,
+                                  int mix_pc, cudaStream_t st);
+unsigned int read_attn_watchdog(cudaStream_t st);
+unsigned int read_scan_watchdog(cudaStream_t st);
 }  // namespace sgsa

@@ -330,7 +330,7 @@ __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol,
 template <bool PLAIN, bool FULL>
 __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ring, int jb,
                                               int nvalid, const RowSel &s, int &pos,
-                                              int &taken) {
+                                              int &taken, int &lastj) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
         const uint32_t m = (PLAIN ? float_key(v[i]) : fast_key(v[i])) & s.mask;
@@ -340,14 +340,15 @@ __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ri
         ring[(pos & 31) * kRows] = (uint32_t)(jb + i);
         pos += sel;
         taken += eq;
+        lastj = eq ? jb + i : lastj;
     }
 }
 
 template <int DI, bool PACKED>
 __global__ void __launch_bounds__(TcCfg<DI, PACKED>::kThreads, (TcCfg<DI, PACKED>::kMinBlocks))
 indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
-                       const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx, int B,
-                       int T, int H, int K, int nqt) {
+                       const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx,
+                       uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt) {
     using C = TcCfg<DI, PACKED>;
     using namespace sm100;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -375,11 +376,16 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int row = quad * 32 + lane;
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
-    int32_t *out_row = (epi && t < T) ? idx + ((size_t)bh * T + t) * K : nullptr;
+    const bool has_row = epi && t < T;
+    int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
+    uint4 *thr_row = (has_row && thr) ? thr + (size_t)bh * T + t : nullptr;
     RowSel s{0u, 0u, K, 32, true, false};
     if (epi && nvalid > K) s.done = false;
-    if (epi && half == 0 && out_row && nvalid <= K)
-        for (int i = 0; i < K; ++i) out_row[i] = (i < nvalid) ? i : -1;
+    if (epi && half == 0 && has_row && nvalid <= K) {
+        if (out_row)
+            for (int i = 0; i < K; ++i) out_row[i] = (i < nvalid) ? i : -1;
+        if (thr_row) *thr_row = make_uint4(0u, 0u, 0x7fffffffu, 1u);  // every column j <= t
+    }
     if (q_last + 1 <= K) return;  // every row of the tile keeps all its columns
 
     if (warp == 0 && lane == 0) {
@@ -454,14 +460,14 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         } else {
             const bool active = !s.done;
             uint32_t *hcol = hist + row;
-            const bool collect = collecting && half == 0 && out_row && nvalid > K;
+            const bool collect = collecting && half == 0 && has_row && nvalid > K;
             if (!collecting) {
                 if (half == 0 && active)
                     for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
                 epi_bar();
             }
             uint32_t *ring = hist + row;  // the histogram is idle during the collect pass
-            int pos = 0, taken = 0, flushed = 0;
+            int pos = 0, taken = 0, flushed = 0, lastj = -1;
             for (int kt = 0; kt < nkt; ++kt, ++it_e) {
                 const uint32_t buf = it_e % C::kAcc, bph = (it_e / C::kAcc) & 1;
                 mbar_wait(&tfull[buf], bph, wd, 16u);
@@ -494,14 +500,16 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const int jb = kt * C::kN + c * 32;
                         if (!collect || jb >= nvalid) continue;
                         if (!s.plain) {
-                            if (full_tile) collect_chunk<false, true>(v, ring, jb, nvalid, s, pos, taken);
-                            else collect_chunk<false, false>(v, ring, jb, nvalid, s, pos, taken);
+                            if (full_tile) collect_chunk<false, true>(v, ring, jb, nvalid, s, pos, taken, lastj);
+                            else collect_chunk<false, false>(v, ring, jb, nvalid, s, pos, taken, lastj);
                         } else {
-                            if (full_tile) collect_chunk<true, true>(v, ring, jb, nvalid, s, pos, taken);
-                            else collect_chunk<true, false>(v, ring, jb, nvalid, s, pos, taken);
+                            if (full_tile) collect_chunk<true, true>(v, ring, jb, nvalid, s, pos, taken, lastj);
+                            else collect_chunk<true, false>(v, ring, jb, nvalid, s, pos, taken, lastj);
                         }
-                        for (; flushed < pos; ++flushed)
-                            if (flushed < K) out_row[flushed] = (int32_t)ring[(flushed & 31) * kRows];
+                        if (out_row) {
+                            for (; flushed < pos; ++flushed)
+                                if (flushed < K) out_row[flushed] = (int32_t)ring[(flushed & 31) * kRows];
+                        }
                     }
                 }
                 tc_fence_before();
@@ -515,7 +523,10 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     else row_choose<PACKED, false>(s, hist, row, K);
                 }
             } else if (collect) {
-                for (int i = flushed; i < K; ++i) out_row[i] = -1;
+                if (out_row)
+                    for (int i = min(pos, K); i < K; ++i) out_row[i] = -1;
+                // the exact selection as a threshold: key & mask > prefix, or equal and j <= cut
+                if (thr_row) *thr_row = make_uint4(s.prefix, s.mask, (uint32_t)lastj, 1u);
             }
         }
         const int more = __syncthreads_or(epi && !s.done);
@@ -529,8 +540,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 }
 
 template <int DI, bool PACKED>
-cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, int B, int T, int H, int K,
-                   cudaStream_t st) {
+cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T, int H,
+                   int K, cudaStream_t st) {
     using C = TcCfg<DI, PACKED>;
     CUtensorMap mq, mk;
     if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
@@ -541,16 +552,16 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, int B, int T, i
                                          (int)C::kSmem);
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRows);
-    kern<<<nqt * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, B, T, H, K, nqt);
+    kern<<<nqt * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, thr, B, T, H, K, nqt);
     return cudaGetLastError();
 }
 
 template <int DI>
-cudaError_t run_tc_t(const void *iq, const void *ik, int32_t *idx, int B, int T, int H, int K,
-                     cudaStream_t st) {
+cudaError_t run_tc_t(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T,
+                     int H, int K, cudaStream_t st) {
     // 16-bit counters hold any count below 65536, the longest row they can see.
-    if (T < 65536) return run_tc<DI, true>(iq, ik, idx, B, T, H, K, st);
-    return run_tc<DI, false>(iq, ik, idx, B, T, H, K, st);
+    if (T < 65536) return run_tc<DI, true>(iq, ik, idx, thr, B, T, H, K, st);
+    return run_tc<DI, false>(iq, ik, idx, thr, B, T, H, K, st);
 }
 
 template <typename Tin, int DI>
@@ -579,12 +590,23 @@ cudaError_t run_simt_d(int DI, const void *iq, const void *ik, int32_t *idx, int
 
 }  // namespace
 
+bool indexer_tc_eligible(int DI, int dtype) {
+    return dtype == SGSA_DTYPE_BF16 && (DI == 64 || DI == 128) && indexer_use_tc();
+}
+
+cudaError_t launch_indexer_topk_thr(const void *iq, const void *ik, int32_t *idx, uint32_t *thr,
+                                    int B, int T, int H, int DI, int K, cudaStream_t st) {
+    if (DI == 64) return run_tc_t<64>(iq, ik, idx, (uint4 *)thr, B, T, H, K, st);
+    if (DI == 128) return run_tc_t<128>(iq, ik, idx, (uint4 *)thr, B, T, H, K, st);
+    return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T, int H,
                                 int DI, int K, int dtype, cudaStream_t st) {
     if (dtype == SGSA_DTYPE_F32) return run_simt_d<float>(DI, iq, ik, idx, B, T, H, K, st);
     if (indexer_use_tc()) {
-        if (DI == 64) return run_tc_t<64>(iq, ik, idx, B, T, H, K, st);
-        if (DI == 128) return run_tc_t<128>(iq, ik, idx, B, T, H, K, st);
+        if (DI == 64) return run_tc_t<64>(iq, ik, idx, nullptr, B, T, H, K, st);
+        if (DI == 128) return run_tc_t<128>(iq, ik, idx, nullptr, B, T, H, K, st);
     }
     return run_simt_d<__nv_bfloat16>(DI, iq, ik, idx, B, T, H, K, st);
 }

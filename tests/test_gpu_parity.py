@@ -266,3 +266,21 @@ def test_indexer_tc_score_ranges(kind):
     got = ops.indexer_topk(iq.cuda(), ik.cuda(), K).cpu().numpy()
     want, kth = oracle.indexer_topk(iq, ik, K, return_kth=True)
     check_index_sets(got, want, iq.float(), ik.float(), kth, 1e-5)
+
+
+@pytest.mark.parametrize("B,T,H,K", [(1, 1000, 2, 64), (2, 2048, 2, 512), (1, 4096, 1, 300)])
+def test_layer_fused_attention_matches_gather_and_oracle(B, T, H, K, monkeypatch):
+    """The tensor-core attention (selection applied as the indexer's exact
+    per-row threshold) against the row-gather path and the oracle."""
+    cfg = CONFIGS["b200_bf16"].scaled(name="fused", B=B, T=T, H=H, top_k=K)
+    x = make_inputs(cfg, seed=3)
+    d = dev(x)
+    args = (d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"], d["ik"], d["mix"], K)
+    fused, idx = ops.sgsa_layer_fwd(*args, return_indices=True)
+    monkeypatch.setenv("SGSA_ATTN_GATHER", "1")
+    gather, idx2 = ops.sgsa_layer_fwd(*args, return_indices=True)
+    assert torch.equal(idx, idx2)
+    assert oracle.rel_l2(fused.float().cpu().numpy(), gather.float().cpu().numpy()) < 2e-3
+    ro, _ = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"])
+    want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx.cpu().numpy(), ro, x["mix"])
+    assert oracle.rel_l2(fused.float().cpu().numpy(), want) < 2e-3
