@@ -59,8 +59,11 @@ def algorithmic_counts(cfg):
     sel = sum(min(K, t + 1) for t in range(T))
     f_sp = B * H * sel * 4 * D
     bytes_gather = B * H * sel * (2 * D) * 2
+    # tensor-core attention: indexer scores, QK^T and PV over every causal pair
+    f_attn_tc = B * H * (T * (T + 1) // 2) * 2 * (DI + 2 * D)
     bytes_io = B * T * H * (2 * 3 * D + 2 * 2 * DI + 2 * D + 2 * D + 2 * 2) + 2 * B * H * D * D * 4
-    return dict(f_delta=f_delta, f_idx=f_idx, f_sp=f_sp, bytes_gather=bytes_gather,
+    return dict(f_delta=f_delta, f_idx=f_idx, f_sp=f_sp, f_attn_tc=f_attn_tc,
+                bytes_gather=bytes_gather,
                 bytes_io=bytes_io, selected=B * H * sel)
 
 
@@ -234,10 +237,26 @@ def stage_times(cfg, d, reps=3, only=None):
                                             1.0 / math.sqrt(D), 1, _lib.DTYPE_BF16,
                                             st.cuda_stream), "attn")
 
+    thr = torch.empty(B, H, T, 4, device="cuda", dtype=torch.int32)
+
+    def index_thr():
+        _lib.check(lib.sgsa_indexer_thresholds(P(d["iq"]), P(d["ik"]), None, P(thr), B, T, H,
+                                               cfg.d_idx, cfg.top_k, st.cuda_stream), "indexer")
+
+    def attn_tc():
+        _lib.check(lib.sgsa_sparse_attn_thresholds(P(d["q"]), P(d["k"]), P(d["v"]), P(d["iq"]),
+                                                   P(d["ik"]), P(thr), P(od), P(d["mix"]), P(out),
+                                                   B, T, H, D, cfg.d_idx, 1.0 / math.sqrt(D), 1,
+                                                   st.cuda_stream), "attn_tc")
+
     res = {}
-    stages = (("delta", delta), ("indexer_topk", index), ("sparse_attn_mix", attn))
+    # the stages as the layer runs them (fused) and the standalone index/gather pair
+    stages = (("delta", delta), ("indexer_thresholds", index_thr), ("sparse_attn_tc", attn_tc),
+              ("indexer_topk", index), ("sparse_attn_mix", attn))
     if only == "sparse_attn_mix":
         index()  # the attention stage reads the indexer's output
+    if only == "sparse_attn_tc":
+        index_thr()
     for name, fn in stages:
         if only and name != only:
             continue
@@ -323,16 +342,14 @@ def run_ours(args, ws, rank, local):
     cnt = algorithmic_counts(cfg)
     hbm, tfl, src = peaks()
     # the dominant kernel and its roofline
-    dom = max(stages, key=stages.get)
-    if dom == "sparse_attn_mix":
-        ach = cnt["bytes_gather"] / (stages[dom] / 1e3) / 1e9
-        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s"}
-    elif dom == "indexer_topk":
-        ach = cnt["f_idx"] / (stages[dom] / 1e3) / 1e12
-        roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tfl, "unit": "TFLOP/s"}
-    else:
-        ach = cnt["f_delta"] / (stages[dom] / 1e3) / 1e12
-        roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tfl, "unit": "TFLOP/s"}
+    # the dominant kernel among the stages the layer runs, and its roofline
+    layer_stages = ("delta", "indexer_thresholds", "sparse_attn_tc")
+    dom = max(layer_stages, key=lambda n: stages[n])
+    flops = {"delta": cnt["f_delta"], "indexer_thresholds": cnt["f_idx"],
+             "sparse_attn_tc": cnt["f_attn_tc"]}[dom]
+    ach = flops / (stages[dom] / 1e3) / 1e12
+    roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tfl, "unit": "TFLOP/s"}
+    roof["gather_equiv_gbs"] = cnt["bytes_gather"] / (stages["sparse_attn_tc"] / 1e3) / 1e9
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = src
     roof["traffic"] = None
@@ -366,7 +383,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["delta", "indexer_topk", "sparse_attn_mix"],
+    ap.add_argument("--only", default=None, choices=["delta", "indexer_topk", "sparse_attn_mix", "indexer_thresholds",
+                             "sparse_attn_tc"],
                     help="profiling aid: run one stage --steps times on a (scaled) config, no JSON")
     ap.add_argument("--B", type=int, default=None)
     ap.add_argument("--T", type=int, default=None)

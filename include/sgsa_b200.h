@@ -132,6 +132,31 @@ int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int3
                          void *stream);
 
 /*
+ * The indexer of sgsa_indexer_topk (bf16, DI == 64 or 128) that also writes,
+ * per query row, the exact selection as a threshold record
+ * thresholds[B,H,T][4] = {prefix, mask, cut, 1}: column j <= t is selected iff
+ * (key(s_tj) & mask) > prefix, or == prefix and j <= cut, where key() is the
+ * order-preserving 32-bit image of the fp32 score.  indices may be NULL.
+ * Replaces the selection of modelings/hybrid_dense_delta_topk.py:344-349.
+ */
+int sgsa_indexer_thresholds(const void *iq, const void *ik, int32_t *indices,
+                            uint32_t *thresholds, int B, int T, int H, int DI, int top_k,
+                            void *stream);
+
+/*
+ * Sparse attention + gate over the rows selected by threshold records from
+ * sgsa_indexer_thresholds, computed on the tensor cores over the causal
+ * prefix (bf16, D == 128, DI == 64, T < 65536).  Same result as
+ * sgsa_sparse_attn_mix on the equivalent index rows; out is bf16.
+ * Replaces modelings/hybrid_dense_delta_topk.py:343-356 and :389-390.
+ */
+int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, const void *iq,
+                                const void *ik, const uint32_t *thresholds,
+                                const float *o_delta, const void *mix, void *out, int B, int T,
+                                int H, int D, int DI, float scale, int mix_per_channel,
+                                void *stream);
+
+/*
  * The composite layer forward: chunked delta stage (no sparse write),
  * indexer top-k, sparse attention and gate, in one stream-ordered call.
  * indices may be NULL (kept in the workspace).  final_state may be NULL.

@@ -142,6 +142,35 @@ int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int3
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_indexer_thresholds(const void *iq, const void *ik, int32_t *indices,
+                            uint32_t *thresholds, int B, int T, int H, int DI, int top_k,
+                            void *stream) {
+    if (B < 0 || T < 0 || H < 0 || top_k <= 0) return SGSA_ERR_SHAPE;
+    if (!sgsa::indexer_tc_eligible(DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!iq || !ik || !thresholds) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thresholds, B, T, H, DI, top_k,
+                                                  (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, const void *iq,
+                                const void *ik, const uint32_t *thresholds,
+                                const float *o_delta, const void *mix, void *out, int B, int T,
+                                int H, int D, int DI, float scale, int mix_per_channel,
+                                void *stream) {
+    if (B < 0 || T < 0 || H < 0) return SGSA_ERR_SHAPE;
+    if (!sgsa::sparse_attn_tc_eligible(T, D, DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!q || !k || !v || !iq || !ik || !thresholds || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thresholds, o_delta, mix, out,
+                                                B, T, H, scale, mix_per_channel,
+                                                (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
 size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top_k) {
     if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D) || top_k <= 0) return 0;
     (void)DI;

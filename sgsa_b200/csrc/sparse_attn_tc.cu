@@ -20,8 +20,8 @@
 // updated lazily: O and the row sum are rescaled only when a tile's maximum
 // exceeds the one in use by more than 2^8, which keeps p <= 256 and is exact.
 //
-// Warp roles (192 threads, one CTA per (b, h, 128-query tile)): warp 0 TMA,
-// warp 1 TMEM owner + MMA issuer, warps 2-5 one thread per query row.
+// Warp roles (320 threads, one CTA per (b, h, 128-query tile)): warp 0 TMA,
+// warp 1 TMEM owner + MMA issuer, warps 2-9 two threads per query row.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -40,12 +40,12 @@ constexpr int kStage = kIQ + 16384;      // 2 stages x 40 KB
 constexpr int kStageBytes = 40960;       //   IK 8 KB | K 2 x 8 KB | V 2 x 8 KB
 constexpr int kP = kStage + 2 * kStageBytes;  // 2 buffers x (hi 16 KB | lo 16 KB)
 constexpr int kBar = kP + 2 * 32768;
-constexpr int kBytes = kBar + 256;
+constexpr int kBytes = kBar + 128 + 4 * 128 * 4;  // barriers | tile maxima
 constexpr size_t kSmem = 1024 + kBytes;
 }  // namespace L
 
 template <typename Tmix>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
 sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
@@ -78,8 +78,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
             mbar_init(&sfull[i], 1);
-            mbar_init(&sfree[i], 4);
-            mbar_init(&pfull[i], 4);
+            mbar_init(&sfree[i], 8);
+            mbar_init(&pfull[i], 8);
             mbar_init(&pfree[i], 1);
         }
         fence_barrier_init();
@@ -159,10 +159,13 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         }
         __syncwarp();
     } else {
-        const int quad = warp & 3, r = quad * 32 + lane;
+        // two threads per query row: warps w and w+4 share a TMEM lane quarter,
+        // `half` picks 32 of the tile's 64 key columns (and 64 of O's 128).
+        const int quad = warp & 3, r = quad * 32 + lane, half = (warp - 2) >> 2;
         const int t = q0 + r;
         const bool valid_row = t < T;
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
+        float *xmax = (float *)(sm + L::kBar + 128);  // [2 tiles][2 halves][128 rows]
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
         if (valid_row) th = thr[(size_t)bh * T + t];
         const uint32_t prefix = th.x, mask = th.y;
@@ -172,26 +175,25 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             const int buf = j & 1;
             mbar_wait(&sfull[buf], (j >> 1) & 1, wd, 32u);
             tc_fence_after();
-            float x[kNk];
+            float x[32], si[32], sv[32];
             float mt = -INFINITY;
+            tmem_ld32(tSidx + lrow + buf * kNk + half * 32, si);
+            tmem_ld32(tS + lrow + buf * kNk + half * 32, sv);
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                float si[32], sv[32];
-                tmem_ld32(tSidx + lrow + buf * kNk + hf * 32, si);
-                tmem_ld32(tS + lrow + buf * kNk + hf * 32, sv);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int jj = j * kNk + hf * 32 + i;
-                    const uint32_t mk = float_key(si[i]) & mask;
-                    const bool sel = jj <= t && (mk > prefix || (mk == prefix && jj <= cut));
-                    const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
-                    x[hf * 32 + i] = xv;
-                    mt = fmaxf(mt, xv);
-                }
+            for (int i = 0; i < 32; ++i) {
+                const int jj = j * kNk + half * 32 + i;
+                const uint32_t mk = float_key(si[i]) & mask;
+                const bool sel = jj <= t && (mk > prefix || (mk == prefix && jj <= cut));
+                const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
+                x[i] = xv;
+                mt = fmaxf(mt, xv);
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sfree[buf]);
+            xmax[(buf * 2 + half) * 128 + r] = mt;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            mt = fmaxf(xmax[(buf * 2 + 0) * 128 + r], xmax[(buf * 2 + 1) * 128 + r]);
             // lazy maximum: rescale only when this tile's maximum is > m_used + 8
             const bool grow = mt > m_used + 8.f || (m_used == -INFINITY && mt != -INFINITY);
             if (__any_sync(0xffffffffu, grow)) {
@@ -202,13 +204,13 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     mbar_wait(&pfree[(j - 1) & 1], ((j - 1) >> 1) & 1, wd, 64u);
                     tc_fence_after();
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < 2; ++c) {
                         float o[32];
-                        tmem_ld32(tO + lrow + c * 32, o);
+                        tmem_ld32(tO + lrow + half * 64 + c * 32, o);
                         const float g = grow ? f : 1.f;
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] *= g;
-                        tmem_st32(tO + lrow + c * 32, o);
+                        tmem_st32(tO + lrow + half * 64 + c * 32, o);
                     }
                     tc_fence_before();
                 }
@@ -218,7 +220,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             if (j >= 2) mbar_wait(&pfree[buf], ((j >> 1) & 1) ^ 1, wd, 128u);
             unsigned char *ph = sm + L::kP + buf * 32768;
 #pragma unroll
-            for (int c8 = 0; c8 < kNk / 8; ++c8) {
+            for (int c8 = 0; c8 < 4; ++c8) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -232,7 +234,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     hi[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lo[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                const uint32_t off = (uint32_t)r * 128 + (uint32_t)((c8 ^ (r & 7)) << 4);
+                const int chunk = half * 4 + c8;
+                const uint32_t off = (uint32_t)r * 128 + (uint32_t)((chunk ^ (r & 7)) << 4);
                 *(uint4 *)(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                 *(uint4 *)(ph + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
@@ -240,22 +243,26 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfull[buf]);
         }
-        // epilogue: out = mix * O / l + (1 - mix) * o_delta
+        // epilogue: out = mix * O / l + (1 - mix) * o_delta, l summed over both halves
+        xmax[half * 128 + r] = l;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
+        l = xmax[r] + xmax[128 + r];
         mbar_wait(&pfree[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, wd, 256u);
         tc_fence_after();
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
         const size_t rowq = ((size_t)b * T + t) * H + h;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
             float o[32];
-            tmem_ld32(tO + lrow + c * 32, o);
+            const int c0 = half * 64 + c * 32;
+            tmem_ld32(tO + lrow + c0, o);
             if (valid_row) {
-                __nv_bfloat16 *dst = out + rowq * D + c * 32;
+                __nv_bfloat16 *dst = out + rowq * D + c0;
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     float r0 = o[i] * inv, r1 = o[i + 1] * inv;
                     if (od) {
-                        const size_t e = rowq * D + c * 32 + i;
+                        const size_t e = rowq * D + c0 + i;
                         const float m0 = mix ? to_f32(mix_pc ? mix[e] : mix[rowq]) : 1.f;
                         const float m1 = mix ? to_f32(mix_pc ? mix[e + 1] : mix[rowq]) : 1.f;
                         r0 = m0 * r0 + (1.f - m0) * od[e];
@@ -294,7 +301,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                          (int)L::kSmem);
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRowsA);
-    kern<<<nqt * B * H, 192, L::kSmem, st>>>(mq, mk, mv, miq, mik, (const uint4 *)thr, od,
+    kern<<<nqt * B * H, 320, L::kSmem, st>>>(mq, mk, mv, miq, mik, (const uint4 *)thr, od,
                                              (const __nv_bfloat16 *)mix, (__nv_bfloat16 *)out,
                                              B, T, H, scale * 1.4426950408889634f, mix_pc, nqt);
     return cudaGetLastError();
