@@ -20,8 +20,9 @@
 // updated lazily: O and the row sum are rescaled only when a tile's maximum
 // exceeds the one in use by more than 2^8, which keeps p <= 256 and is exact.
 //
-// Warp roles (320 threads, one CTA per (b, h, 128-query tile)): warp 0 TMA,
-// warp 1 TMEM owner + MMA issuer, warps 2-9 two threads per query row.
+// Warp roles (96 + 128 kParts threads, one CTA per (b, h, 128-query tile)): warp 0 TMA,
+// warp 1 TMEM owner + MMA issuer, warp 2 TMA of the values, warps 3.. kParts
+// threads per query row.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -33,19 +34,27 @@ static __device__ unsigned int g_attn_watchdog;
 
 constexpr int kRowsA = 128;
 constexpr int kNk = 64;  // keys per tile
+constexpr int kParts = 4;              // softmax threads per query row
+constexpr int kCP = kNk / kParts;      // key columns per thread
+constexpr int kOP = 128 / kParts;      // O columns per thread
+constexpr int kAttnThreads = 96 + 128 * kParts;
+constexpr int kKS = 3;                 // stages of the (indexer key, key) ring
+constexpr int kVS = 2;                 // stages of the value ring
 namespace L {
 constexpr int kQ = 0;                    // Q tile, 2 x 16 KB (K-major, 64-col blocks)
 constexpr int kIQ = kQ + 32768;          // IQ tile 16 KB
-constexpr int kStage = kIQ + 16384;      // 2 stages x 40 KB
-constexpr int kStageBytes = 40960;       //   IK 8 KB | K 2 x 8 KB | V 2 x 8 KB
-constexpr int kP = kStage + 2 * kStageBytes;  // 2 buffers x (hi 16 KB | lo 16 KB)
+constexpr int kKStage = kIQ + 16384;     // kKS stages x 24 KB: IK 8 KB | K 2 x 8 KB
+constexpr int kKBytes = 24576;
+constexpr int kVStage = kKStage + kKS * kKBytes;  // kVS stages x 16 KB: V 2 x 8 KB
+constexpr int kVBytes = 16384;
+constexpr int kP = kVStage + kVS * kVBytes;  // 2 buffers x (hi 16 KB | lo 16 KB)
 constexpr int kBar = kP + 2 * 32768;
-constexpr int kBytes = kBar + 128 + 4 * 128 * 4;  // barriers | tile maxima
+constexpr int kBytes = kBar + 256 + 2 * kParts * 128 * 4;  // barriers | tile maxima
 constexpr size_t kSmem = 1024 + kBytes;
 }  // namespace L
 
 template <typename Tmix>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(kAttnThreads, 1)
 sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
@@ -59,8 +68,9 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(sm + L::kBar);
-    uint64_t *qfull = bars, *full = bars + 1, *empty = bars + 3, *sfull = bars + 5,
-             *sfree = bars + 7, *pfull = bars + 9, *pfree = bars + 11;
+    uint64_t *qfull = bars, *kfull = bars + 1, *kempty = bars + 4, *vfull = bars + 7,
+             *vempty = bars + 9, *sfull = bars + 11, *sfree = bars + 13, *pfull = bars + 15,
+             *pfree = bars + 17;
     __shared__ uint32_t s_tmem;
     unsigned int *wd = &g_attn_watchdog;
 
@@ -74,12 +84,18 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 
     if (threadIdx.x == 0) {
         mbar_init(qfull, 1);
+        for (int i = 0; i < kKS; ++i) {
+            mbar_init(&kfull[i], 1);
+            mbar_init(&kempty[i], 1);
+        }
+        for (int i = 0; i < kVS; ++i) {
+            mbar_init(&vfull[i], 1);
+            mbar_init(&vempty[i], 1);
+        }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
             mbar_init(&sfull[i], 1);
-            mbar_init(&sfree[i], 8);
-            mbar_init(&pfull[i], 8);
+            mbar_init(&sfree[i], 4 * kParts);
+            mbar_init(&pfull[i], 4 * kParts);
             mbar_init(&pfree[i], 1);
         }
         fence_barrier_init();
@@ -92,23 +108,34 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     // TMEM columns: Sidx[2] at 0/64, S[2] at 128/192, O at 256..383
     const uint32_t tSidx = tmem, tS = tmem + 128, tO = tmem + 256;
 
-    if (warp == 0) {
+    if (warp == 0) {  // producer of the query tiles and the (indexer key, key) ring
         if (lane == 0) {
             mbar_arrive_expect_tx(qfull, 32768 + 16384);
             tma_load_3d(sm + L::kQ, &tm_q, qfull, 0, h, b * T + q0);
             tma_load_3d(sm + L::kQ + 16384, &tm_q, qfull, 64, h, b * T + q0);
             tma_load_3d(sm + L::kIQ, &tm_iq, qfull, 0, h, b * T + q0);
             for (int j = 0; j < nkt; ++j) {
-                const int st = j & 1;
-                mbar_wait(&empty[st], ((j >> 1) & 1) ^ 1, wd, 1u);
-                unsigned char *stg = sm + L::kStage + st * L::kStageBytes;
-                mbar_arrive_expect_tx(&full[st], L::kStageBytes);
+                const int st = j % kKS;
+                mbar_wait(&kempty[st], ((j / kKS) & 1) ^ 1, wd, 1u);
+                unsigned char *stg = sm + L::kKStage + st * L::kKBytes;
+                mbar_arrive_expect_tx(&kfull[st], L::kKBytes);
                 const int row = b * T + j * kNk;
-                tma_load_3d(stg, &tm_ik, &full[st], 0, h, row);
-                tma_load_3d(stg + 8192, &tm_k, &full[st], 0, h, row);
-                tma_load_3d(stg + 16384, &tm_k, &full[st], 64, h, row);
-                tma_load_3d(stg + 24576, &tm_v, &full[st], 0, h, row);
-                tma_load_3d(stg + 32768, &tm_v, &full[st], 64, h, row);
+                tma_load_3d(stg, &tm_ik, &kfull[st], 0, h, row);
+                tma_load_3d(stg + 8192, &tm_k, &kfull[st], 0, h, row);
+                tma_load_3d(stg + 16384, &tm_k, &kfull[st], 64, h, row);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 2) {  // producer of the value ring
+        if (lane == 0) {
+            for (int j = 0; j < nkt; ++j) {
+                const int st = j % kVS;
+                mbar_wait(&vempty[st], ((j / kVS) & 1) ^ 1, wd, 1u);
+                unsigned char *stg = sm + L::kVStage + st * L::kVBytes;
+                mbar_arrive_expect_tx(&vfull[st], L::kVBytes);
+                const int row = b * T + j * kNk;
+                tma_load_3d(stg, &tm_v, &vfull[st], 0, h, row);
+                tma_load_3d(stg + 8192, &tm_v, &vfull[st], 64, h, row);
             }
         }
         __syncwarp();
@@ -120,10 +147,12 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_wait(qfull, 0, wd, 2u);
             auto issue_pv = [&](int jj) {
                 const int pb = jj & 1;
+                const int vs = jj % kVS;
+                mbar_wait(&vfull[vs], (jj / kVS) & 1, wd, 4u);
                 mbar_wait(&pfull[pb], (jj >> 1) & 1, wd, 4u);
                 tc_fence_after();
                 const uint32_t ph = smem_u32(sm + L::kP + pb * 32768);
-                const uint32_t vq = smem_u32(sm + L::kStage + (jj & 1) * L::kStageBytes + 24576);
+                const uint32_t vq = smem_u32(sm + L::kVStage + vs * L::kVBytes);
 #pragma unroll
                 for (int part = 0; part < 2; ++part)
 #pragma unroll
@@ -133,14 +162,14 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         mma_bf16(tO, ad, bd, id_pv, (jj | part | kk) ? 1u : 0u);
                     }
                 mma_commit(&pfree[pb]);
-                mma_commit(&empty[jj & 1]);
+                mma_commit(&vempty[vs]);
             };
             for (int j = 0; j < nkt; ++j) {
-                const int st = j & 1, buf = j & 1;
-                mbar_wait(&full[st], (j >> 1) & 1, wd, 8u);
+                const int st = j % kKS, buf = j & 1;
+                mbar_wait(&kfull[st], (j / kKS) & 1, wd, 8u);
                 mbar_wait(&sfree[buf], ((j >> 1) & 1) ^ 1, wd, 16u);
                 tc_fence_after();
-                const uint32_t stg = smem_u32(sm + L::kStage + st * L::kStageBytes);
+                const uint32_t stg = smem_u32(sm + L::kKStage + st * L::kKBytes);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)  // indexer scores: same sequence as the indexer
                     mma_bf16(tSidx + buf * kNk, sdesc_kmajor_sw128(aiq + kk * 32),
@@ -153,19 +182,20 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                                  sdesc_kmajor_sw128(stg + 8192 + kb * 8192 + kk * 32), id_s,
                                  (kb | kk) ? 1u : 0u);
                 mma_commit(&sfull[buf]);
+                mma_commit(&kempty[st]);
                 if (j > 0) issue_pv(j - 1);
             }
             issue_pv(nkt - 1);
         }
         __syncwarp();
     } else {
-        // two threads per query row: warps w and w+4 share a TMEM lane quarter,
-        // `half` picks 32 of the tile's 64 key columns (and 64 of O's 128).
-        const int quad = warp & 3, r = quad * 32 + lane, half = (warp - 2) >> 2;
+        // kParts threads per query row: warps w, w+4, w+8, ... share a TMEM lane
+        // quarter; `part` picks kCP of the tile's 64 key columns (and kOP of O's).
+        const int quad = warp & 3, r = quad * 32 + lane, part = (warp - 3) >> 2;
         const int t = q0 + r;
         const bool valid_row = t < T;
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
-        float *xmax = (float *)(sm + L::kBar + 128);  // [2 tiles][2 halves][128 rows]
+        float *xmax = (float *)(sm + L::kBar + 256);  // [2 tiles][kParts][128 rows]
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
         if (valid_row) th = thr[(size_t)bh * T + t];
         const uint32_t prefix = th.x, mask = th.y;
@@ -175,15 +205,17 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             const int buf = j & 1;
             mbar_wait(&sfull[buf], (j >> 1) & 1, wd, 32u);
             tc_fence_after();
-            float x[32], si[32], sv[32];
+            float x[kCP], si[kCP], sv[kCP];
             float mt = -INFINITY;
-            tmem_ld32(tSidx + lrow + buf * kNk + half * 32, si);
-            tmem_ld32(tS + lrow + buf * kNk + half * 32, sv);
+            tmem_ld16(tSidx + lrow + buf * kNk + part * kCP, si);
+            tmem_ld16(tS + lrow + buf * kNk + part * kCP, sv);
+            const int jb = j * kNk + part * kCP;
+            const bool full = jb + kCP - 1 <= q0;  // every row of the tile sees all columns
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const int jj = j * kNk + half * 32 + i;
+            for (int i = 0; i < kCP; ++i) {
+                const int jj = jb + i;
                 const uint32_t mk = float_key(si[i]) & mask;
-                const bool sel = jj <= t && (mk > prefix || (mk == prefix && jj <= cut));
+                const bool sel = (full || jj <= t) && (mk > prefix || (mk == prefix && jj <= cut));
                 const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
                 x[i] = xv;
                 mt = fmaxf(mt, xv);
@@ -191,9 +223,10 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sfree[buf]);
-            xmax[(buf * 2 + half) * 128 + r] = mt;
-            asm volatile("bar.sync 1, 256;" ::: "memory");
-            mt = fmaxf(xmax[(buf * 2 + 0) * 128 + r], xmax[(buf * 2 + 1) * 128 + r]);
+            xmax[(buf * kParts + part) * 128 + r] = mt;
+            asm volatile("bar.sync 1, %0;" ::"r"(kParts * 128) : "memory");
+#pragma unroll
+            for (int p2 = 0; p2 < kParts; ++p2) mt = fmaxf(mt, xmax[(buf * kParts + p2) * 128 + r]);
             // lazy maximum: rescale only when this tile's maximum is > m_used + 8
             const bool grow = mt > m_used + 8.f || (m_used == -INFINITY && mt != -INFINITY);
             if (__any_sync(0xffffffffu, grow)) {
@@ -203,30 +236,27 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 if (j > 0) {  // O holds tiles < j: wait for the last PV into it
                     mbar_wait(&pfree[(j - 1) & 1], ((j - 1) >> 1) & 1, wd, 64u);
                     tc_fence_after();
+                    float o[32];
+                    tmem_ld32(tO + lrow + part * kOP, o);
+                    const float g = grow ? f : 1.f;
 #pragma unroll
-                    for (int c = 0; c < 2; ++c) {
-                        float o[32];
-                        tmem_ld32(tO + lrow + half * 64 + c * 32, o);
-                        const float g = grow ? f : 1.f;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= g;
-                        tmem_st32(tO + lrow + half * 64 + c * 32, o);
-                    }
+                    for (int i = 0; i < 32; ++i) o[i] *= g;
+                    tmem_st32(tO + lrow + part * kOP, o);
                     tc_fence_before();
                 }
                 if (grow) m_used = m_new;
             }
             // P = exp2(x - m_used) as bf16 hi + lo, K-major rows of 64 keys
+            const float mref = (m_used == -INFINITY) ? 0.f : m_used;  // x = -inf -> p = 0
             if (j >= 2) mbar_wait(&pfree[buf], ((j >> 1) & 1) ^ 1, wd, 128u);
             unsigned char *ph = sm + L::kP + buf * 32768;
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
+            for (int c8 = 0; c8 < kCP / 8; ++c8) {
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    const float x0 = x[c8 * 8 + 2 * u], x1 = x[c8 * 8 + 2 * u + 1];
-                    const float p0 = (x0 == -INFINITY) ? 0.f : exp2f(x0 - m_used);
-                    const float p1 = (x1 == -INFINITY) ? 0.f : exp2f(x1 - m_used);
+                    const float p0 = exp2f(x[c8 * 8 + 2 * u] - mref);
+                    const float p1 = exp2f(x[c8 * 8 + 2 * u + 1] - mref);
                     l += p0 + p1;
                     const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
                     const float2 hf = __bfloat1622float2(h2);
@@ -234,7 +264,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     hi[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lo[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                const int chunk = half * 4 + c8;
+                const int chunk = part * (kCP / 8) + c8;
                 const uint32_t off = (uint32_t)r * 128 + (uint32_t)((chunk ^ (r & 7)) << 4);
                 *(uint4 *)(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                 *(uint4 *)(ph + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -243,18 +273,19 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfull[buf]);
         }
-        // epilogue: out = mix * O / l + (1 - mix) * o_delta, l summed over both halves
-        xmax[half * 128 + r] = l;
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        l = xmax[r] + xmax[128 + r];
+        // epilogue: out = mix * O / l + (1 - mix) * o_delta, l summed over the parts
+        xmax[part * 128 + r] = l;
+        asm volatile("bar.sync 1, %0;" ::"r"(kParts * 128) : "memory");
+        l = 0.f;
+#pragma unroll
+        for (int p2 = 0; p2 < kParts; ++p2) l += xmax[p2 * 128 + r];
         mbar_wait(&pfree[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, wd, 256u);
         tc_fence_after();
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
         const size_t rowq = ((size_t)b * T + t) * H + h;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        {
             float o[32];
-            const int c0 = half * 64 + c * 32;
+            const int c0 = part * kOP;
             tmem_ld32(tO + lrow + c0, o);
             if (valid_row) {
                 __nv_bfloat16 *dst = out + rowq * D + c0;
@@ -301,7 +332,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                          (int)L::kSmem);
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRowsA);
-    kern<<<nqt * B * H, 320, L::kSmem, st>>>(mq, mk, mv, miq, mik, (const uint4 *)thr, od,
+    kern<<<nqt * B * H, kAttnThreads, L::kSmem, st>>>(mq, mk, mv, miq, mik, (const uint4 *)thr, od,
                                              (const __nv_bfloat16 *)mix, (__nv_bfloat16 *)out,
                                              B, T, H, scale * 1.4426950408889634f, mix_pc, nqt);
     return cudaGetLastError();
