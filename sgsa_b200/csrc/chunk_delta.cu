@@ -530,6 +530,245 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
     if (warp == 1) tmem_dealloc(tmem, 256);
 }
 
+// ---- tensor-core prep (bf16 inputs, D = 128, no sparse write) --------------
+//
+// One CTA per pair of consecutive chunks of one (b, h), stacked into 128 rows:
+//   KK^T, QK^T   bf16 tcgen05.mma (only the two 64x64 diagonal blocks are used)
+//   T = (I + A)^-1 per 64x64 block: one thread per column, the column in
+//                registers, forward substitution with broadcast reads of A
+//   W  = T diag(lam e^G) K,  Uh = T diag(lam) V   bf16 tcgen05.mma with the
+//                scaled T split into bf16 hi + lo parts (fp32-level accuracy;
+//                K and V enter exactly, straight from their TMA tiles as
+//                MN-major operands)
+// plus the operands of the tensor-core scan (Aqk, Qt, Kt^T, G) of both chunks.
+namespace ptc {
+constexpr int kK = 0;           // K tile bf16 [128 j][128 dk], 2 x 16 KB
+constexpr int kV = 32768;       // V tile bf16, 2 x 16 KB
+constexpr int kQ = 65536;       // Q tile bf16 (2 x 16 KB), then T''hi (16 KB) | T''lo
+constexpr int kA = 98304;       // A blocks fp32 [2][64][64] (32 KB), then (kQ..): T''
+constexpr int kX = 131072;      // T'hi | T'lo bf16 [128 i][128 j], 2 x 32 KB
+constexpr int kBar = 196608;
+constexpr size_t kSmem = 1024 + kBar + 64;
+}  // namespace ptc
+
+// Byte offset of bf16 element (r, c) in a K-major 128-byte-swizzled operand of
+// 128 rows (64 columns per 16 KB block).
+__device__ __forceinline__ uint32_t sw128_bf16(int r, int c) {
+    return (uint32_t)((c >> 6) * 16384 + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4) +
+                      ((c & 7) << 1));
+}
+
+__global__ void __launch_bounds__(256, 1)
+chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_v) {
+    using namespace sm100;
+    constexpr int D = 128;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(sm + ptc::kBar);
+    uint64_t *ldbar = bars, *mma1 = bars + 1, *mma2 = bars + 2;
+    __shared__ uint32_t s_tmem;
+    __shared__ float sG[128], sLam[128];
+    unsigned int *wd = &g_scan_watchdog;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c0 = blockIdx.x * 2, bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+    const int NC = a.NC, T = a.T;
+    const int t0 = c0 * kC;
+    const __nv_bfloat16 *beta = (const __nv_bfloat16 *)a.beta,
+                        *gamma = (const __nv_bfloat16 *)a.gamma;
+    auto valid = [&](int i) { return t0 + i < T && (i < kC || c0 + 1 < NC); };
+    auto row = [&](int i) -> size_t { return ((size_t)b * T + t0 + i) * a.H + h; };
+
+    if (tid == 0) {
+        mbar_init(ldbar, 1);
+        mbar_init(mma1, 1);
+        mbar_init(mma2, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(ldbar, 3 * 32768);
+        for (int kb = 0; kb < 2; ++kb) {
+            tma_load_3d(sm + ptc::kK + kb * 16384, &tm_k, ldbar, kb * 64, h, b * T + t0);
+            tma_load_3d(sm + ptc::kV + kb * 16384, &tm_v, ldbar, kb * 64, h, b * T + t0);
+            tma_load_3d(sm + ptc::kQ + kb * 16384, &tm_q, ldbar, kb * 64, h, b * T + t0);
+        }
+    }
+    if (warp == 1) tmem_alloc(&s_tmem, 256);
+    if (tid < 128) {
+        const bool ok = valid(tid);
+        sG[tid] = ok ? logf(__bfloat162float(gamma[row(tid)])) : 0.f;
+        sLam[tid] = ok ? __bfloat162float(beta[row(tid)]) : 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    if (warp < 2) {  // inclusive cumsum of log(gamma) per 64-token chunk, two tokens per lane
+        float *g = sG + warp * kC;
+        const float x0 = g[2 * lane], x1 = g[2 * lane + 1];
+        float s = x0 + x1;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, s, off);
+            if (lane >= off) s += y;
+        }
+        const float ex = s - (x0 + x1);
+        g[2 * lane] = ex + x0;
+        g[2 * lane + 1] = ex + x0 + x1;
+    }
+    if (tid == 0) {  // KK^T -> cols [0,128), QK^T -> cols [128,256)
+        mbar_wait(ldbar, 0, wd, 0x100u);
+        tc_fence_after();
+        constexpr uint32_t id = idesc_bf16_f32(128, 128);
+        const uint32_t kq = smem_u32(sm + ptc::kK), qq = smem_u32(sm + ptc::kQ);
+        for (int kb = 0; kb < 2; ++kb)
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t bd = sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32);
+                const uint32_t acc = (kb | kk) ? 1u : 0u;
+                mma_bf16(tmem, sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32), bd, id, acc);
+                mma_bf16(tmem + 128, sdesc_kmajor_sw128(qq + kb * 16384 + kk * 32), bd, id, acc);
+            }
+        mma_commit(mma1);
+    }
+    __syncthreads();
+    mbar_wait(mma1, 0, wd, 0x200u);
+    tc_fence_after();
+    float *Ablk = (float *)(sm + ptc::kA);  // [2][64 i][64 j]
+    {   // A (warps 0-3) and Aqk (warps 4-7), one row per thread, its own 64-column block
+        const int quad = warp & 3, i = quad * 32 + lane, cb = i >> 6, tau = i & 63;
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (warp < 4 ? 0 : 128) + cb * 64;
+        const bool vi = valid(i);
+        float *aqk = a.Aqk + (((size_t)bh * NC + c0 + cb) * kC + tau) * kC;
+        const bool chunk_ok = c0 + cb < NC;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            float d[32];
+            tmem_ld32(taddr + hf * 32, d);
+#pragma unroll
+            for (int jj = 0; jj < 32; jj += 4) {
+                float4 r4;
+                float *r = &r4.x;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int m = hf * 32 + jj + u, j = cb * 64 + m;
+                    const bool vj = valid(j);
+                    if (warp < 4)
+                        r[u] = (vi && vj && m < tau) ? sLam[i] * __expf(sG[i] - sG[j]) * d[jj + u] : 0.f;
+                    else
+                        r[u] = (vi && vj && m <= tau) ? __expf(sG[i] - sG[j]) * d[jj + u] : 0.f;
+                }
+                if (warp < 4) *(float4 *)(Ablk + (cb * 64 + tau) * 64 + hf * 32 + jj) = r4;
+                else if (chunk_ok) *(float4 *)(aqk + hf * 32 + jj) = r4;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    float tcol[64];
+    if (tid < 128) {
+        // column c of T = (I + A)^-1 of block blk: t_i = [i == c] - sum_{j<i} A[i][j] t_j
+        const int blk = tid >> 6, c = tid & 63;
+        const float *Ab = Ablk + blk * 4096;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            float s = (i == c) ? 1.f : 0.f;
+#pragma unroll
+            for (int j = 0; j < i; j += 4) {
+                const float4 a4 = *(const float4 *)(Ab + i * 64 + j);  // broadcast
+                s -= a4.x * tcol[j];
+                if (j + 1 < i) s -= a4.y * tcol[j + 1];
+                if (j + 2 < i) s -= a4.z * tcol[j + 2];
+                if (j + 3 < i) s -= a4.w * tcol[j + 3];
+            }
+            tcol[i] = s;
+        }
+    } else {
+        // operands of the scan: Qt = e^{G} q (row-major), Kt^T = e^{G_last - G} k ([dk][tok]),
+        // read from the swizzled Q and K tiles; G
+        const int u = tid - 128;
+        const unsigned char *Kt = sm + ptc::kK, *Qt = sm + ptc::kQ;
+        for (int cb = 0; cb < 2; ++cb) {
+            if (c0 + cb >= NC) break;
+            const size_t cix = (size_t)bh * NC + c0 + cb;
+            const float glast = sG[cb * 64 + 63];
+            for (int e = u; e < kC * D; e += 128) {  // Qt: d fastest (coalesced)
+                const int m = e / D, d = e % D, j = cb * 64 + m;
+                const float qv = __bfloat162float(*(const __nv_bfloat16 *)(Qt + sw128_bf16(j, d)));
+                a.Qt[(cix * kC + m) * D + d] = valid(j) ? __expf(sG[j]) * qv : 0.f;
+            }
+            for (int e = u; e < kC * D; e += 128) {  // Kt^T: m fastest (coalesced)
+                const int d = e / kC, m = e % kC, j = cb * 64 + m;
+                const float kv = __bfloat162float(*(const __nv_bfloat16 *)(Kt + sw128_bf16(j, d)));
+                a.KtT[(cix * D + d) * kC + m] = valid(j) ? __expf(glast - sG[j]) * kv : 0.f;
+            }
+            if (u < 64) a.G[cix * kC + u] = sG[cb * 64 + u];
+        }
+    }
+    __syncthreads();  // the Q tile and the A blocks are dead from here
+    if (tid < 128) {
+        // T' = T diag(lam e^G) into kX (hi | lo), T'' = T diag(lam) into kQ.. (hi | lo);
+        // rows of the other block are zero
+        const int blk = tid >> 6, c = tid & 63, col = blk * 64 + c;
+        const float s1 = sLam[col] * __expf(sG[col]), s2 = sLam[col];
+        unsigned char *X = sm + ptc::kX, *Y = sm + ptc::kQ;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+            const int li = i - blk * 64;
+            const float tv = (li >= 0 && li < 64) ? tcol[li & 63] : 0.f;
+            const float v1 = tv * s1, v2 = tv * s2;
+            const __nv_bfloat16 h1 = __float2bfloat16_rn(v1), h2 = __float2bfloat16_rn(v2);
+            const uint32_t off = sw128_bf16(i, col);
+            *(__nv_bfloat16 *)(X + off) = h1;
+            *(__nv_bfloat16 *)(X + 32768 + off) = __float2bfloat16_rn(v1 - __bfloat162float(h1));
+            *(__nv_bfloat16 *)(Y + off) = h2;
+            *(__nv_bfloat16 *)(Y + 32768 + off) = __float2bfloat16_rn(v2 - __bfloat162float(h2));
+        }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {  // W -> cols [0,128), Uh -> cols [128,256); B = K / V tiles, MN-major
+        constexpr uint32_t id = idesc_bf16_f32_bmn(128, 128);
+        const uint32_t xq = smem_u32(sm + ptc::kX), yq = smem_u32(sm + ptc::kQ),
+                       kq = smem_u32(sm + ptc::kK), vq = smem_u32(sm + ptc::kV);
+        for (int part = 0; part < 2; ++part)
+            for (int kb = 0; kb < 2; ++kb)
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint32_t aoff = part * 32768 + kb * 16384 + kk * 32;
+                    const uint32_t boff = kb * 8192 + kk * 2048;  // 64 rows of j per block
+                    const uint32_t acc = (part | kb | kk) ? 1u : 0u;
+                    mma_bf16(tmem, sdesc_kmajor_sw128(xq + aoff),
+                             sdesc_mnmajor_sw128(kq + boff, 16384, 1024), id, acc);
+                    mma_bf16(tmem + 128, sdesc_kmajor_sw128(yq + aoff),
+                             sdesc_mnmajor_sw128(vq + boff, 16384, 1024), id, acc);
+                }
+        mma_commit(mma2);
+    }
+    __syncthreads();
+    mbar_wait(mma2, 0, wd, 0x400u);
+    tc_fence_after();
+    {
+        const int quad = warp & 3, i = quad * 32 + lane, cb = i >> 6, tau = i & 63;
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (warp < 4 ? 0 : 128);
+        float *dst = (warp < 4 ? a.W : a.U) + (((size_t)bh * NC + c0 + cb) * kC + tau) * D;
+        const bool ok = c0 + cb < NC;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            float d[32];
+            tmem_ld32(taddr + cc * 32, d);
+            if (ok)
+#pragma unroll
+                for (int jj = 0; jj < 32; jj += 4)
+                    *(float4 *)(dst + cc * 32 + jj) = make_float4(d[jj], d[jj + 1], d[jj + 2], d[jj + 3]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
 static bool scan_use_tc() {
     const char *e = getenv("SGSA_SCAN_SIMT");
     return !(e && e[0] == '1');
@@ -537,22 +776,24 @@ static bool scan_use_tc() {
 
 template <typename Tout>
 cudaError_t run_tc_scan(const ChunkArgs &a, cudaStream_t st) {
-    using Dm = Dims<128, false>;
-    auto prep = chunk_prep_kernel<__nv_bfloat16, 128, false>;
-    cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)Dm::prep_smem);
-    if (e != cudaSuccess) return e;
     const long long nch = (long long)a.B * a.H * a.NC;
-    CUtensorMap mw, mq, ma, mk;
+    CUtensorMap mw, mq, ma, mk, mkin, mqin, mvin;
     if (!make_tmap_2d_f32(&mw, a.W, 128, nch * 64, 64) ||
         !make_tmap_2d_f32(&mq, a.Qt, 128, nch * 64, 64) ||
         !make_tmap_2d_f32(&ma, a.Aqk, 64, nch * 64, 64) ||
-        !make_tmap_2d_f32(&mk, a.KtT, 64, nch * 128, 128))
+        !make_tmap_2d_f32(&mk, a.KtT, 64, nch * 128, 128) ||
+        !make_tmap_rows_bf16(&mkin, a.k, a.B, a.T, a.H, 128, 128) ||
+        !make_tmap_rows_bf16(&mqin, a.q, a.B, a.T, a.H, 128, 128) ||
+        !make_tmap_rows_bf16(&mvin, a.v, a.B, a.T, a.H, 128, 128))
         return cudaErrorInvalidValue;
+    auto prep = chunk_prep_tc_kernel;
+    cudaError_t e = cudaFuncSetAttribute(prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)ptc::kSmem);
+    if (e != cudaSuccess) return e;
     auto scan = chunk_scan_tc_kernel<Tout>;
     e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmem);
     if (e != cudaSuccess) return e;
-    prep<<<dim3(a.NC, a.B * a.H), kThreads, Dm::prep_smem, st>>>(a);
+    prep<<<dim3((a.NC + 1) / 2, a.B * a.H), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     scan<<<a.B * a.H, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
