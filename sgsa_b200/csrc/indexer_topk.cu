@@ -223,6 +223,7 @@ struct RowSel {
     int top;     // bits [top-1 : 0] of the k-th key are still unknown
     bool done;
     bool plain;  // the row left the fast window: full order-preserving keys
+    bool exact;  // resolved with every key of the final group selected (no tie cut)
 };
 
 // Key of a score for a row whose k-th score is a positive float: the raw bits
@@ -264,6 +265,7 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
         s.mask |= ((1u << w) - 1u) << shift;
         s.top = shift;
     }
+    if (cnt == s.need) s.exact = true;
     if (cnt == s.need || s.top == 0) s.done = true;
 }
 
@@ -379,8 +381,11 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const bool has_row = epi && t < T;
     int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
     uint4 *thr_row = (has_row && thr) ? thr + (size_t)bh * T + t : nullptr;
-    RowSel s{0u, 0u, K, 32, true, false};
-    if (epi && nvalid > K) s.done = false;
+    RowSel s{0u, 0u, K, 32, true, false, true};
+    if (epi && nvalid > K) {
+        s.done = false;
+        s.exact = false;
+    }
     if (epi && half == 0 && has_row && nvalid <= K) {
         if (out_row)
             for (int i = 0; i < K; ++i) out_row[i] = (i < nvalid) ? i : -1;
@@ -531,7 +536,19 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         }
         const int more = __syncthreads_or(epi && !s.done);
         if (collecting) break;
-        if (!more || pass + 1 >= kMaxDigitPasses) collecting = true;
+        if (!more || pass + 1 >= kMaxDigitPasses) {
+            // Without index rows to write, the collect pass only finds the tie cut of
+            // rows whose k-th key is an exact tie; if there is none, it is skipped.
+            if (!idx) {
+                const bool ties = __syncthreads_or(epi && has_row && nvalid > K && !s.exact);
+                if (!ties) {
+                    if (epi && half == 0 && thr_row && nvalid > K)
+                        *thr_row = make_uint4(s.prefix, s.mask, 0x7fffffffu, 1u);
+                    break;
+                }
+            }
+            collecting = true;
+        }
     }
     tc_fence_before();
     __syncthreads();

@@ -284,3 +284,21 @@ def test_layer_fused_attention_matches_gather_and_oracle(B, T, H, K, monkeypatch
     ro, _ = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"])
     want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx.cpu().numpy(), ro, x["mix"])
     assert oracle.rel_l2(fused.float().cpu().numpy(), want) < 2e-3
+
+
+def test_layer_fused_attention_with_exact_score_ties(monkeypatch):
+    """Integer-valued indexer vectors make many k-th scores exact ties, so the
+    threshold carries a tie cut; the fused path must still select exactly the
+    rows the index-writing path selects."""
+    cfg = CONFIGS["b200_bf16"].scaled(name="ties", B=1, T=1500, H=2, top_k=100)
+    x = make_inputs(cfg, seed=4)
+    g = torch.Generator().manual_seed(5)
+    x["iq"] = torch.randint(-2, 3, x["iq"].shape, generator=g).bfloat16()
+    x["ik"] = torch.randint(-2, 3, x["ik"].shape, generator=g).bfloat16()
+    d = dev(x)
+    args = (d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"], d["ik"], d["mix"], cfg.top_k)
+    fused = ops.sgsa_layer_fwd(*args)
+    monkeypatch.setenv("SGSA_ATTN_GATHER", "1")
+    gather, idx = ops.sgsa_layer_fwd(*args, return_indices=True)
+    np.testing.assert_array_equal(idx.cpu().numpy(), oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k))
+    assert oracle.rel_l2(fused.float().cpu().numpy(), gather.float().cpu().numpy()) < 2e-3
