@@ -322,10 +322,7 @@ def run_ours(args, ws, rank, local):
     d2h = out_host.numel() * out_host.element_size()
 
     def e2e_step():
-        g = {n: pinned[n].to("cuda", non_blocking=True) for n in names}
-        o = ops.sgsa_layer_fwd(g["q"], g["k"], g["v"], g["beta"], g["gamma"], g["iq"], g["ik"],
-                               g["mix"], cfg.top_k)
-        out_host.copy_(o, non_blocking=True)
+        ops.sgsa_layer_fwd_from_host(*(pinned[n] for n in names), cfg.top_k, out=out_host)
 
     for _ in range(2):
         e2e_step()

@@ -257,3 +257,94 @@ def sgsa_layer_fwd(q: Tensor, k: Tensor, v: Tensor, beta: Tensor, gamma: Tensor,
     if return_indices:
         res.append(ix)
     return res[0] if len(res) == 1 else tuple(res)
+
+
+def indexer_thresholds(iq: Tensor, ik: Tensor, top_k: int, return_indices: bool = False):
+    """Tensor-core indexer (bf16, DI 64/128) returning the exact per-row selection as
+    threshold records int32 ``[B, H, T, 4]`` (see include/sgsa_b200.h), plus the
+    index rows if asked for."""
+    _dev(iq, "iq"), _dev(ik, "ik")
+    B, T, H, DI = iq.shape
+    iq_, ik_ = iq.contiguous(), ik.to(iq.dtype).contiguous()
+    thr = torch.empty(B, H, T, 4, device=iq.device, dtype=torch.int32)
+    ix = torch.empty(B, H, T, top_k, device=iq.device, dtype=torch.int32) if return_indices else None
+    st = _lib.load().sgsa_indexer_thresholds(_ptr(iq_), _ptr(ik_), _ptr(ix), _ptr(thr), B, T, H,
+                                              DI, top_k, _stream(iq))
+    _lib.check(st, "sgsa_indexer_thresholds")
+    return (thr, ix) if return_indices else thr
+
+
+def sparse_attn_thresholds(q, k, v, iq, ik, thresholds, o_delta=None, mix=None, scale=None):
+    """Tensor-core sparse attention + gate over the rows selected by ``thresholds``."""
+    B, T, H, D = q.shape
+    DI = iq.shape[-1]
+    out = torch.empty_like(q)
+    od = None if o_delta is None else o_delta.to(torch.float32).contiguous()
+    mx = None if mix is None else mix.to(q.dtype).contiguous()
+    per_channel = int(mx is not None and mx.dim() == 4)
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    st = _lib.load().sgsa_sparse_attn_thresholds(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(iq), _ptr(ik), _ptr(thresholds), _ptr(od), _ptr(mx),
+        _ptr(out), B, T, H, D, DI, sc, per_channel, _stream(q))
+    _lib.check(st, "sgsa_sparse_attn_thresholds")
+    return out
+
+
+_copy_streams = {}
+
+
+def sgsa_layer_fwd_from_host(q, k, v, beta, gamma, iq, ik, mix, top_k, device=None,
+                             out: Optional[Tensor] = None):
+    """``sgsa_layer_fwd`` for inputs in host memory: returns the output in host memory.
+
+    The host->device copies run on a side stream in the order the stages consume
+    them (indexer vectors, then q/k/v/beta/gamma, then the mix), so they overlap the
+    indexer and the delta stage; the output is copied back on the same stream as the
+    last kernel.  Host tensors should be pinned for the copies to be asynchronous.
+    """
+    dev = torch.device(device) if device is not None else torch.device("cuda",
+                                                                        torch.cuda.current_device())
+    comp = torch.cuda.current_stream(dev)
+    cs = _copy_streams.get(dev.index)
+    if cs is None:
+        cs = _copy_streams[dev.index] = torch.cuda.Stream(dev)
+    host = dict(iq=iq, ik=ik, q=q, k=k, v=v, beta=beta, gamma=gamma, mix=mix)
+    d, ev = {}, {}
+    cs.wait_stream(comp)
+    with torch.cuda.stream(cs):
+        for n in ("iq", "ik", "q", "k", "v", "beta", "gamma", "mix"):
+            d[n] = host[n].to(dev, non_blocking=True)
+            ev[n] = torch.cuda.Event()
+            ev[n].record(cs)
+    for t in d.values():
+        t.record_stream(comp)
+    B, T, H, D = q.shape
+    DI = iq.shape[-1]
+    fused = (q.dtype == torch.bfloat16 and D == 128 and DI == 64 and T < 65536)
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    if not fused:
+        comp.wait_event(ev["mix"])
+        res = sgsa_layer_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"], d["ik"],
+                             d["mix"], top_k)
+        out.copy_(res, non_blocking=True)
+        return out
+    comp.wait_event(ev["ik"])
+    thr = indexer_thresholds(d["iq"], d["ik"], top_k)
+    comp.wait_event(ev["gamma"])
+    od, _ = chunk_sgsa_fp32_state(d["q"], d["k"], d["v"], d["beta"], d["gamma"], out_f32=True)
+    comp.wait_event(ev["mix"])
+    # attention batch by batch; each batch's output returns while the next one runs
+    res = torch.empty_like(d["q"])
+    for bi in range(B):
+        sl = slice(bi, bi + 1)
+        res[sl] = sparse_attn_thresholds(d["q"][sl], d["k"][sl], d["v"][sl], d["iq"][sl],
+                                         d["ik"][sl], thr[sl], od[sl], d["mix"][sl])
+        done = torch.cuda.Event()
+        done.record(comp)
+        cs.wait_event(done)
+        with torch.cuda.stream(cs):
+            out[sl].copy_(res[sl], non_blocking=True)
+    res.record_stream(cs)
+    comp.wait_stream(cs)
+    return out

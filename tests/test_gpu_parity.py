@@ -302,3 +302,14 @@ def test_layer_fused_attention_with_exact_score_ties(monkeypatch):
     gather, idx = ops.sgsa_layer_fwd(*args, return_indices=True)
     np.testing.assert_array_equal(idx.cpu().numpy(), oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k))
     assert oracle.rel_l2(fused.float().cpu().numpy(), gather.float().cpu().numpy()) < 2e-3
+
+
+def test_layer_from_host_matches_device_call():
+    cfg = CONFIGS["b200_bf16"].scaled(name="host", B=2, T=1024, H=2, top_k=128)
+    x = make_inputs(cfg, seed=6)
+    names = ["q", "k", "v", "beta", "gamma", "iq", "ik", "mix"]
+    host = [x[n].pin_memory() for n in names]
+    got = ops.sgsa_layer_fwd_from_host(*host, cfg.top_k)
+    torch.cuda.synchronize()
+    want = ops.sgsa_layer_fwd(*[x[n].cuda() for n in names], cfg.top_k).cpu()
+    assert torch.equal(got, want)
