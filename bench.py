@@ -148,34 +148,23 @@ def barrier(ws):
     torch.cuda.synchronize()
 
 
-def cpu_reference(cfg, cores: int, budget_s: float = 20.0):
-    """Time the oracle port on a bounded sample; returns (tokens/s, sample text, seconds)."""
+def cpu_reference(cfg, cores: int):
+    """Time the oracle port on batch row 0 of the workload (all heads, all T queries:
+    exactly 1/B of it) with `cores` threads; returns (tokens/s, sample text, seconds)."""
     from oracle import oracle
     from sgsa_b200.inputs import make_inputs
 
     oracle.set_num_threads(cores)
-    small = cfg.scaled(B=1)
-    x = make_inputs(small, seed=0)
-    hs = min(cfg.H, max(1, cores))
+    x = make_inputs(cfg.scaled(B=1), seed=0)
     t0 = time.perf_counter()
-    oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], heads=(0, hs))
-    t_delta = (time.perf_counter() - t0) / hs * cores  # core-seconds per (b,h)
-    nq = 512
-    mid = cfg.T // 2
-    tr = (mid - nq // 2, mid + nq // 2)
-    t0 = time.perf_counter()
-    idx = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k, t_range=tr)
-    od = torch.zeros(1, cfg.T, cfg.H, cfg.D)
-    oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx, od, x["mix"], t_range=tr)
-    t_sel = time.perf_counter() - t0  # all H heads, nq queries, in parallel
-    # queries around T/2 have the mean causal prefix, so work scales by T/nq
-    per_bh_sel = t_sel * cores / cfg.H * (cfg.T / nq)
-    total_core_s = cfg.B * cfg.H * (t_delta + per_bh_sel)
-    wall = total_core_s / cores
-    sample = (f"delta: b0 heads 0..{hs - 1} full T={cfg.T}; indexer+attention+gate: b0 all "
-              f"{cfg.H} heads, queries [{tr[0]},{tr[1]}) (mean causal prefix) scaled by T/{nq}; "
-              f"extrapolated to B={cfg.B} H={cfg.H} at {cores} threads")
-    return cfg.tokens / wall, sample, t_delta * hs / cores + t_sel
+    od, _ = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"])
+    idx = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k)
+    oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx, od, x["mix"])
+    secs = time.perf_counter() - t0
+    sample = (f"batch row 0 of the workload (T={cfg.T}, all {cfg.H} heads, every query: delta "
+              f"recurrence, causal top-{cfg.top_k} indexer, sparse attention, gate), float64, "
+              f"{cores} threads; tokens/s = T / seconds")
+    return cfg.T / secs, sample, secs
 
 
 def run_reference(args, ws, rank):
@@ -186,9 +175,9 @@ def run_reference(args, ws, rank):
     cfg = CONFIGS[CONFIG_NAME]
     cores = os.cpu_count() or 1
     vals, sample = [], ""
-    for _ in range(max(args.warmup, 0)):
-        pass  # the CPU port has no warm-up effects worth a full step
-    for _ in range(max(args.steps, 1)):
+    # every step is one batch row of the workload (~10 s of CPU work); at most 3 are
+    # timed so that the run stays within a few minutes whatever --steps is
+    for _ in range(min(max(args.steps, 1), 3)):
         v, sample, _ = cpu_reference(cfg, cores)
         vals.append(v)
     v = statistics.median(vals)
