@@ -168,6 +168,43 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
                    int B, int T, int H, int D, int DI, int top_k, int mix_per_channel,
                    int dtype, void *workspace, size_t workspace_bytes, void *stream);
 
+/*
+ * Token-by-token SGSA recurrence (forward): the semantics of
+ * naive_recurrent_sgsa (modelings/sgsa_ops/naive.py:39-55).  Replaces the
+ * forward of fused_recurrent_sgsa (modelings/sgsa_ops/recurrent.py:138-175,
+ * Triton kernel recurrent_fwd_triton.py:19-87).  Same arguments and flags as
+ * sgsa_chunk_fwd without the workspace; D in {32, 64, 128}.  With T = 1 it is
+ * the decode step of the delta stage (state read and written once).
+ */
+int sgsa_recurrent_fwd(const void *q, const void *k, const void *v, const void *beta,
+                       const void *gamma, const void *sparse_k, const void *sparse_v,
+                       const void *alpha, const float *initial_state, void *o,
+                       float *final_state, int B, int T, int H, int D, int dtype, int flags,
+                       void *stream);
+
+/*
+ * Decode-time indexer: for each (b, h), the top-k of iq[b,h] . ik_cache[b,j,h]
+ * over the cache positions j < n (the current token included), ties to the
+ * lowest j, ascending, -1 padded.  iq [B,H,DI]; ik_cache [B,Tc,H,DI] (Tc the
+ * allocated cache length, n <= Tc and n <= 57344).  The decode form of the
+ * selection of modelings/hybrid_dense_delta_topk.py:343-349, which the
+ * reference re-scores against the whole cache at every step (:343-349 with
+ * the cache of :226-230).
+ */
+int sgsa_decode_topk(const void *iq, const void *ik_cache, int32_t *indices, int B, int H,
+                     int Tc, int n, int DI, int top_k, int dtype, void *stream);
+
+/*
+ * Decode-time sparse attention + gate for one query per (b, h) over its
+ * selected cache rows (modelings/hybrid_dense_delta_topk.py:350-356, :389-390).
+ * q, o_delta (float32), mix, out: [B,H,D] (mix may be [B,H]); k_cache,
+ * v_cache [B,Tc,H,D]; indices [B,H,K] as written by sgsa_decode_topk.
+ */
+int sgsa_decode_attn_mix(const void *q, const void *k_cache, const void *v_cache,
+                         const int32_t *indices, const float *o_delta, const void *mix, void *out,
+                         int B, int H, int Tc, int D, int top_k, float scale, int mix_per_channel,
+                         int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

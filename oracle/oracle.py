@@ -145,3 +145,47 @@ def rel_l2(a, b) -> float:
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def decode_topk(iq, ik_cache, n, k, return_kth=False):
+    """Top-k rows (ascending, -1 padded) of iq [B,H,DI] . ik_cache[:, :n] [B,Tc,H,DI],
+    float64 scores, ties to the lowest row: the decode form of the selection of
+    modelings/hybrid_dense_delta_topk.py:343-349 against the cache (:226-230)."""
+    iq = np.asarray(_f32(iq), np.float64)
+    ikc = np.asarray(_f32(ik_cache), np.float64)[:, :n]
+    s = np.einsum("bhd,bjhd->bhj", iq, ikc)
+    B, H, _ = s.shape
+    out = np.full((B, H, k), -1, np.int32)
+    kth = np.empty((B, H))
+    for b in range(B):
+        for h in range(H):
+            order = np.lexsort((np.arange(n), -s[b, h]))  # score desc, index asc
+            m = min(k, n)
+            sel = np.sort(order[:m])
+            out[b, h, :m] = sel
+            kth[b, h] = s[b, h, order[m - 1]]
+    return (out, kth) if return_kth else out
+
+
+def decode_attn_mix(q, k_cache, v_cache, idx, o_delta=None, mix=None, scale=None):
+    """Softmax attention of q [B,H,D] over the selected cache rows, then the gate
+    (modelings/hybrid_dense_delta_topk.py:350-356, :389-390), float64."""
+    q = np.asarray(_f32(q), np.float64)
+    kc = np.asarray(_f32(k_cache), np.float64)
+    vc = np.asarray(_f32(v_cache), np.float64)
+    B, H, D = q.shape
+    sc = float(scale) if scale is not None else 1.0 / np.sqrt(D)
+    out = np.zeros((B, H, D))
+    for b in range(B):
+        for h in range(H):
+            sel = idx[b, h][idx[b, h] >= 0]
+            s = kc[b, sel, h] @ q[b, h] * sc
+            p = np.exp(s - s.max())
+            out[b, h] = (p / p.sum()) @ vc[b, sel, h]
+    if o_delta is not None:
+        od = np.asarray(_f32(o_delta), np.float64)
+        m = np.asarray(_f32(mix), np.float64) if mix is not None else np.ones((B, H))
+        if m.ndim == 2:
+            m = m[..., None]
+        out = m * out + (1.0 - m) * od
+    return out

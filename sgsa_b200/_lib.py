@@ -33,6 +33,9 @@ SIGNATURES = {
     "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_indexer_thresholds": (_i, [_vp] * 4 + [_i] * 5 + [_vp]),
     "sgsa_sparse_attn_thresholds": (_i, [_vp] * 9 + [_i] * 5 + [ctypes.c_float, _i, _vp]),
+    "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
+    "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),
+    "sgsa_decode_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_layer_fwd_workspace_size": (_sz, [_i] * 6),
     "sgsa_layer_fwd": (_i, [_vp] * 12 + [_i] * 8 + [_vp, _sz, _vp]),
 }

@@ -224,4 +224,55 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_recurrent_fwd(const void *q, const void *k, const void *v, const void *beta,
+                       const void *gamma, const void *sparse_k, const void *sparse_v,
+                       const void *alpha, const float *initial_state, void *o,
+                       float *final_state, int B, int T, int H, int D, int dtype, int flags,
+                       void *stream) {
+    if (B < 0 || T < 0 || H < 0 || !head_dim_ok(D)) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * H == 0) return SGSA_OK;
+    if (T > 0 && (!q || !k || !v || !beta || !gamma || !o)) return SGSA_ERR_NULL;
+    const bool sparse = flags & SGSA_FLAG_HAS_SPARSE;
+    if (sparse && (!sparse_k || !sparse_v || !alpha)) return SGSA_ERR_NULL;
+    if ((flags & SGSA_FLAG_HAS_INIT) && !initial_state) return SGSA_ERR_NULL;
+    if ((flags & SGSA_FLAG_STORE_FINAL) && !final_state) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_recurrent(
+        q, k, v, beta, gamma, sparse ? sparse_k : nullptr, sparse ? sparse_v : nullptr,
+        sparse ? alpha : nullptr, (flags & SGSA_FLAG_HAS_INIT) ? initial_state : nullptr, o,
+        (flags & SGSA_FLAG_STORE_FINAL) ? final_state : nullptr, B, T, H, D, dtype,
+        (flags & SGSA_FLAG_OUT_F32) != 0, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_decode_topk(const void *iq, const void *ik_cache, int32_t *indices, int B, int H,
+                     int Tc, int n, int DI, int top_k, int dtype, void *stream) {
+    if (B < 0 || H < 0 || Tc < 0 || n < 0 || n > Tc || top_k <= 0) return SGSA_ERR_SHAPE;
+    if (DI != 32 && DI != 64 && DI != 128) return SGSA_ERR_SHAPE;
+    if (n > sgsa::decode_max_cache()) return SGSA_ERR_UNSUPPORTED;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * H == 0) return SGSA_OK;
+    if (!iq || !ik_cache || !indices) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_decode_topk(iq, ik_cache, indices, B, H, Tc, n, DI, top_k,
+                                             dtype, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_decode_attn_mix(const void *q, const void *k_cache, const void *v_cache,
+                         const int32_t *indices, const float *o_delta, const void *mix, void *out,
+                         int B, int H, int Tc, int D, int top_k, float scale, int mix_per_channel,
+                         int dtype, void *stream) {
+    if (B < 0 || H < 0 || Tc < 0 || top_k <= 0 || !head_dim_ok(D)) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * H == 0) return SGSA_OK;
+    if (!q || !k_cache || !v_cache || !indices || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_decode_attn(q, k_cache, v_cache, indices, o_delta, mix, out, B,
+                                             H, Tc, D, top_k, scale, mix_per_channel, dtype,
+                                             (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
 }  // extern "C"

@@ -37,6 +37,16 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);
+int decode_max_cache();
+cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const void *beta,
+                             const void *gamma, const void *sk, const void *sv, const void *alpha,
+                             const float *s0, void *o, float *sT, int B, int T, int H, int D,
+                             int dtype, bool out_f32, cudaStream_t st);
+cudaError_t launch_decode_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H,
+                               int Tc, int n, int DI, int K, int dtype, cudaStream_t st);
+cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, const int32_t *idx,
+                               const float *od, const void *mix, void *out, int B, int H, int Tc,
+                               int D, int K, float scale, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_scan_watchdog(cudaStream_t st);
 }  // namespace sgsa
 
@@ -70,5 +80,15 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);
+int decode_max_cache();
+cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const void *beta,
+                             const void *gamma, const void *sk, const void *sv, const void *alpha,
+                             const float *s0, void *o, float *sT, int B, int T, int H, int D,
+                             int dtype, bool out_f32, cudaStream_t st);
+cudaError_t launch_decode_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H,
+                               int Tc, int n, int DI, int K, int dtype, cudaStream_t st);
+cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, const int32_t *idx,
+                               const float *od, const void *mix, void *out, int B, int H, int Tc,
+                               int D, int K, float scale, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_scan_watchdog(cudaStream_t st);
 }  // namespace sgsa

@@ -1,0 +1,352 @@
+// Recurrent SGSA and the decode-time pieces of the layer.
+//
+// * recurrent_sgsa_kernel: the token-by-token recurrence of
+//   modelings/sgsa_ops/naive.py:39-55 (the semantics of fused_recurrent_sgsa,
+//   modelings/sgsa_ops/recurrent.py:138-175, whose Triton forward is
+//   recurrent_fwd_triton.py:19-87).  One CTA per (b, h), one thread per state
+//   column v: the column S[:, v] (D fp32 values) lives in registers for the
+//   whole sequence; each token's k / q / sparse_k are staged in shared memory
+//   and read as broadcasts.  A decode step is the T = 1 case.
+// * decode_topk_kernel: top-k of one query row against an indexer key cache,
+//   the decode form of the causal indexer (one CTA per (b, h); the row's scores
+//   live in shared memory; block-wide radix select; ordered compaction with the
+//   lowest-index tie-break).
+// * decode_attn_kernel: softmax attention of one query over its selected cache
+//   rows plus the gate (one CTA per (b, h), 8 warps split the rows, online
+//   softmax states merged through shared memory).
+#include "common.cuh"
+
+namespace sgsa {
+namespace {
+
+// ---------------------------------------------------------------- recurrence
+template <typename Tin, typename Tout, int D>
+__global__ void __launch_bounds__(D) recurrent_sgsa_kernel(
+    const Tin *__restrict__ q, const Tin *__restrict__ k, const Tin *__restrict__ v,
+    const Tin *__restrict__ beta, const Tin *__restrict__ gamma, const Tin *__restrict__ sk,
+    const Tin *__restrict__ sv, const Tin *__restrict__ alpha, const float *__restrict__ s0,
+    Tout *__restrict__ o, float *__restrict__ sT, int T, int H) {
+    __shared__ __align__(16) float sh[2][3][D];  // [buffer][k | q | sparse_k][d]
+    __shared__ float sc[2][3];                   // [buffer][gamma | beta | alpha]
+    const int e = threadIdx.x, bh = blockIdx.x, b = bh / H, h = bh % H;
+    const bool sparse = sk != nullptr;
+    float col[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) col[d] = s0 ? s0[((size_t)bh * D + d) * D + e] : 0.f;
+    auto stage = [&](int t, int buf) {
+        const size_t row = ((size_t)b * T + t) * H + h;
+        sh[buf][0][e] = to_f32(k[row * D + e]);
+        sh[buf][1][e] = to_f32(q[row * D + e]);
+        if (sparse) sh[buf][2][e] = to_f32(sk[row * D + e]);
+        if (e == 0) {
+            sc[buf][0] = to_f32(gamma[row]);
+            sc[buf][1] = to_f32(beta[row]);
+            sc[buf][2] = sparse ? to_f32(alpha[row]) : 0.f;
+        }
+    };
+    if (T > 0) stage(0, 0);
+    __syncthreads();
+    for (int t = 0; t < T; ++t) {
+        const int buf = t & 1;
+        const size_t row = ((size_t)b * T + t) * H + h;
+        const float vv = to_f32(v[row * D + e]);
+        const float svv = sparse ? to_f32(sv[row * D + e]) : 0.f;
+        if (t + 1 < T) stage(t + 1, buf ^ 1);
+        const float g = sc[buf][0], bt = sc[buf][1], al = sc[buf][2];
+        const float *kk = sh[buf][0], *qq = sh[buf][1], *ss = sh[buf][2];
+        // predictions read the decayed base state gamma * S (both writes read the same base)
+        float pl = 0.f, ps = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) pl = fmaf(col[d], kk[d], pl);
+        if (sparse) {
+#pragma unroll
+            for (int d = 0; d < D; ++d) ps = fmaf(col[d], ss[d], ps);
+        }
+        const float dl = (vv - g * pl) * bt;
+        const float ds = sparse ? (svv - g * ps) * al : 0.f;
+        float out = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+            float x = fmaf(kk[d], dl, g * col[d]);
+            if (sparse) x = fmaf(ss[d], ds, x);
+            col[d] = x;
+            out = fmaf(x, qq[d], out);
+        }
+        o[row * D + e] = from_f32<Tout>(out);
+        __syncthreads();
+    }
+    if (sT) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) sT[((size_t)bh * D + d) * D + e] = col[d];
+    }
+}
+
+// ------------------------------------------------------------- decode top-k
+constexpr int kTopkThreads = 512;
+
+template <typename Tin, int DI>
+__global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
+    const Tin *__restrict__ iq, const Tin *__restrict__ ikc, int32_t *__restrict__ idx, int H,
+    int Tc, int n, int K) {
+    extern __shared__ __align__(16) uint32_t keys[];  // n order-preserving score keys
+    __shared__ uint32_t hist[256];
+    __shared__ int s_scan[kTopkThreads];
+    __shared__ uint32_t s_prefix, s_mask;
+    __shared__ int s_need, s_done;
+    __shared__ float s_q[DI];
+    const int tid = threadIdx.x, bh = blockIdx.x, b = bh / H, h = bh % H;
+    int32_t *out = idx + (size_t)bh * K;
+    if (n <= K) {  // every cached key is selected
+        for (int i = tid; i < K; i += kTopkThreads) out[i] = (i < n) ? i : -1;
+        return;
+    }
+    if (tid < DI) s_q[tid] = to_f32(iq[(size_t)bh * DI + tid]);
+    __syncthreads();
+    for (int j = tid; j < n; j += kTopkThreads) {
+        const Tin *kr = ikc + (((size_t)b * Tc + j) * H + h) * DI;
+        float s = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < DI; ++d) s = fmaf(s_q[d], to_f32(kr[d]), s);
+        keys[j] = float_key(s);
+    }
+    if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = K; s_done = 0; }
+    __syncthreads();
+    for (int shift = 24; shift >= 0 && !s_done; shift -= 8) {
+        for (int i = tid; i < 256; i += kTopkThreads) hist[i] = 0u;
+        __syncthreads();
+        const uint32_t pre = s_prefix, msk = s_mask;
+        for (int j = tid; j < n; j += kTopkThreads) {
+            const uint32_t u = keys[j];
+            if ((u & msk) == pre) atomicAdd(&hist[(u >> shift) & 0xffu], 1u);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            int cum = 0, chosen = 0, cnt = 0;
+            for (int bin = 255; bin >= 0; --bin) {
+                cnt = (int)hist[bin];
+                if (cum + cnt >= s_need) { chosen = bin; break; }
+                cum += cnt;
+            }
+            s_need -= cum;
+            s_prefix |= (uint32_t)chosen << shift;
+            s_mask |= 0xffu << shift;
+            if (cnt == s_need) s_done = 1;
+        }
+        __syncthreads();
+    }
+    // ordered compaction: thread tid owns the contiguous index segment [lo, hi)
+    const uint32_t pre = s_prefix, msk = s_mask;
+    const int need = s_need;
+    const int seg = (n + kTopkThreads - 1) / kTopkThreads;
+    const int lo = min(n, tid * seg), hi = min(n, lo + seg);
+    int gt = 0, eq = 0;
+    for (int j = lo; j < hi; ++j) {
+        const uint32_t m = keys[j] & msk;
+        gt += m > pre;
+        eq += m == pre;
+    }
+    // exclusive scan of the equal counts, then of the output counts
+    s_scan[tid] = eq;
+    __syncthreads();
+    for (int off = 1; off < kTopkThreads; off <<= 1) {
+        const int x = (tid >= off) ? s_scan[tid - off] : 0;
+        __syncthreads();
+        s_scan[tid] += x;
+        __syncthreads();
+    }
+    const int eq_before = s_scan[tid] - eq;
+    const int take_eq = max(0, min(eq, need - eq_before));
+    __syncthreads();
+    s_scan[tid] = gt + take_eq;
+    __syncthreads();
+    for (int off = 1; off < kTopkThreads; off <<= 1) {
+        const int x = (tid >= off) ? s_scan[tid - off] : 0;
+        __syncthreads();
+        s_scan[tid] += x;
+        __syncthreads();
+    }
+    int pos = s_scan[tid] - (gt + take_eq);
+    int taken = 0;
+    for (int j = lo; j < hi; ++j) {
+        const uint32_t m = keys[j] & msk;
+        if (m > pre || (m == pre && taken < take_eq)) {
+            if (m == pre) ++taken;
+            out[pos++] = j;
+        }
+    }
+}
+
+// ------------------------------------------------------- decode attention
+constexpr int kAttnWarps = 8;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(
+    const T *__restrict__ q, const T *__restrict__ kc, const T *__restrict__ vc,
+    const int32_t *__restrict__ idx, const float *__restrict__ od, const T *__restrict__ mix,
+    T *__restrict__ out, int H, int Tc, int K, float scale_log2, int mix_pc) {
+    constexpr int EPL = D / 16;
+    __shared__ float s_m[kAttnWarps * 2], s_l[kAttnWarps * 2];
+    __shared__ float s_acc[kAttnWarps * 2][D];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, half = lane >> 4, hl = lane & 15;
+    const int bh = blockIdx.x, b = bh / H, h = bh % H;
+    const size_t stride = (size_t)H * D;
+    const T *kb = kc + ((size_t)b * Tc * H + h) * D + hl * EPL;
+    const T *vb = vc + ((size_t)b * Tc * H + h) * D + hl * EPL;
+    float qv[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) qv[e] = to_f32(q[(size_t)bh * D + hl * EPL + e]) * scale_log2;
+    const int32_t *ix = idx + (size_t)bh * K;
+    float m = -INFINITY, l = 0.f, acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    // slot s is handled by warp (s / 2) % kAttnWarps, half s % 2; both halves of a
+    // warp run the same number of iterations (the shuffles need the whole warp)
+    for (int base = 2 * warp; base < K; base += 2 * kAttnWarps) {
+        const int s = base + half;
+        const int j = (s < K) ? ix[s] : -1;
+        float d0 = 0.f;
+        float kr[EPL], vr[EPL];
+        if (j >= 0) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) {
+                kr[e] = to_f32(kb[(size_t)j * stride + e]);
+                vr[e] = to_f32(vb[(size_t)j * stride + e]);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) kr[e] = vr[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) d0 = fmaf(qv[e], kr[e], d0);
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) d0 += __shfl_xor_sync(0xffffffffu, d0, off);
+        if (j >= 0) {
+            const float mn = fmaxf(m, d0);
+            const float c = (m == -INFINITY) ? 0.f : exp2f(m - mn);
+            const float p = exp2f(d0 - mn);
+            l = l * c + p;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(p, vr[e], acc[e] * c);
+            m = mn;
+        }
+    }
+    const int slot = warp * 2 + half;
+    if (hl == 0) {
+        s_m[slot] = m;
+        s_l[slot] = l;
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s_acc[slot][hl * EPL + e] = acc[e];
+    __syncthreads();
+    if (threadIdx.x < D) {
+        const int c = threadIdx.x;
+        float mt = -INFINITY;
+        for (int i = 0; i < 2 * kAttnWarps; ++i) mt = fmaxf(mt, s_m[i]);
+        float lt = 0.f, o = 0.f;
+        for (int i = 0; i < 2 * kAttnWarps; ++i) {
+            if (s_m[i] == -INFINITY) continue;
+            const float f = exp2f(s_m[i] - mt);
+            lt += s_l[i] * f;
+            o += s_acc[i][c] * f;
+        }
+        float r = (lt > 0.f) ? o / lt : 0.f;
+        if (od) {
+            const float mm = mix ? to_f32(mix_pc ? mix[(size_t)bh * D + c] : mix[bh]) : 1.f;
+            r = mm * r + (1.f - mm) * od[(size_t)bh * D + c];
+        }
+        out[(size_t)bh * D + c] = from_f32<T>(r);
+    }
+}
+
+template <typename Tin, typename Tout, int D>
+cudaError_t run_rec(const void *q, const void *k, const void *v, const void *beta,
+                    const void *gamma, const void *sk, const void *sv, const void *alpha,
+                    const float *s0, void *o, float *sT, int B, int T, int H, cudaStream_t st) {
+    recurrent_sgsa_kernel<Tin, Tout, D><<<B * H, D, 0, st>>>(
+        (const Tin *)q, (const Tin *)k, (const Tin *)v, (const Tin *)beta, (const Tin *)gamma,
+        (const Tin *)sk, (const Tin *)sv, (const Tin *)alpha, s0, (Tout *)o, sT, T, H);
+    return cudaGetLastError();
+}
+
+template <typename Tin, typename Tout>
+cudaError_t run_rec_d(int D, const void *q, const void *k, const void *v, const void *beta,
+                      const void *gamma, const void *sk, const void *sv, const void *alpha,
+                      const float *s0, void *o, float *sT, int B, int T, int H,
+                      cudaStream_t st) {
+    switch (D) {
+        case 32: return run_rec<Tin, Tout, 32>(q, k, v, beta, gamma, sk, sv, alpha, s0, o, sT, B, T, H, st);
+        case 64: return run_rec<Tin, Tout, 64>(q, k, v, beta, gamma, sk, sv, alpha, s0, o, sT, B, T, H, st);
+        case 128: return run_rec<Tin, Tout, 128>(q, k, v, beta, gamma, sk, sv, alpha, s0, o, sT, B, T, H, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <typename Tin, int DI>
+cudaError_t run_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H, int Tc, int n,
+                     int K, cudaStream_t st) {
+    const size_t smem = (size_t)max(n, 1) * 4;
+    auto kern = decode_topk_kernel<Tin, DI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<B * H, kTopkThreads, smem, st>>>((const Tin *)iq, (const Tin *)ikc, idx, H, Tc, n, K);
+    return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t run_dattn(const void *q, const void *kc, const void *vc, const int32_t *idx,
+                      const float *od, const void *mix, void *out, int B, int H, int Tc, int K,
+                      float scale, int mix_pc, cudaStream_t st) {
+    decode_attn_kernel<T, D><<<B * H, kAttnWarps * 32, 0, st>>>(
+        (const T *)q, (const T *)kc, (const T *)vc, idx, od, (const T *)mix, (T *)out, H, Tc, K,
+        scale * 1.4426950408889634f, mix_pc);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+constexpr int kDecodeMaxCache = 56 * 1024;  // scores of one row in shared memory
+
+int decode_max_cache() { return kDecodeMaxCache; }
+
+cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const void *beta,
+                             const void *gamma, const void *sk, const void *sv, const void *alpha,
+                             const float *s0, void *o, float *sT, int B, int T, int H, int D,
+                             int dtype, bool out_f32, cudaStream_t st) {
+    if (dtype == SGSA_DTYPE_F32)
+        return run_rec_d<float, float>(D, q, k, v, beta, gamma, sk, sv, alpha, s0, o, sT, B, T, H, st);
+    if (out_f32)
+        return run_rec_d<__nv_bfloat16, float>(D, q, k, v, beta, gamma, sk, sv, alpha, s0, o, sT, B, T, H, st);
+    return run_rec_d<__nv_bfloat16, __nv_bfloat16>(D, q, k, v, beta, gamma, sk, sv, alpha, s0, o, sT, B, T, H, st);
+}
+
+cudaError_t launch_decode_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H,
+                               int Tc, int n, int DI, int K, int dtype, cudaStream_t st) {
+    if (dtype == SGSA_DTYPE_F32) {
+        if (DI == 32) return run_topk<float, 32>(iq, ikc, idx, B, H, Tc, n, K, st);
+        if (DI == 64) return run_topk<float, 64>(iq, ikc, idx, B, H, Tc, n, K, st);
+        if (DI == 128) return run_topk<float, 128>(iq, ikc, idx, B, H, Tc, n, K, st);
+    } else {
+        if (DI == 32) return run_topk<__nv_bfloat16, 32>(iq, ikc, idx, B, H, Tc, n, K, st);
+        if (DI == 64) return run_topk<__nv_bfloat16, 64>(iq, ikc, idx, B, H, Tc, n, K, st);
+        if (DI == 128) return run_topk<__nv_bfloat16, 128>(iq, ikc, idx, B, H, Tc, n, K, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, const int32_t *idx,
+                               const float *od, const void *mix, void *out, int B, int H, int Tc,
+                               int D, int K, float scale, int mix_pc, int dtype, cudaStream_t st) {
+    if (dtype == SGSA_DTYPE_F32) {
+        if (D == 32) return run_dattn<float, 32>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
+        if (D == 64) return run_dattn<float, 64>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
+        if (D == 128) return run_dattn<float, 128>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
+    } else {
+        if (D == 32) return run_dattn<__nv_bfloat16, 32>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
+        if (D == 64) return run_dattn<__nv_bfloat16, 64>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
+        if (D == 128) return run_dattn<__nv_bfloat16, 128>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace sgsa

@@ -348,3 +348,131 @@ def sgsa_layer_fwd_from_host(q, k, v, beta, gamma, iq, ik, mix, top_k, device=No
     res.record_stream(cs)
     comp.wait_stream(cs)
     return out
+
+
+def fused_recurrent_sgsa(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    beta: Tensor,
+    gamma: Tensor,
+    sparse_k: Optional[Tensor] = None,
+    sparse_v: Optional[Tensor] = None,
+    alpha: Optional[Tensor] = None,
+    initial_state: Optional[Tensor] = None,
+    output_final_state: bool = False,
+    use_triton: bool = True,
+) -> Tuple[Tensor, Optional[Tensor]]:
+    """Token-by-token SGSA forward with the signature of the reference's
+    ``fused_recurrent_sgsa`` (modelings/sgsa_ops/recurrent.py:138-175): ``o`` in
+    q.dtype and the final state in float32, as its Triton forward returns it
+    (recurrent_fwd_triton.py:120-125).  ``use_triton`` is accepted and ignored."""
+    del use_triton
+    for n, t in (("q", q), ("k", k), ("v", v), ("beta", beta), ("gamma", gamma)):
+        _dev(t, n)
+    _no_grad_check(q, k, v, beta, gamma, sparse_k, sparse_v, alpha, initial_state)
+    B, T, H, D = q.shape
+    dt = _dtype_code(q)
+    has_sparse = sparse_k is not None and sparse_v is not None and alpha is not None
+    cast = lambda t: None if t is None else t.to(device=q.device, dtype=q.dtype).contiguous()
+    args = [q.contiguous()] + [cast(t) for t in (k, v, beta, gamma)]
+    sp = [cast(t) for t in (sparse_k, sparse_v, alpha)] if has_sparse else [None] * 3
+    flags = _lib.FLAG_HAS_SPARSE if has_sparse else 0
+    s0 = None
+    if initial_state is not None:
+        s0 = initial_state.to(device=q.device, dtype=torch.float32).contiguous()
+        flags |= _lib.FLAG_HAS_INIT
+    o = torch.empty_like(args[0])
+    sT = None
+    if output_final_state:
+        sT = torch.empty(B, H, D, D, device=q.device, dtype=torch.float32)
+        flags |= _lib.FLAG_STORE_FINAL
+    st = _lib.load().sgsa_recurrent_fwd(*[_ptr(t) for t in args], *[_ptr(t) for t in sp],
+                                         _ptr(s0), _ptr(o), _ptr(sT), B, T, H, D, dt, flags,
+                                         _stream(q))
+    _lib.check(st, "sgsa_recurrent_fwd")
+    return o, sT
+
+
+def decode_topk(iq: Tensor, ik_cache: Tensor, n: int, top_k: int) -> Tensor:
+    """Top-k of ``iq [B, H, DI]`` against the first ``n`` rows of ``ik_cache
+    [B, Tc, H, DI]`` -> int32 ``[B, H, top_k]`` (ascending, ties to the lowest row)."""
+    _dev(iq, "iq"), _dev(ik_cache, "ik_cache")
+    B, H, DI = iq.shape
+    Tc = ik_cache.shape[1]
+    out = torch.empty(B, H, top_k, device=iq.device, dtype=torch.int32)
+    st = _lib.load().sgsa_decode_topk(_ptr(iq.contiguous()), _ptr(ik_cache), _ptr(out), B, H, Tc,
+                                       int(n), DI, top_k, _dtype_code(iq), _stream(iq))
+    _lib.check(st, "sgsa_decode_topk")
+    return out
+
+
+def decode_attn_mix(q: Tensor, k_cache: Tensor, v_cache: Tensor, indices: Tensor,
+                    o_delta: Optional[Tensor] = None, mix: Optional[Tensor] = None,
+                    scale: Optional[float] = None) -> Tensor:
+    """Attention of ``q [B, H, D]`` over its selected cache rows, then the gate."""
+    B, H, D = q.shape
+    Tc = k_cache.shape[1]
+    K = indices.shape[-1]
+    out = torch.empty_like(q)
+    od = None if o_delta is None else o_delta.to(torch.float32).contiguous()
+    mx = None if mix is None else mix.to(q.dtype).contiguous()
+    per_channel = int(mx is not None and mx.dim() == 3)
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    st = _lib.load().sgsa_decode_attn_mix(_ptr(q.contiguous()), _ptr(k_cache), _ptr(v_cache),
+                                           _ptr(indices.to(torch.int32).contiguous()), _ptr(od),
+                                           _ptr(mx), _ptr(out), B, H, Tc, D, K, sc, per_channel,
+                                           _dtype_code(q), _stream(q))
+    _lib.check(st, "sgsa_decode_attn_mix")
+    return out
+
+
+class DecodeCache:
+    """Decode-time state of one SGSA layer: the delta-rule state, the K/V and
+    indexer-key caches, and the top-k rows reused between refreshes.
+
+    ``step`` runs one token: recurrent delta step, cache append, indexer top-k
+    (recomputed every ``reuse`` steps and on the first step, reused otherwise --
+    the top-k reuse studied in experiments/attention_topk_reuse_experiment.md:28-46),
+    sparse attention over the selected rows and the gate.
+    """
+
+    def __init__(self, k_cache: Tensor, v_cache: Tensor, ik_cache: Tensor, length: int,
+                 state: Tensor, top_k: int, reuse: int = 1):
+        self.k, self.v, self.ik = k_cache, v_cache, ik_cache
+        self.n = int(length)
+        self.state = state.to(torch.float32).contiguous()
+        self.top_k, self.reuse = int(top_k), max(1, int(reuse))
+        self.steps = 0
+        self.indices = None
+
+    def step(self, q, k, v, beta, gamma, iq, ik, mix):
+        """q, k, v [B, H, D]; beta, gamma [B, H]; iq, ik [B, H, DI]; mix [B, H, D] or [B, H]."""
+        B, H, D = q.shape
+        if self.n >= self.k.shape[1]:
+            raise ValueError("decode cache is full")
+        o_d, self.state = chunk_free_recurrent_step(q, k, v, beta, gamma, self.state)
+        self.k[:, self.n] = k
+        self.v[:, self.n] = v
+        self.ik[:, self.n] = ik
+        self.n += 1
+        if self.indices is None or self.steps % self.reuse == 0:
+            self.indices = decode_topk(iq, self.ik, self.n, self.top_k)
+        self.steps += 1
+        return decode_attn_mix(q, self.k, self.v, self.indices, o_d, mix)
+
+
+def chunk_free_recurrent_step(q, k, v, beta, gamma, state):
+    """One-token delta step: ``(o float32 [B, H, D], new state float32)``."""
+    B, H, D = q.shape
+    st = torch.empty_like(state)
+    o = torch.empty(B, H, D, device=q.device, dtype=torch.float32)
+    dt = _dtype_code(q)
+    cast = lambda t: t.to(q.dtype).contiguous()
+    flags = _lib.FLAG_HAS_INIT | _lib.FLAG_STORE_FINAL | _lib.FLAG_OUT_F32
+    rc = _lib.load().sgsa_recurrent_fwd(_ptr(q.contiguous()), _ptr(cast(k)), _ptr(cast(v)),
+                                         _ptr(cast(beta)), _ptr(cast(gamma)), None, None, None,
+                                         _ptr(state), _ptr(o), _ptr(st), B, 1, H, D, dt, flags,
+                                         _stream(q))
+    _lib.check(rc, "sgsa_recurrent_fwd")
+    return o, st

@@ -1,0 +1,121 @@
+"""Recurrent forward and decode-time ops (through the C ABI) against the oracle.
+
+Tolerances as in test_gpu_parity: relative L2 1e-5 (float32) / 2e-3 (bfloat16);
+index sets exact up to near ties of the k-th score.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from sgsa_b200 import ops
+
+pytestmark = pytest.mark.gpu
+TOL = {torch.float32: 1e-5, torch.bfloat16: 2e-3}
+
+
+def _gen(seed):
+    g = torch.Generator().manual_seed(seed)
+    return lambda *s: torch.randn(*s, generator=g)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("sparse", [False, True])
+def test_fused_recurrent_matches_oracle(dtype, D, sparse):
+    r = _gen(D + sparse)
+    B, T, H = 2, 97, 3
+    x = dict(q=torch.nn.functional.normalize(r(B, T, H, D), dim=-1),
+             k=torch.nn.functional.normalize(r(B, T, H, D), dim=-1), v=r(B, T, H, D),
+             beta=torch.sigmoid(r(B, T, H)),
+             gamma=torch.exp(-torch.nn.functional.softplus(r(B, T, H))))
+    if sparse:
+        x.update(sparse_k=torch.nn.functional.normalize(r(B, T, H, D), dim=-1),
+                 sparse_v=r(B, T, H, D), alpha=0.25 * torch.sigmoid(r(B, T, H)))
+    x = {n: t.to(dtype) for n, t in x.items()}
+    s0 = 0.1 * r(B, H, D, D)
+    o, st = ops.fused_recurrent_sgsa(**{n: t.cuda() for n, t in x.items()},
+                                     initial_state=s0.cuda(), output_final_state=True)
+    ro, rs = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"],
+                                   x.get("sparse_k"), x.get("sparse_v"), x.get("alpha"), s0)
+    assert st.dtype == torch.float32
+    assert oracle.rel_l2(o.float().cpu().numpy(), ro) < TOL[dtype]
+    assert oracle.rel_l2(st.cpu().numpy(), rs) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n,K,DI", [(700, 64, 64), (3000, 1024, 64), (50, 128, 32), (2048, 2048, 128)])
+def test_decode_topk_matches_oracle(dtype, n, K, DI):
+    r = _gen(n + K)
+    B, H, Tc = 2, 3, max(n, 64) + 5
+    iq = r(B, H, DI).to(dtype)
+    ikc = r(B, Tc, H, DI).to(dtype)
+    got = ops.decode_topk(iq.cuda(), ikc.cuda(), n, K).cpu().numpy()
+    want, kth = oracle.decode_topk(iq, ikc, n, K, return_kth=True)
+    if not np.array_equal(got, want):
+        s = np.einsum("bhd,bjhd->bhj", iq.double().numpy(), ikc.double().numpy()[:, :n])
+        for b, h in np.argwhere((got != want).any(-1)):
+            a, w = set(got[b, h].tolist()) - {-1}, set(want[b, h].tolist()) - {-1}
+            assert len(a) == len(w)
+            for j in a ^ w:
+                assert abs(s[b, h, j] - kth[b, h]) <= 1e-5 * max(1.0, abs(kth[b, h]))
+
+
+def test_decode_topk_ties_lowest_index():
+    g = torch.Generator().manual_seed(9)
+    iq = torch.randint(-1, 2, (1, 2, 32), generator=g).float()
+    ikc = torch.randint(-1, 2, (1, 900, 2, 32), generator=g).float()
+    got = ops.decode_topk(iq.cuda(), ikc.cuda(), 900, 40).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle.decode_topk(iq, ikc, 900, 40))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [64, 128])
+def test_decode_attn_matches_oracle(dtype, D):
+    r = _gen(D)
+    B, H, Tc, K, n = 2, 3, 1500, 256, 1200
+    q = torch.nn.functional.normalize(r(B, H, D), dim=-1).to(dtype)
+    kc = torch.nn.functional.normalize(r(B, Tc, H, D), dim=-1).to(dtype)
+    vc = r(B, Tc, H, D).to(dtype)
+    idx = oracle.decode_topk(r(B, H, 32), r(B, Tc, H, 32), n, K)
+    idx[0, 0, 100:] = -1  # a short row
+    od, mix = r(B, H, D), torch.sigmoid(r(B, H, D)).to(dtype)
+    got = ops.decode_attn_mix(q.cuda(), kc.cuda(), vc.cuda(), torch.from_numpy(idx).cuda(),
+                              od.cuda(), mix.cuda())
+    want = oracle.decode_attn_mix(q, kc, vc, idx, od, mix)
+    assert oracle.rel_l2(got.float().cpu().numpy(), want) < TOL[dtype]
+
+
+@pytest.mark.parametrize("reuse", [1, 4])
+def test_decode_cache_steps_match_oracle(reuse):
+    """Several decode steps through DecodeCache against a step-by-step oracle that
+    refreshes the selection on the same steps."""
+    r = _gen(reuse)
+    B, H, D, DI, Tc, n0, K = 2, 2, 128, 64, 600, 500, 64
+    dtype = torch.bfloat16
+    kc = torch.nn.functional.normalize(r(B, Tc, H, D), dim=-1).to(dtype)
+    vc = r(B, Tc, H, D).to(dtype)
+    ikc = r(B, Tc, H, DI).to(dtype)
+    s0 = 0.1 * r(B, H, D, D)
+    cache = ops.DecodeCache(kc.clone().cuda(), vc.clone().cuda(), ikc.clone().cuda(), n0,
+                            s0.cuda(), K, reuse=reuse)
+    state = s0.numpy()
+    kc_o, vc_o, ikc_o = kc.clone(), vc.clone(), ikc.clone()
+    idx = None
+    for step in range(6):
+        q = torch.nn.functional.normalize(r(B, H, D), dim=-1).to(dtype)
+        k = torch.nn.functional.normalize(r(B, H, D), dim=-1).to(dtype)
+        v = r(B, H, D).to(dtype)
+        beta = torch.sigmoid(r(B, H)).to(dtype)
+        gamma = torch.exp(-torch.nn.functional.softplus(r(B, H))).to(dtype)
+        iq, ik = r(B, H, DI).to(dtype), r(B, H, DI).to(dtype)
+        mix = torch.sigmoid(r(B, H, D)).to(dtype)
+        got = cache.step(*(t.cuda() for t in (q, k, v, beta, gamma, iq, ik, mix)))
+        od, state = oracle.sgsa_recurrent(q[:, None], k[:, None], v[:, None], beta[:, None],
+                                          gamma[:, None], initial_state=state)
+        n = n0 + step
+        kc_o[:, n], vc_o[:, n], ikc_o[:, n] = k, v, ik
+        if step % reuse == 0:
+            idx = oracle.decode_topk(iq, ikc_o, n + 1, K)
+        want = oracle.decode_attn_mix(q, kc_o, vc_o, idx, od[:, 0], mix)
+        assert oracle.rel_l2(got.float().cpu().numpy(), want) < 2e-3
