@@ -262,6 +262,60 @@ def stage_times(cfg, d, reps=3, only=None):
     return res
 
 
+def run_decode(args):
+    """decode with top-k reuse over a planted-retrieval cache (1 GPU)."""
+    from sgsa_b200 import ops
+
+    torch.cuda.set_device(0)
+    B, H, D, DI, Tc, K, reuse, nplant = 64, 16, 128, 64, 32768, 1024, 4, 256
+    steps = args.steps
+    n0 = Tc - (args.warmup + steps + 1)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    bf = torch.bfloat16
+    kc = torch.nn.functional.normalize(torch.randn(B, Tc, H, D, device="cuda", generator=g), dim=-1).to(bf)
+    vc = torch.randn(B, Tc, H, D, device="cuda", generator=g).to(bf)
+    ikc = torch.randn(B, Tc, H, DI, device="cuda", generator=g)
+    # 256 planted keys per sequence (x4 scaled) at seeded positions of the prefilled part
+    pos = torch.randint(0, n0, (B, nplant), device="cuda", generator=g)
+    bidx = torch.arange(B, device="cuda")[:, None].expand(B, nplant)
+    ikc[bidx, pos] = 4.0 * torch.randn(B, nplant, H, DI, device="cuda", generator=g)
+    ikc = ikc.to(bf)
+    state = 0.1 * torch.randn(B, H, D, D, device="cuda", generator=g)
+    cache = ops.DecodeCache(kc, vc, ikc, n0, state, K, reuse=reuse)
+    # each step's query is aligned to one planted key of its sequence (chosen per step)
+    targets = pos[torch.arange(B, device="cuda"), torch.randint(0, nplant, (B,), device="cuda", generator=g)]
+
+    def token(i):
+        r = lambda *s: torch.randn(*s, device="cuda", generator=g)
+        q = torch.nn.functional.normalize(r(B, H, D), dim=-1).to(bf)
+        k = torch.nn.functional.normalize(r(B, H, D), dim=-1).to(bf)
+        iq = ikc[torch.arange(B, device="cuda"), targets].clone()
+        return (q, k, r(B, H, D).to(bf), torch.sigmoid(r(B, H)).to(bf),
+                torch.exp(-torch.nn.functional.softplus(r(B, H))).to(bf), iq, r(B, H, DI).to(bf),
+                torch.sigmoid(r(B, H, D)).to(bf))
+
+    toks = [token(i) for i in range(args.warmup + steps)]
+    hits = []
+    for i in range(args.warmup):
+        cache.step(*toks[i])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.warmup, args.warmup + steps):
+        cache.step(*toks[i])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    sel = cache.indices  # [B, H, K]
+    hit = (sel == targets[:, None, None].int()).any(-1).float().mean().item()
+    print(json.dumps({
+        "metric": "SGSA decode tokens/s", "workload": "decode_topk_reuse (configs[4])",
+        "value": B / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+        "warmup": args.warmup, "config": {"batch": B, "cache": Tc, "H": H, "d": D, "d_idx": DI,
+                                          "top_k": K, "reuse": reuse, "planted": nplant},
+        "retrieval_hit_rate": hit, "dtype": "bf16", "data": "synthetic planted retrieval"}))
+
+
 def run_only(args):
     """Run a single stage on a scaled configuration (for ncu captures)."""
     from sgsa_b200.inputs import CONFIGS, make_inputs
@@ -372,12 +426,18 @@ def main():
     ap.add_argument("--only", default=None, choices=["delta", "indexer_topk", "sparse_attn_mix", "indexer_thresholds",
                              "sparse_attn_tc"],
                     help="profiling aid: run one stage --steps times on a (scaled) config, no JSON")
+    ap.add_argument("--workload", default="layer", choices=["layer", "decode"],
+                    help="decode: configs[4] (batch 64, 32768-token cache, top-k 1024 reused "
+                         "every 4 steps, planted retrieval) instead of the layer forward")
     ap.add_argument("--B", type=int, default=None)
     ap.add_argument("--T", type=int, default=None)
     ap.add_argument("--H", type=int, default=None)
     args = ap.parse_args()
     if args.only:
         run_only(args)
+        return
+    if args.workload == "decode":
+        run_decode(args)
         return
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))

@@ -19,6 +19,24 @@
 namespace sgsa {
 namespace {
 
+// Load 8 consecutive elements (16 bytes of bf16, 32 of fp32) as floats.
+__device__ __forceinline__ void load8(const __nv_bfloat16 *p, float *x) {
+    const uint4 r = __ldg(reinterpret_cast<const uint4 *>(p));
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void load8(const float *p, float *x) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
 // ---------------------------------------------------------------- recurrence
 template <typename Tin, typename Tout, int D>
 __global__ void __launch_bounds__(D) recurrent_sgsa_kernel(
@@ -105,8 +123,13 @@ __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
     for (int j = tid; j < n; j += kTopkThreads) {
         const Tin *kr = ikc + (((size_t)b * Tc + j) * H + h) * DI;
         float s = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < DI; ++d) s = fmaf(s_q[d], to_f32(kr[d]), s);
+#pragma unroll
+        for (int d0 = 0; d0 < DI; d0 += 8) {
+            float x[8];
+            load8(kr + d0, x);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s = fmaf(s_q[d0 + i], x[i], s);
+        }
         keys[j] = float_key(s);
     }
     if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = K; s_done = 0; }
@@ -207,10 +230,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(
         float d0 = 0.f;
         float kr[EPL], vr[EPL];
         if (j >= 0) {
+            if constexpr (EPL == 8) {
+                load8(kb + (size_t)j * stride, kr);
+                load8(vb + (size_t)j * stride, vr);
+            } else {
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) {
-                kr[e] = to_f32(kb[(size_t)j * stride + e]);
-                vr[e] = to_f32(vb[(size_t)j * stride + e]);
+                for (int e = 0; e < EPL; ++e) {
+                    kr[e] = to_f32(kb[(size_t)j * stride + e]);
+                    vr[e] = to_f32(vb[(size_t)j * stride + e]);
+                }
             }
         } else {
 #pragma unroll
