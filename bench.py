@@ -229,14 +229,16 @@ def stage_times(cfg, d, reps=3, only=None):
     thr = torch.empty(B, H, T, 4, device="cuda", dtype=torch.int32)
 
     def index_thr():
-        _lib.check(lib.sgsa_indexer_thresholds(P(d["iq"]), P(d["ik"]), None, P(thr), B, T, H,
-                                               cfg.d_idx, cfg.top_k, st.cuda_stream), "indexer")
+        _lib.check(lib.sgsa_indexer_thresholds(P(d["iq"]), P(d["ik"]), None, P(thr), None, 0, B,
+                                               T, H, cfg.d_idx, cfg.top_k, st.cuda_stream),
+                   "indexer")
 
     def attn_tc():
         _lib.check(lib.sgsa_sparse_attn_thresholds(P(d["q"]), P(d["k"]), P(d["v"]), P(d["iq"]),
-                                                   P(d["ik"]), P(thr), P(od), P(d["mix"]), P(out),
-                                                   B, T, H, D, cfg.d_idx, 1.0 / math.sqrt(D), 1,
-                                                   st.cuda_stream), "attn_tc")
+                                                   P(d["ik"]), P(thr), None, 0, P(od), P(d["mix"]),
+                                                   P(out), B, T, H, D, cfg.d_idx,
+                                                   1.0 / math.sqrt(D), 1, 0, st.cuda_stream),
+                   "attn_tc")
 
     res = {}
     # the stages as the layer runs them (fused) and the standalone index/gather pair

@@ -44,7 +44,12 @@ enum {
     SGSA_FLAG_HAS_SPARSE = 1,   /* sparse_k/sparse_v/alpha given: 2 virtual samples per token */
     SGSA_FLAG_HAS_INIT = 2,     /* initial_state given */
     SGSA_FLAG_STORE_FINAL = 4,  /* write final_state */
-    SGSA_FLAG_OUT_F32 = 8       /* o is float32 regardless of dtype */
+    SGSA_FLAG_OUT_F32 = 8,      /* o is float32 regardless of dtype */
+    /* Tensor-core path only (bf16, D == 128, no sparse write): */
+    SGSA_FLAG_TRANSITION = 16,  /* v taken as zero and o not written: final_state = M initial_state,
+                                   M the product of the chunk transitions (sequence-parallel pass) */
+    SGSA_FLAG_REUSE_PREP = 32   /* the workspace holds the per-chunk operands of these same inputs
+                                   from a previous call: only the scan runs */
 };
 
 /* Human-readable text of a status code (static storage). */
@@ -137,24 +142,36 @@ int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int3
  * thresholds[B,H,T][4] = {prefix, mask, cut, 1}: column j <= t is selected iff
  * (key(s_tj) & mask) > prefix, or == prefix and j <= cut, where key() is the
  * order-preserving 32-bit image of the fp32 score.  indices may be NULL.
+ * q_tiles (NULL: all) lists the 128-query tiles to compute, heaviest first;
+ * rows of other tiles are left untouched (sequence-parallel ranks split them).
  * Replaces the selection of modelings/hybrid_dense_delta_topk.py:344-349.
  */
 int sgsa_indexer_thresholds(const void *iq, const void *ik, int32_t *indices,
-                            uint32_t *thresholds, int B, int T, int H, int DI, int top_k,
-                            void *stream);
+                            uint32_t *thresholds, const int32_t *q_tiles, int n_tiles, int B,
+                            int T, int H, int DI, int top_k, void *stream);
 
 /*
  * Sparse attention + gate over the rows selected by threshold records from
  * sgsa_indexer_thresholds, computed on the tensor cores over the causal
- * prefix (bf16, D == 128, DI == 64, T < 65536).  Same result as
- * sgsa_sparse_attn_mix on the equivalent index rows; out is bf16.
+ * prefix (bf16 inputs, D == 128, DI == 64).  Same result as
+ * sgsa_sparse_attn_mix on the equivalent index rows.  out is bf16, or float32
+ * with out_f32; q_tiles as for sgsa_indexer_thresholds.
  * Replaces modelings/hybrid_dense_delta_topk.py:343-356 and :389-390.
  */
 int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, const void *iq,
                                 const void *ik, const uint32_t *thresholds,
-                                const float *o_delta, const void *mix, void *out, int B, int T,
-                                int H, int D, int DI, float scale, int mix_per_channel,
-                                void *stream);
+                                const int32_t *q_tiles, int n_tiles, const float *o_delta,
+                                const void *mix, void *out, int B, int T, int H, int D, int DI,
+                                float scale, int mix_per_channel, int out_f32, void *stream);
+
+/*
+ * The gate alone: out = mix * o_s + (1 - mix) * o_delta over `rows` rows of D
+ * (o_s, o_delta float32; mix [rows, D] or [rows]; out in dtype).  The mix of
+ * modelings/hybrid_dense_delta_topk.py:389-390, used where the two branch
+ * outputs are produced on different ranks.
+ */
+int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void *out,
+                  long long rows, int D, int mix_per_channel, int dtype, void *stream);
 
 /*
  * The composite layer forward: chunked delta stage (no sparse write),

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libsgsa_b200.so")
 SGSA_OK = 0
 DTYPE_F32, DTYPE_BF16 = 0, 1
 FLAG_HAS_SPARSE, FLAG_HAS_INIT, FLAG_STORE_FINAL, FLAG_OUT_F32 = 1, 2, 4, 8
+FLAG_TRANSITION, FLAG_REUSE_PREP = 16, 32
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -31,8 +32,10 @@ SIGNATURES = {
     "sgsa_indexer_topk": (_i, [_vp, _vp, _vp] + [_i] * 6 + [_vp]),
     "sgsa_topk_select": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
-    "sgsa_indexer_thresholds": (_i, [_vp] * 4 + [_i] * 5 + [_vp]),
-    "sgsa_sparse_attn_thresholds": (_i, [_vp] * 9 + [_i] * 5 + [ctypes.c_float, _i, _vp]),
+    "sgsa_indexer_thresholds": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),
+    "sgsa_sparse_attn_thresholds": (_i, [_vp] * 7 + [_i] + [_vp] * 3 + [_i] * 5 +
+                                    [ctypes.c_float, _i, _i, _vp]),
+    "sgsa_gate_mix": (_i, [_vp] * 4 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
     "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),
     "sgsa_decode_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),

@@ -94,6 +94,9 @@ int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta
     if ((flags & SGSA_FLAG_HAS_SPARSE) && (!sparse_k || !sparse_v || !alpha)) return SGSA_ERR_NULL;
     if ((flags & SGSA_FLAG_HAS_INIT) && !initial_state) return SGSA_ERR_NULL;
     if ((flags & SGSA_FLAG_STORE_FINAL) && !final_state) return SGSA_ERR_NULL;
+    if ((flags & (SGSA_FLAG_TRANSITION | SGSA_FLAG_REUSE_PREP)) &&
+        !sgsa::chunk_tc_eligible(D, dtype, flags))
+        return SGSA_ERR_UNSUPPORTED;
     if (int s = check_device()) return s;
     const size_t need = sgsa::chunk_delta_ws_bytes(B, T, H, D, flags);
     if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255)) return SGSA_ERR_WORKSPACE;
@@ -143,31 +146,43 @@ int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int3
 }
 
 int sgsa_indexer_thresholds(const void *iq, const void *ik, int32_t *indices,
-                            uint32_t *thresholds, int B, int T, int H, int DI, int top_k,
-                            void *stream) {
-    if (B < 0 || T < 0 || H < 0 || top_k <= 0) return SGSA_ERR_SHAPE;
+                            uint32_t *thresholds, const int32_t *q_tiles, int n_tiles, int B,
+                            int T, int H, int DI, int top_k, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || top_k <= 0 || n_tiles < 0) return SGSA_ERR_SHAPE;
     if (!sgsa::indexer_tc_eligible(DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
     if ((size_t)B * T * H == 0) return SGSA_OK;
     if (!iq || !ik || !thresholds) return SGSA_ERR_NULL;
     if (int s = check_device()) return s;
     cudaError_t e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thresholds, B, T, H, DI, top_k,
-                                                  (cudaStream_t)stream);
+                                                  q_tiles, n_tiles, (cudaStream_t)stream);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
 int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, const void *iq,
                                 const void *ik, const uint32_t *thresholds,
-                                const float *o_delta, const void *mix, void *out, int B, int T,
-                                int H, int D, int DI, float scale, int mix_per_channel,
-                                void *stream) {
-    if (B < 0 || T < 0 || H < 0) return SGSA_ERR_SHAPE;
+                                const int32_t *q_tiles, int n_tiles, const float *o_delta,
+                                const void *mix, void *out, int B, int T, int H, int D, int DI,
+                                float scale, int mix_per_channel, int out_f32, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || n_tiles < 0) return SGSA_ERR_SHAPE;
     if (!sgsa::sparse_attn_tc_eligible(T, D, DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
     if ((size_t)B * T * H == 0) return SGSA_OK;
     if (!q || !k || !v || !iq || !ik || !thresholds || !out) return SGSA_ERR_NULL;
     if (int s = check_device()) return s;
     cudaError_t e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thresholds, o_delta, mix, out,
-                                                B, T, H, scale, mix_per_channel,
-                                                (cudaStream_t)stream);
+                                                B, T, H, scale, mix_per_channel, q_tiles, n_tiles,
+                                                out_f32 != 0, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void *out,
+                  long long rows, int D, int mix_per_channel, int dtype, void *stream) {
+    if (rows < 0 || D <= 0) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (rows == 0) return SGSA_OK;
+    if (!o_s || !o_delta || !mix || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_gate_mix(o_s, o_delta, mix, out, rows, D, mix_per_channel, dtype,
+                                          (cudaStream_t)stream);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
@@ -211,10 +226,11 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     const float scale = 1.0f / sqrtf((float)D);
     if (fused) {
         // selection exported as per-row thresholds; indices written only if asked for
-        e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, H, DI, top_k, st);
+        e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, H, DI, top_k, nullptr, 0,
+                                          st);
         if (e != cudaSuccess) return fail_cuda(e);
         e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
-                                        mix_per_channel, st);
+                                        mix_per_channel, nullptr, 0, false, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
     e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, H, DI, top_k, dtype, st);

@@ -43,6 +43,7 @@ struct ChunkArgs {
     int B, T, H, NC;
     float *W, *U, *Aqk, *G;
     float *Qt, *KtT;  // tensor-core scan only: exp(G_t) q_t [C x D] and Kap~^T [D x C]
+    int transition;   // tensor-core scan only: v taken as zero, o not written
 };
 
 template <int D, bool SPARSE>
@@ -465,7 +466,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
             const float *Uh = a.U + cix * kC * tc::kD + v;
             float uh[kC];
 #pragma unroll
-            for (int t = 0; t < kC; ++t) uh[t] = Uh[t * tc::kD];
+            for (int t = 0; t < kC; ++t) uh[t] = a.transition ? 0.f : Uh[t * tc::kD];
             mbar_wait(d1done, ph, wd, 16u);
             tc_fence_after();
 #pragma unroll
@@ -495,7 +496,8 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int t = half * 32 + j;
-                    if (t < L) o[(((size_t)b * a.T + t0 + t) * a.H + h) * tc::kD + v] = from_f32<Tout>(d[j]);
+                    if (t < L && !a.transition)
+                        o[(((size_t)b * a.T + t0 + t) * a.H + h) * tc::kD + v] = from_f32<Tout>(d[j]);
                 }
             }
 #pragma unroll
@@ -775,7 +777,7 @@ static bool scan_use_tc() {
 }
 
 template <typename Tout>
-cudaError_t run_tc_scan(const ChunkArgs &a, cudaStream_t st) {
+cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
     const long long nch = (long long)a.B * a.H * a.NC;
     CUtensorMap mw, mq, ma, mk, mkin, mqin, mvin;
     if (!make_tmap_2d_f32(&mw, a.W, 128, nch * 64, 64) ||
@@ -793,9 +795,11 @@ cudaError_t run_tc_scan(const ChunkArgs &a, cudaStream_t st) {
     auto scan = chunk_scan_tc_kernel<Tout>;
     e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmem);
     if (e != cudaSuccess) return e;
-    prep<<<dim3((a.NC + 1) / 2, a.B * a.H), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (!reuse_prep) {
+        prep<<<dim3((a.NC + 1) / 2, a.B * a.H), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     scan<<<a.B * a.H, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
     return cudaGetLastError();
 }
@@ -811,6 +815,11 @@ cudaError_t run_d(int D, const ChunkArgs &a, cudaStream_t st) {
 }
 
 }  // namespace
+
+bool chunk_tc_eligible(int D, int dtype, int flags) {
+    return dtype == SGSA_DTYPE_BF16 && D == 128 && !(flags & SGSA_FLAG_HAS_SPARSE) &&
+           scan_use_tc();
+}
 
 unsigned int read_scan_watchdog(cudaStream_t st) {
     unsigned int v = 0, z = 0;
@@ -860,9 +869,11 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
         a.Qt = tail;
         a.KtT = a.Qt + nchunk * kC * D;
     }
-    if (dtype == SGSA_DTYPE_BF16 && D == 128 && !sparse && scan_use_tc()) {
+    a.transition = (flags & SGSA_FLAG_TRANSITION) ? 1 : 0;
+    if (chunk_tc_eligible(D, dtype, flags)) {
         const bool of32b = (flags & SGSA_FLAG_OUT_F32);
-        return of32b ? run_tc_scan<float>(a, st) : run_tc_scan<__nv_bfloat16>(a, st);
+        const bool reuse = (flags & SGSA_FLAG_REUSE_PREP);
+        return of32b ? run_tc_scan<float>(a, reuse, st) : run_tc_scan<__nv_bfloat16>(a, reuse, st);
     }
     a.Qt = nullptr;
     a.KtT = nullptr;

@@ -35,7 +35,10 @@ bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype);
 cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
-                                  int mix_pc, cudaStream_t st);
+                                  int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
+                                  cudaStream_t st);
+cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
+                            long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);
 int decode_max_cache();
 cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const void *beta,
@@ -58,6 +61,7 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
                                int T, int H, int D, int dtype, int flags, void *ws,
                                cudaStream_t st);
 size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags);
+bool chunk_tc_eligible(int D, int dtype, int flags);
 
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T,
                                 int H, int DI, int K, int dtype, cudaStream_t st);
@@ -67,7 +71,8 @@ unsigned int read_index_watchdog(cudaStream_t st);
 // (key(s_tj) & mask) > prefix, or == prefix and j <= cut.  idx may be NULL.
 bool indexer_tc_eligible(int DI, int dtype);
 cudaError_t launch_indexer_topk_thr(const void *iq, const void *ik, int32_t *idx, uint32_t *thr,
-                                    int B, int T, int H, int DI, int K, cudaStream_t st);
+                                    int B, int T, int H, int DI, int K, const int32_t *q_tiles,
+                                    int n_tiles, cudaStream_t st);
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,
                                int S, int K, cudaStream_t st);
 cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
@@ -78,7 +83,10 @@ bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype);
 cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
-                                  int mix_pc, cudaStream_t st);
+                                  int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
+                                  cudaStream_t st);
+cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
+                            long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);
 int decode_max_cache();
 cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const void *beta,

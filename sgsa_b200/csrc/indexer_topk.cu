@@ -272,12 +272,14 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
 template <int DI, bool PACKED>
 struct TcCfg {
     static constexpr int kKB = DI / 64;                // 128-byte K blocks
-    static constexpr int kN = PACKED ? 64 : 128;       // keys per tile
-    static constexpr int kStages = PACKED ? 3 : 2;
+    // 64-key tiles in both modes: the tensor-core attention recomputes these
+    // scores with the same instruction shapes, which keeps them bit-identical
+    static constexpr int kN = 64;                      // keys per tile
+    static constexpr int kStages = 3;
     static constexpr int kQBytes = 128 * DI * 2;
     static constexpr int kKBytes = kN * DI * 2;
     static constexpr int kHistBytes = (PACKED ? 128 : 256) * kRows * 4;
-    static constexpr int kAcc = PACKED ? 4 : 2;        // TMEM accumulator buffers
+    static constexpr int kAcc = 4;                     // TMEM accumulator buffers
     static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
     static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
     static constexpr int kMinBlocks = (kSmem * 2 + 2048 <= 233472) ? 2 : 1;
@@ -350,7 +352,8 @@ template <int DI, bool PACKED>
 __global__ void __launch_bounds__(TcCfg<DI, PACKED>::kThreads, (TcCfg<DI, PACKED>::kMinBlocks))
 indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx,
-                       uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt) {
+                       uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt,
+                       const int32_t *__restrict__ q_tiles) {
     using C = TcCfg<DI, PACKED>;
     using namespace sm100;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -365,7 +368,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int BH = B * H;
-    const int qt = nqt - 1 - (int)(blockIdx.x / BH);
+    // query tile: an explicit list (heaviest first) or all tiles, heaviest first
+    const int qt = q_tiles ? q_tiles[blockIdx.x / BH] : nqt - 1 - (int)(blockIdx.x / BH);
     const int bh = (int)(blockIdx.x % BH), b = bh / H, h = bh % H;
     const int q0 = qt * kRows;
     const int q_last = min(T - 1, q0 + kRows - 1);
@@ -558,7 +562,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 
 template <int DI, bool PACKED>
 cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T, int H,
-                   int K, cudaStream_t st) {
+                   int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st) {
     using C = TcCfg<DI, PACKED>;
     CUtensorMap mq, mk;
     if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
@@ -569,16 +573,18 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int
                                          (int)C::kSmem);
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRows);
-    kern<<<nqt * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, thr, B, T, H, K, nqt);
+    const int ntiles = q_tiles ? n_tiles : nqt;
+    if (ntiles <= 0) return cudaSuccess;
+    kern<<<ntiles * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, thr, B, T, H, K, nqt, q_tiles);
     return cudaGetLastError();
 }
 
 template <int DI>
 cudaError_t run_tc_t(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T,
-                     int H, int K, cudaStream_t st) {
+                     int H, int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st) {
     // 16-bit counters hold any count below 65536, the longest row they can see.
-    if (T < 65536) return run_tc<DI, true>(iq, ik, idx, thr, B, T, H, K, st);
-    return run_tc<DI, false>(iq, ik, idx, thr, B, T, H, K, st);
+    if (T < 65536) return run_tc<DI, true>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st);
+    return run_tc<DI, false>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st);
 }
 
 template <typename Tin, int DI>
@@ -612,9 +618,10 @@ bool indexer_tc_eligible(int DI, int dtype) {
 }
 
 cudaError_t launch_indexer_topk_thr(const void *iq, const void *ik, int32_t *idx, uint32_t *thr,
-                                    int B, int T, int H, int DI, int K, cudaStream_t st) {
-    if (DI == 64) return run_tc_t<64>(iq, ik, idx, (uint4 *)thr, B, T, H, K, st);
-    if (DI == 128) return run_tc_t<128>(iq, ik, idx, (uint4 *)thr, B, T, H, K, st);
+                                    int B, int T, int H, int DI, int K, const int32_t *q_tiles,
+                                    int n_tiles, cudaStream_t st) {
+    if (DI == 64) return run_tc_t<64>(iq, ik, idx, (uint4 *)thr, B, T, H, K, q_tiles, n_tiles, st);
+    if (DI == 128) return run_tc_t<128>(iq, ik, idx, (uint4 *)thr, B, T, H, K, q_tiles, n_tiles, st);
     return cudaErrorInvalidValue;
 }
 
@@ -622,8 +629,8 @@ cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, in
                                 int DI, int K, int dtype, cudaStream_t st) {
     if (dtype == SGSA_DTYPE_F32) return run_simt_d<float>(DI, iq, ik, idx, B, T, H, K, st);
     if (indexer_use_tc()) {
-        if (DI == 64) return run_tc_t<64>(iq, ik, idx, nullptr, B, T, H, K, st);
-        if (DI == 128) return run_tc_t<128>(iq, ik, idx, nullptr, B, T, H, K, st);
+        if (DI == 64) return run_tc_t<64>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st);
+        if (DI == 128) return run_tc_t<128>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st);
     }
     return run_simt_d<__nv_bfloat16>(DI, iq, ik, idx, B, T, H, K, st);
 }

@@ -11,6 +11,8 @@
 // warp keeps up to 16 k rows and 16 v rows in flight; the score is reduced over the
 // half-warp with shuffles, and each half keeps its own online-softmax state
 // (running max, sum, accumulator) that the two halves merge at the end.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace sgsa {
@@ -241,6 +243,31 @@ cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
     if (dtype == SGSA_DTYPE_F32)
         return run_d<float>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, st);
     return run_d<__nv_bfloat16>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, st);
+}
+
+namespace {
+template <typename T>
+__global__ void gate_mix_kernel(const float *__restrict__ os, const float *__restrict__ od,
+                                const T *__restrict__ mix, T *__restrict__ out, long long n, int D,
+                                int mix_pc) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float m = to_f32(mix_pc ? mix[i] : mix[i / D]);
+        out[i] = from_f32<T>(m * os[i] + (1.f - m) * od[i]);
+    }
+}
+}  // namespace
+
+cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
+                            long long rows, int D, int mix_pc, int dtype, cudaStream_t st) {
+    const long long n = rows * D;
+    const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+    if (dtype == SGSA_DTYPE_F32)
+        gate_mix_kernel<float><<<grid, 256, 0, st>>>(os, od, (const float *)mix, (float *)out, n, D, mix_pc);
+    else
+        gate_mix_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(os, od, (const __nv_bfloat16 *)mix,
+                                                             (__nv_bfloat16 *)out, n, D, mix_pc);
+    return cudaGetLastError();
 }
 
 }  // namespace sgsa

@@ -53,7 +53,7 @@ constexpr int kBytes = kBar + 256 + 2 * kParts * 128 * 4;  // barriers | tile ma
 constexpr size_t kSmem = 1024 + kBytes;
 }  // namespace L
 
-template <typename Tmix>
+template <typename Tmix, typename Tout>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
@@ -61,8 +61,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_iq,
                       const __grid_constant__ CUtensorMap tm_ik, const uint4 *__restrict__ thr,
                       const float *__restrict__ od, const Tmix *__restrict__ mix,
-                      __nv_bfloat16 *__restrict__ out, int B, int T, int H, float scale_log2,
-                      int mix_pc, int nqt) {
+                      Tout *__restrict__ out, int B, int T, int H, float scale_log2,
+                      int mix_pc, int nqt, const int32_t *__restrict__ q_tiles) {
     using namespace sm100;
     constexpr int D = 128;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -76,7 +76,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int BH = B * H;
-    const int qt = nqt - 1 - (int)(blockIdx.x / BH);
+    const int qt = q_tiles ? q_tiles[blockIdx.x / BH] : nqt - 1 - (int)(blockIdx.x / BH);
     const int bh = (int)(blockIdx.x % BH), b = bh / H, h = bh % H;
     const int q0 = qt * kRowsA;
     const int q_last = min(T - 1, q0 + kRowsA - 1);
@@ -288,7 +288,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             const int c0 = part * kOP;
             tmem_ld32(tO + lrow + c0, o);
             if (valid_row) {
-                __nv_bfloat16 *dst = out + rowq * D + c0;
+                Tout *dst = out + rowq * D + c0;
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     float r0 = o[i] * inv, r1 = o[i + 1] * inv;
@@ -299,7 +299,11 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         r0 = m0 * r0 + (1.f - m0) * od[e];
                         r1 = m1 * r1 + (1.f - m1) * od[e + 1];
                     }
-                    *reinterpret_cast<__nv_bfloat162 *>(dst + i) = __floats2bfloat162_rn(r0, r1);
+                    if constexpr (sizeof(Tout) == 2) {
+                        *reinterpret_cast<__nv_bfloat162 *>(dst + i) = __floats2bfloat162_rn(r0, r1);
+                    } else {
+                        *reinterpret_cast<float2 *>(dst + i) = make_float2(r0, r1);
+                    }
                 }
             }
         }
@@ -313,13 +317,15 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 }  // namespace
 
 bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype) {
-    return dtype == SGSA_DTYPE_BF16 && D == 128 && DI == 64 && T < 65536;
+    (void)T;
+    return dtype == SGSA_DTYPE_BF16 && D == 128 && DI == 64;
 }
 
 cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
-                                  int mix_pc, cudaStream_t st) {
+                                  int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
+                                  cudaStream_t st) {
     CUtensorMap mq, mk, mv, miq, mik;
     if (!make_tmap_rows_bf16(&mq, q, B, T, H, 128, 128) ||
         !make_tmap_rows_bf16(&mk, k, B, T, H, 128, kNk) ||
@@ -327,14 +333,27 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         !make_tmap_rows_bf16(&miq, iq, B, T, H, 64, 128) ||
         !make_tmap_rows_bf16(&mik, ik, B, T, H, 64, kNk))
         return cudaErrorInvalidValue;
-    auto kern = sparse_attn_tc_kernel<__nv_bfloat16>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)L::kSmem);
-    if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRowsA);
-    kern<<<nqt * B * H, kAttnThreads, L::kSmem, st>>>(mq, mk, mv, miq, mik, (const uint4 *)thr, od,
-                                             (const __nv_bfloat16 *)mix, (__nv_bfloat16 *)out,
-                                             B, T, H, scale * 1.4426950408889634f, mix_pc, nqt);
+    const int ntiles = q_tiles ? n_tiles : nqt;
+    if (ntiles <= 0) return cudaSuccess;
+    const float sl = scale * 1.4426950408889634f;
+    if (out_f32) {
+        auto kern = sparse_attn_tc_kernel<__nv_bfloat16, float>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)L::kSmem);
+        if (e != cudaSuccess) return e;
+        kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
+            mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
+            (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles);
+    } else {
+        auto kern = sparse_attn_tc_kernel<__nv_bfloat16, __nv_bfloat16>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)L::kSmem);
+        if (e != cudaSuccess) return e;
+        kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
+            mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
+            (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles);
+    }
     return cudaGetLastError();
 }
 

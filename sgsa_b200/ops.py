@@ -259,33 +259,45 @@ def sgsa_layer_fwd(q: Tensor, k: Tensor, v: Tensor, beta: Tensor, gamma: Tensor,
     return res[0] if len(res) == 1 else tuple(res)
 
 
-def indexer_thresholds(iq: Tensor, ik: Tensor, top_k: int, return_indices: bool = False):
+def indexer_thresholds(iq: Tensor, ik: Tensor, top_k: int, return_indices: bool = False,
+                       q_tiles: Optional[Tensor] = None, out: Optional[Tensor] = None):
     """Tensor-core indexer (bf16, DI 64/128) returning the exact per-row selection as
     threshold records int32 ``[B, H, T, 4]`` (see include/sgsa_b200.h), plus the
-    index rows if asked for."""
+    index rows if asked for.  ``q_tiles`` (int32, heaviest first) restricts the
+    work to those 128-query tiles; ``out`` receives the records."""
     _dev(iq, "iq"), _dev(ik, "ik")
     B, T, H, DI = iq.shape
     iq_, ik_ = iq.contiguous(), ik.to(iq.dtype).contiguous()
-    thr = torch.empty(B, H, T, 4, device=iq.device, dtype=torch.int32)
+    thr = out if out is not None else torch.empty(B, H, T, 4, device=iq.device, dtype=torch.int32)
     ix = torch.empty(B, H, T, top_k, device=iq.device, dtype=torch.int32) if return_indices else None
-    st = _lib.load().sgsa_indexer_thresholds(_ptr(iq_), _ptr(ik_), _ptr(ix), _ptr(thr), B, T, H,
-                                              DI, top_k, _stream(iq))
+    qt = None if q_tiles is None else q_tiles.to(device=iq.device, dtype=torch.int32).contiguous()
+    nt = 0 if qt is None else qt.numel()
+    st = _lib.load().sgsa_indexer_thresholds(_ptr(iq_), _ptr(ik_), _ptr(ix), _ptr(thr), _ptr(qt),
+                                              nt, B, T, H, DI, top_k, _stream(iq))
     _lib.check(st, "sgsa_indexer_thresholds")
     return (thr, ix) if return_indices else thr
 
 
-def sparse_attn_thresholds(q, k, v, iq, ik, thresholds, o_delta=None, mix=None, scale=None):
-    """Tensor-core sparse attention + gate over the rows selected by ``thresholds``."""
+def sparse_attn_thresholds(q, k, v, iq, ik, thresholds, o_delta=None, mix=None, scale=None,
+                           q_tiles: Optional[Tensor] = None, out: Optional[Tensor] = None,
+                           out_f32: bool = False):
+    """Tensor-core sparse attention + gate over the rows selected by ``thresholds``
+    (bf16 output, or float32 with ``out_f32``); ``q_tiles`` as for indexer_thresholds."""
     B, T, H, D = q.shape
     DI = iq.shape[-1]
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty(q.shape, device=q.device,
+                          dtype=torch.float32 if out_f32 else q.dtype)
     od = None if o_delta is None else o_delta.to(torch.float32).contiguous()
     mx = None if mix is None else mix.to(q.dtype).contiguous()
     per_channel = int(mx is not None and mx.dim() == 4)
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    qt = None if q_tiles is None else q_tiles.to(device=q.device, dtype=torch.int32).contiguous()
+    nt = 0 if qt is None else qt.numel()
     st = _lib.load().sgsa_sparse_attn_thresholds(
-        _ptr(q), _ptr(k), _ptr(v), _ptr(iq), _ptr(ik), _ptr(thresholds), _ptr(od), _ptr(mx),
-        _ptr(out), B, T, H, D, DI, sc, per_channel, _stream(q))
+        _ptr(q), _ptr(k), _ptr(v), _ptr(iq), _ptr(ik), _ptr(thresholds), _ptr(qt), nt, _ptr(od),
+        _ptr(mx), _ptr(out), B, T, H, D, DI, sc, per_channel, int(out.dtype == torch.float32),
+        _stream(q))
     _lib.check(st, "sgsa_sparse_attn_thresholds")
     return out
 
@@ -320,7 +332,7 @@ def sgsa_layer_fwd_from_host(q, k, v, beta, gamma, iq, ik, mix, top_k, device=No
         t.record_stream(comp)
     B, T, H, D = q.shape
     DI = iq.shape[-1]
-    fused = (q.dtype == torch.bfloat16 and D == 128 and DI == 64 and T < 65536)
+    fused = (q.dtype == torch.bfloat16 and D == 128 and DI == 64)
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
     if not fused:
@@ -476,3 +488,16 @@ def chunk_free_recurrent_step(q, k, v, beta, gamma, state):
                                          _stream(q))
     _lib.check(rc, "sgsa_recurrent_fwd")
     return o, st
+
+
+def gate_mix(o_s: Tensor, o_delta: Tensor, mix: Tensor, dtype=torch.bfloat16) -> Tensor:
+    """out = mix * o_s + (1 - mix) * o_delta (o_s, o_delta float32 [..., D])."""
+    D = o_s.shape[-1]
+    rows = o_s.numel() // D
+    out = torch.empty(o_s.shape, device=o_s.device, dtype=dtype)
+    mx = mix.to(dtype).contiguous()
+    per_channel = int(mx.numel() == o_s.numel())
+    st = _lib.load().sgsa_gate_mix(_ptr(o_s.contiguous()), _ptr(o_delta.contiguous()), _ptr(mx),
+                                    _ptr(out), rows, D, per_channel, _DT[dtype], _stream(o_s))
+    _lib.check(st, "sgsa_gate_mix")
+    return out
