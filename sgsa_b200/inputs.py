@@ -71,3 +71,20 @@ def make_inputs(cfg: LayerConfig, seed: int = 0, device="cpu"):
     if device != "cpu":
         out = {n: t.to(device) for n, t in out.items()}
     return out
+
+
+def make_inputs_slice(cfg: LayerConfig, t0: int, t1: int, seed: int = 0, block: int = 1024,
+                      device="cpu"):
+    """Tokens [t0, t1) of a long input drawn block by block: block i of `block`
+    tokens comes from its own generator seeded (seed, i), with the distributions
+    of ``make_inputs``.  Any slicing into whole blocks gives identical data, so
+    every GPU count of a sequence-parallel run sees the same sequence."""
+    if t0 % block or t1 % block:
+        raise ValueError("slice bounds must be multiples of the block")
+    parts = []
+    for i in range(t0 // block, t1 // block):
+        parts.append(make_inputs(replace(cfg, T=block), seed=seed * 1000003 + i))
+    out = {n: torch.cat([p[n] for p in parts], dim=1) for n in parts[0]}
+    if device != "cpu":
+        out = {n: t.to(device) for n, t in out.items()}
+    return out
