@@ -138,6 +138,9 @@ def _gather_seq(x: Tensor, world: int, group) -> Tensor:
     return buf.transpose(0, 1).reshape(x.shape[0], world * x.shape[1], *x.shape[2:])
 
 
+_delta_streams = {}
+
+
 def sp_layer_fwd(q, k, v, beta, gamma, iq, ik, mix, top_k, group=None,
                  output_final_state: bool = False):
     """Sequence-parallel layer forward on an NCCL process group.  Inputs are this
@@ -150,22 +153,24 @@ def sp_layer_fwd(q, k, v, beta, gamma, iq, ik, mix, top_k, group=None,
     rank = dist.get_rank(group)
     B, Tl, H, D = q.shape
     T = Tl * world
-    comm = torch.cuda.Stream(q.device)
     comp = torch.cuda.current_stream(q.device)
-    # keys for the attention: gathered on a side stream while the delta stage runs
-    comm.wait_stream(comp)
-    with torch.cuda.stream(comm):
-        full = [_gather_seq(t, world, group) for t in (q, k, v, iq, ik)]
-    delta = _Delta(q, k, v, beta, gamma)
-    h, M = delta.pass1()
-    hm = torch.stack([h, M])
-    allhm = torch.empty((world,) + tuple(hm.shape), dtype=hm.dtype, device=hm.device)
-    dist.all_gather_into_tensor(allhm, hm, group=group)
-    s_in = fold_states([allhm[r, 1] for r in range(world)], [allhm[r, 0] for r in range(world)])
-    o_delta, s_last = delta.pass2(s_in[rank])
-    comp.wait_stream(comm)
-    for t in full:
-        t.record_stream(comp)
+    dstream = _delta_streams.get(q.device.index)
+    if dstream is None:
+        dstream = _delta_streams[q.device.index] = torch.cuda.Stream(q.device)
+    # the delta stage runs on its own stream, beside the gathers, the indexer and the
+    # attention; it only joins at the gate
+    dstream.wait_stream(comp)
+    # keys for the attention (the collective makes the compute stream wait for it)
+    full = [_gather_seq(t, world, group) for t in (q, k, v, iq, ik)]
+    with torch.cuda.stream(dstream):
+        delta = _Delta(q, k, v, beta, gamma)
+        h, M = delta.pass1()
+        hm = torch.stack([h, M])
+        allhm = torch.empty((world,) + tuple(hm.shape), dtype=hm.dtype, device=hm.device)
+        dist.all_gather_into_tensor(allhm, hm, group=group)
+        s_in = fold_states([allhm[r, 1] for r in range(world)],
+                           [allhm[r, 0] for r in range(world)])
+        o_delta, s_last = delta.pass2(s_in[rank])
     fq, fk, fv, fiq, fik = full
     thr = torch.empty(B, H, T, 4, device=q.device, dtype=torch.int32)
     o_s = torch.zeros(B, T, H, D, device=q.device, dtype=torch.float32)
@@ -174,6 +179,8 @@ def sp_layer_fwd(q, k, v, beta, gamma, iq, ik, mix, top_k, group=None,
     o_parts = o_s.view(B, world, Tl, H, D).transpose(0, 1).contiguous()
     mine = torch.empty(B, Tl, H, D, device=q.device, dtype=torch.float32)
     dist.reduce_scatter_tensor(mine, o_parts, group=group)
+    comp.wait_stream(dstream)
+    o_delta.record_stream(comp)
     out = ops.gate_mix(mine, o_delta, mix, q.dtype)
     if not output_final_state:
         return out
