@@ -4,6 +4,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -28,6 +30,18 @@ int check_device() {
 bool head_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
 bool dtype_ok(int dt) { return dt == SGSA_DTYPE_F32 || dt == SGSA_DTYPE_BF16; }
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// One non-blocking side stream per device for the layer's concurrent delta stage.
+cudaStream_t side_stream() {
+    static std::mutex mu;
+    static cudaStream_t streams[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
+        streams[dev] = nullptr;
+    return streams[dev];
+}
 
 // SGSA_ATTN_GATHER=1 makes the layer use the row-gather attention (A/B checks).
 bool fused_attn_enabled() {
@@ -219,20 +233,44 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     if (indices) ix = indices;
     int flags = SGSA_FLAG_OUT_F32 | (initial_state ? SGSA_FLAG_HAS_INIT : 0) |
                 (final_state ? SGSA_FLAG_STORE_FINAL : 0);
-    cudaError_t e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
-                                             initial_state, od, final_state, B, T, H, D, dtype,
-                                             flags, w, st);
-    if (e != cudaSuccess) return fail_cuda(e);
     const float scale = 1.0f / sqrtf((float)D);
+    cudaError_t e;
     if (fused) {
-        // selection exported as per-row thresholds; indices written only if asked for
-        e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, H, DI, top_k, nullptr, 0,
-                                          st);
+        // The delta stage runs on a side stream beside the indexer (neither reads the
+        // other's output); the attention, which gates with the delta output, joins.
+        cudaStream_t side = side_stream();
+        cudaEvent_t fork = nullptr, join = nullptr;
+        if (!side || cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess) {
+            if (fork) cudaEventDestroy(fork);
+            side = st;  // run in order on the caller's stream
+        }
+        if (side != st) {
+            cudaEventRecord(fork, st);
+            cudaStreamWaitEvent(side, fork, 0);
+        }
+        e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
+                                     initial_state, od, final_state, B, T, H, D, dtype, flags, w,
+                                     side);
+        if (side != st) {
+            cudaEventRecord(join, side);
+            cudaEventDestroy(fork);
+        }
+        if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
+            e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, H, DI, top_k, nullptr,
+                                              0, st);
+        if (side != st) {
+            cudaStreamWaitEvent(st, join, 0);
+            cudaEventDestroy(join);
+        }
         if (e != cudaSuccess) return fail_cuda(e);
         e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
                                         mix_per_channel, nullptr, 0, false, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
+    e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr, initial_state,
+                                 od, final_state, B, T, H, D, dtype, flags, w, st);
+    if (e != cudaSuccess) return fail_cuda(e);
     e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, H, DI, top_k, dtype, st);
     if (e != cudaSuccess) return fail_cuda(e);
     e = sgsa::launch_sparse_attn_mix(q, k, v, ix, od, mix, out, B, T, H, D, top_k, scale,
