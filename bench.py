@@ -222,7 +222,7 @@ def stage_times(cfg, d, reps=3, only=None):
 
     def attn():
         _lib.check(lib.sgsa_sparse_attn_mix(P(d["q"]), P(d["k"]), P(d["v"]), P(ix), P(od),
-                                            P(d["mix"]), P(out), B, T, H, D, cfg.top_k,
+                                            P(d["mix"]), P(out), B, T, H, D, cfg.top_k, H,
                                             1.0 / math.sqrt(D), 1, _lib.DTYPE_BF16,
                                             st.cuda_stream), "attn")
 
@@ -236,7 +236,7 @@ def stage_times(cfg, d, reps=3, only=None):
     def attn_tc():
         _lib.check(lib.sgsa_sparse_attn_thresholds(P(d["q"]), P(d["k"]), P(d["v"]), P(d["iq"]),
                                                    P(d["ik"]), P(thr), None, 0, P(od), P(d["mix"]),
-                                                   P(out), B, T, H, D, cfg.d_idx,
+                                                   P(out), B, T, H, D, cfg.d_idx, H,
                                                    1.0 / math.sqrt(D), 1, 0, st.cuda_stream),
                    "attn_tc")
 

@@ -129,12 +129,13 @@ int sgsa_topk_select(const float *scores, const int32_t *valid, int32_t *indices
  * Replaces modelings/hybrid_dense_delta_topk.py:350-356 and :389-390.
  * o_delta is float32 [B,T,H,D] (NULL: out = o_s).  mix_per_channel selects
  * the [B,T,H,D] (1) or [B,T,H] (0) mix layout; mix may be NULL with o_delta.
- * out has the call's dtype.
+ * out has the call's dtype.  idx_heads == H: indices [B,H,T,K]; idx_heads == 1:
+ * one index set per token shared by all heads, indices [B,1,T,K].
  */
 int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int32_t *indices,
                          const float *o_delta, const void *mix, void *out, int B, int T, int H,
-                         int D, int top_k, float scale, int mix_per_channel, int dtype,
-                         void *stream);
+                         int D, int top_k, int idx_heads, float scale, int mix_per_channel,
+                         int dtype, void *stream);
 
 /*
  * The indexer of sgsa_indexer_topk (bf16, DI == 64 or 128) that also writes,
@@ -155,14 +156,18 @@ int sgsa_indexer_thresholds(const void *iq, const void *ik, int32_t *indices,
  * sgsa_indexer_thresholds, computed on the tensor cores over the causal
  * prefix (bf16 inputs, D == 128, DI == 64).  Same result as
  * sgsa_sparse_attn_mix on the equivalent index rows.  out is bf16, or float32
- * with out_f32; q_tiles as for sgsa_indexer_thresholds.
+ * with out_f32; q_tiles as for sgsa_indexer_thresholds.  idx_heads == 1: iq, ik
+ * [B,T,1,DI] and thresholds [B,1,T,4] are shared by all heads (the DeepSeek-style
+ * shared indexer of modelings/deepseek_v3_2.py:435-487, an option: it changes the
+ * selection semantics from per-head to per-token).
  * Replaces modelings/hybrid_dense_delta_topk.py:343-356 and :389-390.
  */
 int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, const void *iq,
                                 const void *ik, const uint32_t *thresholds,
                                 const int32_t *q_tiles, int n_tiles, const float *o_delta,
                                 const void *mix, void *out, int B, int T, int H, int D, int DI,
-                                float scale, int mix_per_channel, int out_f32, void *stream);
+                                int idx_heads, float scale, int mix_per_channel, int out_f32,
+                                void *stream);
 
 /*
  * The gate alone: out = mix * o_s + (1 - mix) * o_delta over `rows` rows of D
@@ -177,13 +182,16 @@ int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void 
  * The composite layer forward: chunked delta stage (no sparse write),
  * indexer top-k, sparse attention and gate, in one stream-ordered call.
  * indices may be NULL (kept in the workspace).  final_state may be NULL.
+ * iq, ik are [B,T,idx_heads,DI] with idx_heads == H (per-head selection) or 1
+ * (one selection per token shared by all heads).
  */
 size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top_k);
 int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta,
                    const void *gamma, const void *iq, const void *ik, const void *mix,
                    const float *initial_state, void *out, float *final_state, int32_t *indices,
-                   int B, int T, int H, int D, int DI, int top_k, int mix_per_channel,
-                   int dtype, void *workspace, size_t workspace_bytes, void *stream);
+                   int B, int T, int H, int D, int DI, int idx_heads, int top_k,
+                   int mix_per_channel, int dtype, void *workspace, size_t workspace_bytes,
+                   void *stream);
 
 /*
  * Token-by-token SGSA recurrence (forward): the semantics of

@@ -31,16 +31,16 @@ SIGNATURES = {
     "sgsa_chunk_fwd_noalloc": (_i, [_vp] * 11 + [_i] * 7 + [_vp]),
     "sgsa_indexer_topk": (_i, [_vp, _vp, _vp] + [_i] * 6 + [_vp]),
     "sgsa_topk_select": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
-    "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
+    "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 6 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_indexer_thresholds": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),
-    "sgsa_sparse_attn_thresholds": (_i, [_vp] * 7 + [_i] + [_vp] * 3 + [_i] * 5 +
+    "sgsa_sparse_attn_thresholds": (_i, [_vp] * 7 + [_i] + [_vp] * 3 + [_i] * 6 +
                                     [ctypes.c_float, _i, _i, _vp]),
     "sgsa_gate_mix": (_i, [_vp] * 4 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
     "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),
     "sgsa_decode_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_layer_fwd_workspace_size": (_sz, [_i] * 6),
-    "sgsa_layer_fwd": (_i, [_vp] * 12 + [_i] * 8 + [_vp, _sz, _vp]),
+    "sgsa_layer_fwd": (_i, [_vp] * 12 + [_i] * 9 + [_vp, _sz, _vp]),
 }
 
 _lib = None

@@ -146,15 +146,16 @@ int sgsa_topk_select(const float *scores, const int32_t *valid, int32_t *indices
 
 int sgsa_sparse_attn_mix(const void *q, const void *k, const void *v, const int32_t *indices,
                          const float *o_delta, const void *mix, void *out, int B, int T, int H,
-                         int D, int top_k, float scale, int mix_per_channel, int dtype,
-                         void *stream) {
+                         int D, int top_k, int idx_heads, float scale, int mix_per_channel,
+                         int dtype, void *stream) {
     if (B < 0 || T < 0 || H < 0 || top_k <= 0 || !head_dim_ok(D)) return SGSA_ERR_SHAPE;
+    if (idx_heads != 1 && idx_heads != H) return SGSA_ERR_SHAPE;
     if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
     if ((size_t)B * T * H == 0) return SGSA_OK;
     if (!q || !k || !v || !indices || !out) return SGSA_ERR_NULL;
     if (int s = check_device()) return s;
     cudaError_t e = sgsa::launch_sparse_attn_mix(q, k, v, indices, o_delta, mix, out, B, T, H, D,
-                                                 top_k, scale, mix_per_channel, dtype,
+                                                 top_k, scale, mix_per_channel, dtype, idx_heads,
                                                  (cudaStream_t)stream);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
@@ -176,15 +177,17 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
                                 const void *ik, const uint32_t *thresholds,
                                 const int32_t *q_tiles, int n_tiles, const float *o_delta,
                                 const void *mix, void *out, int B, int T, int H, int D, int DI,
-                                float scale, int mix_per_channel, int out_f32, void *stream) {
+                                int idx_heads, float scale, int mix_per_channel, int out_f32,
+                                void *stream) {
     if (B < 0 || T < 0 || H < 0 || n_tiles < 0) return SGSA_ERR_SHAPE;
+    if (idx_heads != 1 && idx_heads != H) return SGSA_ERR_SHAPE;
     if (!sgsa::sparse_attn_tc_eligible(T, D, DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
     if ((size_t)B * T * H == 0) return SGSA_OK;
     if (!q || !k || !v || !iq || !ik || !thresholds || !out) return SGSA_ERR_NULL;
     if (int s = check_device()) return s;
     cudaError_t e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thresholds, o_delta, mix, out,
                                                 B, T, H, scale, mix_per_channel, q_tiles, n_tiles,
-                                                out_f32 != 0, (cudaStream_t)stream);
+                                                out_f32 != 0, idx_heads, (cudaStream_t)stream);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
@@ -213,9 +216,11 @@ size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top
 int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta,
                    const void *gamma, const void *iq, const void *ik, const void *mix,
                    const float *initial_state, void *out, float *final_state, int32_t *indices,
-                   int B, int T, int H, int D, int DI, int top_k, int mix_per_channel,
-                   int dtype, void *workspace, size_t workspace_bytes, void *stream) {
+                   int B, int T, int H, int D, int DI, int idx_heads, int top_k,
+                   int mix_per_channel, int dtype, void *workspace, size_t workspace_bytes,
+                   void *stream) {
     if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D) || top_k <= 0) return SGSA_ERR_SHAPE;
+    if (idx_heads != 1 && idx_heads != H) return SGSA_ERR_SHAPE;
     if (DI != 32 && DI != 64 && DI != 128) return SGSA_ERR_SHAPE;
     if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
     if (!q || !k || !v || !beta || !gamma || !iq || !ik || !mix || !out) return SGSA_ERR_NULL;
@@ -257,24 +262,24 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
             cudaEventDestroy(fork);
         }
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
-            e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, H, DI, top_k, nullptr,
-                                              0, st);
+            e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, idx_heads, DI, top_k,
+                                              nullptr, 0, st);
         if (side != st) {
             cudaStreamWaitEvent(st, join, 0);
             cudaEventDestroy(join);
         }
         if (e != cudaSuccess) return fail_cuda(e);
         e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
-                                        mix_per_channel, nullptr, 0, false, st);
+                                        mix_per_channel, nullptr, 0, false, idx_heads, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
     e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr, initial_state,
                                  od, final_state, B, T, H, D, dtype, flags, w, st);
     if (e != cudaSuccess) return fail_cuda(e);
-    e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, H, DI, top_k, dtype, st);
+    e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, idx_heads, DI, top_k, dtype, st);
     if (e != cudaSuccess) return fail_cuda(e);
     e = sgsa::launch_sparse_attn_mix(q, k, v, ix, od, mix, out, B, T, H, D, top_k, scale,
-                                     mix_per_channel, dtype, st);
+                                     mix_per_channel, dtype, idx_heads, st);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 

@@ -36,7 +36,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  cudaStream_t st);
+                                  int HI, cudaStream_t st);
 cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
                             long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);
@@ -78,13 +78,13 @@ cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_
 cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
                                    const int32_t *idx, const float *od, const void *mix,
                                    void *out, int B, int T, int H, int D, int K, float scale,
-                                   int mix_pc, int dtype, cudaStream_t st);
+                                   int mix_pc, int dtype, int HI, cudaStream_t st);
 bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype);
 cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  cudaStream_t st);
+                                  int HI, cudaStream_t st);
 cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
                             long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);

@@ -105,7 +105,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
     const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
     const int32_t *__restrict__ idx, const float *__restrict__ od, const T *__restrict__ mix,
-    T *__restrict__ out, int B, int T_, int H, int K, float scale_log2, int mix_pc) {
+    T *__restrict__ out, int B, int T_, int H, int K, float scale_log2, int mix_pc, int HI) {
     constexpr int EPL = D / 16;
     // rows per half-warp in flight: up to 8, bounded by ~64 registers of packed rows
     constexpr int kWords = EPL * (int)sizeof(T) / 4;
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
 #pragma unroll
     for (int e = 0; e < EPL; ++e) qv[e] *= scale_log2;
 
-    const int32_t *ix = idx + (size_t)qi * K;
+    const int32_t *ix = idx + (((size_t)b * HI + (HI == 1 ? 0 : h)) * T_ + t) * K;
     const int nsel = min(K, t + 1);
     float m = -INFINITY, l = 0.f, acc[EPL];
 #pragma unroll
@@ -213,23 +213,23 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
 template <typename T, int D>
 cudaError_t run(const void *q, const void *k, const void *v, const int32_t *idx, const float *od,
                 const void *mix, void *out, int B, int T_, int H, int K, float scale, int mix_pc,
-                cudaStream_t st) {
+                int HI, cudaStream_t st) {
     const long long nq = (long long)B * H * T_;
     const unsigned grid = (unsigned)((nq + kWarps - 1) / kWarps);
     sparse_attn_mix_kernel<T, D><<<grid, kWarps * 32, 0, st>>>(
         (const T *)q, (const T *)k, (const T *)v, idx, od, (const T *)mix, (T *)out, B, T_, H, K,
-        scale * 1.4426950408889634f, mix_pc);
+        scale * 1.4426950408889634f, mix_pc, HI);
     return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t run_d(int D, const void *q, const void *k, const void *v, const int32_t *idx,
                   const float *od, const void *mix, void *out, int B, int T_, int H, int K,
-                  float scale, int mix_pc, cudaStream_t st) {
+                  float scale, int mix_pc, int HI, cudaStream_t st) {
     switch (D) {
-        case 32: return run<T, 32>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, st);
-        case 64: return run<T, 64>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, st);
-        case 128: return run<T, 128>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, st);
+        case 32: return run<T, 32>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, HI, st);
+        case 64: return run<T, 64>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, HI, st);
+        case 128: return run<T, 128>(q, k, v, idx, od, mix, out, B, T_, H, K, scale, mix_pc, HI, st);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -239,10 +239,10 @@ cudaError_t run_d(int D, const void *q, const void *k, const void *v, const int3
 cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,
                                    const int32_t *idx, const float *od, const void *mix,
                                    void *out, int B, int T, int H, int D, int K, float scale,
-                                   int mix_pc, int dtype, cudaStream_t st) {
+                                   int mix_pc, int dtype, int HI, cudaStream_t st) {
     if (dtype == SGSA_DTYPE_F32)
-        return run_d<float>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, st);
-    return run_d<__nv_bfloat16>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, st);
+        return run_d<float>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, HI, st);
+    return run_d<__nv_bfloat16>(D, q, k, v, idx, od, mix, out, B, T, H, K, scale, mix_pc, HI, st);
 }
 
 namespace {

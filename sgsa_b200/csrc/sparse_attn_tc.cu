@@ -20,6 +20,10 @@
 // updated lazily: O and the row sum are rescaled only when a tile's maximum
 // exceeds the one in use by more than 2^8, which keeps p <= 256 and is exact.
 //
+// With HI == 1 (a shared-across-heads indexer, one index set per token as in
+// the DeepSeek indexer of modelings/deepseek_v3_2.py:435-487) every head reads
+// indexer head 0's vectors and thresholds.
+//
 // Warp roles (96 + 128 kParts threads, one CTA per (b, h, 128-query tile)): warp 0 TMA,
 // warp 1 TMEM owner + MMA issuer, warp 2 TMA of the values, warps 3.. kParts
 // threads per query row.
@@ -62,7 +66,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_ik, const uint4 *__restrict__ thr,
                       const float *__restrict__ od, const Tmix *__restrict__ mix,
                       Tout *__restrict__ out, int B, int T, int H, float scale_log2,
-                      int mix_pc, int nqt, const int32_t *__restrict__ q_tiles) {
+                      int mix_pc, int nqt, const int32_t *__restrict__ q_tiles, int HI) {
     using namespace sm100;
     constexpr int D = 128;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -78,6 +82,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int BH = B * H;
     const int qt = q_tiles ? q_tiles[blockIdx.x / BH] : nqt - 1 - (int)(blockIdx.x / BH);
     const int bh = (int)(blockIdx.x % BH), b = bh / H, h = bh % H;
+    const int hi = (HI == 1) ? 0 : h;  // indexer head: shared by all heads when HI == 1
     const int q0 = qt * kRowsA;
     const int q_last = min(T - 1, q0 + kRowsA - 1);
     const int nkt = q_last / kNk + 1;
@@ -113,14 +118,14 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_arrive_expect_tx(qfull, 32768 + 16384);
             tma_load_3d(sm + L::kQ, &tm_q, qfull, 0, h, b * T + q0);
             tma_load_3d(sm + L::kQ + 16384, &tm_q, qfull, 64, h, b * T + q0);
-            tma_load_3d(sm + L::kIQ, &tm_iq, qfull, 0, h, b * T + q0);
+            tma_load_3d(sm + L::kIQ, &tm_iq, qfull, 0, hi, b * T + q0);
             for (int j = 0; j < nkt; ++j) {
                 const int st = j % kKS;
                 mbar_wait(&kempty[st], ((j / kKS) & 1) ^ 1, wd, 1u);
                 unsigned char *stg = sm + L::kKStage + st * L::kKBytes;
                 mbar_arrive_expect_tx(&kfull[st], L::kKBytes);
                 const int row = b * T + j * kNk;
-                tma_load_3d(stg, &tm_ik, &kfull[st], 0, h, row);
+                tma_load_3d(stg, &tm_ik, &kfull[st], 0, hi, row);
                 tma_load_3d(stg + 8192, &tm_k, &kfull[st], 0, h, row);
                 tma_load_3d(stg + 16384, &tm_k, &kfull[st], 64, h, row);
             }
@@ -197,7 +202,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
         float *xmax = (float *)(sm + L::kBar + 256);  // [2 tiles][kParts][128 rows]
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
-        if (valid_row) th = thr[(size_t)bh * T + t];
+        if (valid_row) th = thr[((size_t)b * HI + hi) * T + t];
         const uint32_t prefix = th.x, mask = th.y;
         const int cut = (int)th.z;
         float m_used = -INFINITY, l = 0.f;
@@ -325,13 +330,13 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  cudaStream_t st) {
+                                  int HI, cudaStream_t st) {
     CUtensorMap mq, mk, mv, miq, mik;
     if (!make_tmap_rows_bf16(&mq, q, B, T, H, 128, 128) ||
         !make_tmap_rows_bf16(&mk, k, B, T, H, 128, kNk) ||
         !make_tmap_rows_bf16(&mv, v, B, T, H, 128, kNk) ||
-        !make_tmap_rows_bf16(&miq, iq, B, T, H, 64, 128) ||
-        !make_tmap_rows_bf16(&mik, ik, B, T, H, 64, kNk))
+        !make_tmap_rows_bf16(&miq, iq, B, T, HI, 64, 128) ||
+        !make_tmap_rows_bf16(&mik, ik, B, T, HI, 64, kNk))
         return cudaErrorInvalidValue;
     const int nqt = ceil_div(T, kRowsA);
     const int ntiles = q_tiles ? n_tiles : nqt;
@@ -344,7 +349,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
             mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
-            (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles);
+            (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI);
     } else {
         auto kern = sparse_attn_tc_kernel<__nv_bfloat16, __nv_bfloat16>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -352,7 +357,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
             mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
-            (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles);
+            (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI);
     }
     return cudaGetLastError();
 }

@@ -204,8 +204,10 @@ def sparse_attn_mix(q: Tensor, k: Tensor, v: Tensor, indices: Tensor,
     for n, t in (("q", q), ("k", k), ("v", v), ("indices", indices)):
         _dev(t, n)
     B, T, H, D = q.shape
-    if indices.dim() != 4 or indices.shape[:3] != (B, H, T):
-        raise ValueError("indices must be [B, H, T, K]")
+    if indices.dim() != 4 or indices.shape[0] != B or indices.shape[2] != T or \
+            indices.shape[1] not in (1, H):
+        raise ValueError("indices must be [B, H, T, K] or [B, 1, T, K]")
+    idx_heads = indices.shape[1]
     K = indices.shape[-1]
     dt = _dtype_code(q)
     cast = lambda t: None if t is None else t.to(q.dtype).contiguous()
@@ -217,8 +219,8 @@ def sparse_attn_mix(q: Tensor, k: Tensor, v: Tensor, indices: Tensor,
     out = torch.empty_like(q_)
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
     st = _lib.load().sgsa_sparse_attn_mix(_ptr(q_), _ptr(k_), _ptr(v_), _ptr(ix), _ptr(od),
-                                           _ptr(mx), _ptr(out), B, T, H, D, K, sc, per_channel,
-                                           dt, _stream(q))
+                                           _ptr(mx), _ptr(out), B, T, H, D, K, idx_heads, sc,
+                                           per_channel, dt, _stream(q))
     _lib.check(st, "sgsa_sparse_attn_mix")
     return out
 
@@ -237,6 +239,9 @@ def sgsa_layer_fwd(q: Tensor, k: Tensor, v: Tensor, beta: Tensor, gamma: Tensor,
     _no_grad_check(q, k, v, beta, gamma, iq, ik, mix, initial_state)
     B, T, H, D = q.shape
     DI = iq.shape[-1]
+    idx_heads = iq.shape[2]
+    if idx_heads not in (1, H) or ik.shape != iq.shape:
+        raise ValueError("iq and ik must be [B, T, H, DI] or [B, T, 1, DI] (shared indexer)")
     dt = _dtype_code(q)
     cast = lambda t: t.to(q.dtype).contiguous()
     args = [q.contiguous()] + [cast(t) for t in (k, v, beta, gamma, iq, ik, mix)]
@@ -244,12 +249,13 @@ def sgsa_layer_fwd(q: Tensor, k: Tensor, v: Tensor, beta: Tensor, gamma: Tensor,
     s0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
     out = torch.empty_like(args[0])
     sT = torch.empty(B, H, D, D, device=q.device, dtype=torch.float32) if output_final_state else None
-    ix = torch.empty(B, H, T, top_k, device=q.device, dtype=torch.int32) if return_indices else None
+    ix = torch.empty(B, idx_heads, T, top_k, device=q.device, dtype=torch.int32) \
+        if return_indices else None
     lib = _lib.load()
     ws = _workspace(lib.sgsa_layer_fwd_workspace_size(B, T, H, D, DI, top_k), q.device)
     st = lib.sgsa_layer_fwd(*[_ptr(t) for t in args], _ptr(s0), _ptr(out), _ptr(sT), _ptr(ix),
-                            B, T, H, D, DI, top_k, per_channel, dt, _ptr(ws), ws.numel(),
-                            _stream(q))
+                            B, T, H, D, DI, idx_heads, top_k, per_channel, dt, _ptr(ws),
+                            ws.numel(), _stream(q))
     _lib.check(st, "sgsa_layer_fwd")
     res = [out]
     if output_final_state:
@@ -296,8 +302,8 @@ def sparse_attn_thresholds(q, k, v, iq, ik, thresholds, o_delta=None, mix=None, 
     nt = 0 if qt is None else qt.numel()
     st = _lib.load().sgsa_sparse_attn_thresholds(
         _ptr(q), _ptr(k), _ptr(v), _ptr(iq), _ptr(ik), _ptr(thresholds), _ptr(qt), nt, _ptr(od),
-        _ptr(mx), _ptr(out), B, T, H, D, DI, sc, per_channel, int(out.dtype == torch.float32),
-        _stream(q))
+        _ptr(mx), _ptr(out), B, T, H, D, DI, iq.shape[2], sc, per_channel,
+        int(out.dtype == torch.float32), _stream(q))
     _lib.check(st, "sgsa_sparse_attn_thresholds")
     return out
 

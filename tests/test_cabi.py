@@ -47,7 +47,7 @@ def test_bad_arguments_rejected_before_any_launch(lib):
     assert lib.sgsa_chunk_fwd(*([None] * 11), 1, 64, 1, 64, 0, 32, 0, None, 0, None) == -1
     assert lib.sgsa_chunk_fwd(*([None] * 11), 1, 64, 1, 64, 7, 64, 0, None, 0, None) == -2
     assert lib.sgsa_indexer_topk(None, None, None, 1, 64, 1, 48, 8, 0, None) == -1
-    assert lib.sgsa_sparse_attn_mix(*([None] * 7), 1, 64, 1, 64, 0, 1.0, 0, 1, None) == -1
+    assert lib.sgsa_sparse_attn_mix(*([None] * 7), 1, 64, 1, 64, 0, 1, 1.0, 0, 1, None) == -1
     # empty problems are a no-op
     assert lib.sgsa_indexer_topk(None, None, None, 0, 64, 1, 64, 8, 1, None) == 0
 

@@ -313,3 +313,23 @@ def test_layer_from_host_matches_device_call():
     torch.cuda.synchronize()
     want = ops.sgsa_layer_fwd(*[x[n].cuda() for n in names], cfg.top_k).cpu()
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("gather", [False, True])
+def test_layer_shared_indexer(gather, monkeypatch):
+    """One index set per token shared by all heads (iq, ik with a single head)."""
+    cfg = CONFIGS["b200_bf16"].scaled(name="shared", B=2, T=1024, H=4, top_k=128)
+    x = make_inputs(cfg, seed=10)
+    x["iq"], x["ik"] = x["iq"][:, :, :1].contiguous(), x["ik"][:, :, :1].contiguous()
+    if gather:
+        monkeypatch.setenv("SGSA_ATTN_GATHER", "1")
+    d = dev(x)
+    out, idx = ops.sgsa_layer_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"], d["ik"],
+                                  d["mix"], cfg.top_k, return_indices=True)
+    assert idx.shape == (2, 1, 1024, 128)
+    want_idx, kth = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k, return_kth=True)
+    check_index_sets(idx.cpu().numpy(), want_idx, x["iq"].float(), x["ik"].float(), kth, 1e-5)
+    ro, _ = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"])
+    idx_h = np.repeat(idx.cpu().numpy(), cfg.H, axis=1)
+    want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx_h, ro, x["mix"])
+    assert oracle.rel_l2(out.float().cpu().numpy(), want) < 2e-3
