@@ -170,6 +170,18 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
                                 void *stream);
 
 /*
+ * Retrieval of the sparse-write SGSA block: k_hat, v_hat [B,T,H,D] (dtype) are
+ * the softmax(q_t . k_j * scale)-weighted sums of the selected k and v rows.
+ * Replaces the aggregation of SparseRetriever._token_only
+ * (modelings/modeling_sgsa.py:113-142); with indices from sgsa_indexer_topk on
+ * iq = q, ik = k it is the retriever's token path, and (k_hat, v_hat) are the
+ * sparse_k / sparse_v of sgsa_chunk_fwd (modelings/modeling_sgsa.py:546-609).
+ */
+int sgsa_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *indices,
+                         void *k_hat, void *v_hat, int B, int T, int H, int D, int top_k,
+                         int idx_heads, float scale, int dtype, void *stream);
+
+/*
  * The gate alone: out = mix * o_s + (1 - mix) * o_delta over `rows` rows of D
  * (o_s, o_delta float32; mix [rows, D] or [rows]; out in dtype).  The mix of
  * modelings/hybrid_dense_delta_topk.py:389-390, used where the two branch

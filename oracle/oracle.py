@@ -189,3 +189,27 @@ def decode_attn_mix(q, k_cache, v_cache, idx, o_delta=None, mix=None, scale=None
             m = m[..., None]
         out = m * out + (1.0 - m) * od
     return out
+
+
+def sparse_retrieve(k, v, idx, q, scale=None):
+    """(k_hat, v_hat) [B, T, H, D]: softmax(q . k_j * scale) weighted sums of the
+    selected k and v rows -- the retriever's token path
+    (modelings/modeling_sgsa.py:113-142), float64."""
+    q = np.asarray(_f32(q), np.float64)
+    k = np.asarray(_f32(k), np.float64)
+    v = np.asarray(_f32(v), np.float64)
+    B, T, H, D = q.shape
+    sc = float(scale) if scale is not None else 1.0 / np.sqrt(D)
+    kh = np.zeros((B, T, H, D))
+    vh = np.zeros((B, T, H, D))
+    for b in range(B):
+        for h in range(H):
+            hh = h if idx.shape[1] == H else 0
+            for t in range(T):
+                sel = idx[b, hh, t][idx[b, hh, t] >= 0]
+                s = k[b, sel, h] @ q[b, t, h] * sc
+                p = np.exp(s - s.max())
+                p /= p.sum()
+                kh[b, t, h] = p @ k[b, sel, h]
+                vh[b, t, h] = p @ v[b, sel, h]
+    return kh, vh

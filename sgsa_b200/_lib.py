@@ -35,6 +35,7 @@ SIGNATURES = {
     "sgsa_indexer_thresholds": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),
     "sgsa_sparse_attn_thresholds": (_i, [_vp] * 7 + [_i] + [_vp] * 3 + [_i] * 6 +
                                     [ctypes.c_float, _i, _i, _vp]),
+    "sgsa_sparse_retrieve": (_i, [_vp] * 6 + [_i] * 6 + [ctypes.c_float, _i, _vp]),
     "sgsa_gate_mix": (_i, [_vp] * 4 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
     "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),

@@ -191,6 +191,21 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *indices,
+                         void *k_hat, void *v_hat, int B, int T, int H, int D, int top_k,
+                         int idx_heads, float scale, int dtype, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || top_k <= 0 || !head_dim_ok(D)) return SGSA_ERR_SHAPE;
+    if (idx_heads != 1 && idx_heads != H) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!q || !k || !v || !indices || !k_hat || !v_hat) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_sparse_retrieve(q, k, v, indices, k_hat, v_hat, B, T, H, D,
+                                                 top_k, scale, idx_heads, dtype,
+                                                 (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
 int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void *out,
                   long long rows, int D, int mix_per_channel, int dtype, void *stream) {
     if (rows < 0 || D <= 0) return SGSA_ERR_SHAPE;

@@ -37,6 +37,9 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
                                   int HI, cudaStream_t st);
+cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
+                                   void *khat, void *vhat, int B, int T, int H, int D, int K,
+                                   float scale, int HI, int dtype, cudaStream_t st);
 cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
                             long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);
@@ -85,6 +88,9 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
                                   int HI, cudaStream_t st);
+cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
+                                   void *khat, void *vhat, int B, int T, int H, int D, int K,
+                                   float scale, int HI, int dtype, cudaStream_t st);
 cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
                             long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);

@@ -101,11 +101,14 @@ struct RawSeg {
     }
 };
 
-template <typename T, int D>
+// WITH_K: also accumulate the same softmax-weighted sum of the k rows into khat
+// (the retrieval k_hat / v_hat of the sparse-write SGSA block).
+template <typename T, int D, bool WITH_K = false>
 __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
     const T *__restrict__ q, const T *__restrict__ k, const T *__restrict__ v,
     const int32_t *__restrict__ idx, const float *__restrict__ od, const T *__restrict__ mix,
-    T *__restrict__ out, int B, int T_, int H, int K, float scale_log2, int mix_pc, int HI) {
+    T *__restrict__ out, int B, int T_, int H, int K, float scale_log2, int mix_pc, int HI,
+    T *__restrict__ khat = nullptr) {
     constexpr int EPL = D / 16;
     // rows per half-warp in flight: up to 8, bounded by ~64 registers of packed rows
     constexpr int kWords = EPL * (int)sizeof(T) / 4;
@@ -129,9 +132,9 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
 
     const int32_t *ix = idx + (((size_t)b * HI + (HI == 1 ? 0 : h)) * T_ + t) * K;
     const int nsel = min(K, t + 1);
-    float m = -INFINITY, l = 0.f, acc[EPL];
+    float m = -INFINITY, l = 0.f, acc[EPL], acck[EPL];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
+    for (int e = 0; e < EPL; ++e) acc[e] = acck[e] = 0.f;
 
     for (int base = 0; base < nsel; base += 32) {
         const int cnt = min(32, nsel - base);
@@ -170,13 +173,19 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
                 const float corr = exp2f(m - mn);  // m == -inf gives 0
                 l *= corr;
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) acc[e] *= corr;
+                for (int e = 0; e < EPL; ++e) {
+                    acc[e] *= corr;
+                    if (WITH_K) acck[e] *= corr;
+                }
 #pragma unroll
                 for (int u = 0; u < kU; ++u) {
                     const float pu = exp2f(s[u] - mn);
                     l += pu;
 #pragma unroll
-                    for (int e = 0; e < EPL; ++e) acc[e] = fmaf(pu, vr[u].get(e), acc[e]);
+                    for (int e = 0; e < EPL; ++e) {
+                        acc[e] = fmaf(pu, vr[u].get(e), acc[e]);
+                        if (WITH_K) acck[e] = fmaf(pu, kr[u].get(e), acck[e]);
+                    }
                 }
                 m = mn;
             }
@@ -190,11 +199,20 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
     const float c2 = (m2 == -INFINITY) ? 0.f : exp2f(m2 - mt);
     const float lt = l * c1 + l2 * c2;
     const float inv = (lt > 0.f) ? 1.f / lt : 0.f;
-    float o[EPL];
+    float o[EPL], ok[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
         const float a2 = __shfl_xor_sync(0xffffffffu, acc[e], 16);
         o[e] = (acc[e] * c1 + a2 * c2) * inv;
+        if (WITH_K) {
+            const float b2 = __shfl_xor_sync(0xffffffffu, acck[e], 16);
+            ok[e] = (acck[e] * c1 + b2 * c2) * inv;
+        }
+    }
+    if (WITH_K && half == 0) {
+        T *dk = khat + rowq * D + hl * EPL;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dk[e] = from_f32<T>(ok[e]);
     }
     if (half == 0) {
         T *dst = out + rowq * D + hl * EPL;
@@ -257,6 +275,35 @@ __global__ void gate_mix_kernel(const float *__restrict__ os, const float *__res
     }
 }
 }  // namespace
+
+namespace {
+template <typename T, int D>
+cudaError_t run_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
+                         void *khat, void *vhat, int B, int T_, int H, int K, float scale, int HI,
+                         cudaStream_t st) {
+    const long long nq = (long long)B * H * T_;
+    const unsigned grid = (unsigned)((nq + kWarps - 1) / kWarps);
+    sparse_attn_mix_kernel<T, D, true><<<grid, kWarps * 32, 0, st>>>(
+        (const T *)q, (const T *)k, (const T *)v, idx, nullptr, nullptr, (T *)vhat, B, T_, H, K,
+        scale * 1.4426950408889634f, 0, HI, (T *)khat);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
+                                   void *khat, void *vhat, int B, int T, int H, int D, int K,
+                                   float scale, int HI, int dtype, cudaStream_t st) {
+    if (dtype == SGSA_DTYPE_F32) {
+        if (D == 32) return run_retrieve<float, 32>(q, k, v, idx, khat, vhat, B, T, H, K, scale, HI, st);
+        if (D == 64) return run_retrieve<float, 64>(q, k, v, idx, khat, vhat, B, T, H, K, scale, HI, st);
+        if (D == 128) return run_retrieve<float, 128>(q, k, v, idx, khat, vhat, B, T, H, K, scale, HI, st);
+    } else {
+        if (D == 32) return run_retrieve<__nv_bfloat16, 32>(q, k, v, idx, khat, vhat, B, T, H, K, scale, HI, st);
+        if (D == 64) return run_retrieve<__nv_bfloat16, 64>(q, k, v, idx, khat, vhat, B, T, H, K, scale, HI, st);
+        if (D == 128) return run_retrieve<__nv_bfloat16, 128>(q, k, v, idx, khat, vhat, B, T, H, K, scale, HI, st);
+    }
+    return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
                             long long rows, int D, int mix_pc, int dtype, cudaStream_t st) {

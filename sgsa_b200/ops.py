@@ -507,3 +507,35 @@ def gate_mix(o_s: Tensor, o_delta: Tensor, mix: Tensor, dtype=torch.bfloat16) ->
                                     _ptr(out), rows, D, per_channel, _DT[dtype], _stream(o_s))
     _lib.check(st, "sgsa_gate_mix")
     return out
+
+
+def sparse_retrieve(q: Tensor, k: Tensor, v: Tensor, indices: Tensor,
+                    scale: Optional[float] = None):
+    """(k_hat, v_hat) [B, T, H, D]: softmax-weighted sums of the selected k and v rows
+    (SparseRetriever._token_only, modelings/modeling_sgsa.py:113-142)."""
+    for n, t in (("q", q), ("k", k), ("v", v), ("indices", indices)):
+        _dev(t, n)
+    B, T, H, D = q.shape
+    K = indices.shape[-1]
+    q_, k_, v_ = q.contiguous(), k.to(q.dtype).contiguous(), v.to(q.dtype).contiguous()
+    kh, vh = torch.empty_like(q_), torch.empty_like(q_)
+    sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
+    st = _lib.load().sgsa_sparse_retrieve(_ptr(q_), _ptr(k_), _ptr(v_),
+                                           _ptr(indices.to(torch.int32).contiguous()), _ptr(kh),
+                                           _ptr(vh), B, T, H, D, K, indices.shape[1], sc,
+                                           _dtype_code(q), _stream(q))
+    _lib.check(st, "sgsa_sparse_retrieve")
+    return kh, vh
+
+
+def sgsa_sparse_write_fwd(q, k, v, beta, gamma, alpha, top_k: int, iq=None, ik=None,
+                          initial_state=None, output_final_state: bool = False):
+    """The SGSA block core with the sparse write (modelings/modeling_sgsa.py:634-684
+    with write_mode "direct"): top-k retrieval (scores iq . ik, by default q . k as
+    in SparseRetriever.forward, modelings/modeling_sgsa.py:407-474), its k_hat / v_hat
+    written into the state as the second virtual sample of each token with gain
+    alpha (modelings/modeling_sgsa.py:546-609).  Returns (o, final state | None)."""
+    idx = indexer_topk(q if iq is None else iq, k if ik is None else ik, top_k)
+    k_hat, v_hat = sparse_retrieve(q, k, v, idx)
+    return chunk_sgsa(q, k, v, beta, gamma, sparse_k=k_hat, sparse_v=v_hat, alpha=alpha,
+                      initial_state=initial_state, output_final_state=output_final_state)

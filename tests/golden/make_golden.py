@@ -13,6 +13,8 @@ writes small ``.npz`` fixtures next to this script:
   (modelings/modeling_sgsa.py:144-165) on random causal scores.
 * ``indexer_cfg0.npz``     -- the same selection applied to the indexer scores
   iq . ik^T of the fp32 CPU configuration (top-k 128, indexer dim 32).
+* ``retriever_token.npz``  -- ``SparseRetriever._token_only`` (modelings/modeling_sgsa.py:113-142):
+  the retrieval k_hat / v_hat of the sparse-write SGSA block.
 * ``sparse_attn_ref.npz``  -- ``TopKSparseKVReuseAttention.forward``
   (modelings/hybrid_dense_delta_topk.py:330-358) with identity projections and
   identity RoPE, then the gate of hybrid_dense_delta_topk.py:389-390.
@@ -26,6 +28,7 @@ Usage:  python -B tests/golden/make_golden.py /path/to/reference
 from __future__ import annotations
 
 import hashlib
+import math
 import os
 import sys
 
@@ -129,6 +132,23 @@ def main(ref_root: str) -> None:
     np.savez_compressed(os.path.join(HERE, "sparse_attn_ref.npz"), q=qa.numpy(), k=ka_.numpy(),
                         v=va.numpy(), o_delta=od.numpy(), mix=mix.numpy(),
                         topk_out=topk_out.numpy(), out=mixed.numpy(), top_k=ka)
+    # (6) the retriever's token path: k_hat / v_hat over the masked top-k
+    #     (modelings/modeling_sgsa.py:113-142), self given as a plain namespace
+    import types
+    torch.manual_seed(3)
+    Br, Tr, Hr, Dr, kr = 1, 200, 2, 32, 24
+    qr, kk, vr = (torch.randn(Br, Hr, Tr, Dr, dtype=torch.float64) for _ in range(3))
+    sc = torch.matmul(qr, kk.transpose(-1, -2)) / math.sqrt(Dr)
+    valid = ~torch.triu(torch.ones(Tr, Tr, dtype=torch.bool), diagonal=1)
+    valid = valid[None, None].expand(Br, Hr, Tr, Tr)
+    ns = types.SimpleNamespace(top_k=kr, eps=1e-6)
+    ns._masked_topk = lambda scores, valid_mask, topk: SparseRetriever._masked_topk(
+        ns, scores=scores, valid_mask=valid_mask, topk=topk)
+    res = SparseRetriever._token_only(ns, scores=sc, valid_mask=valid, k=kk, v=vr)
+    np.savez_compressed(os.path.join(HERE, "retriever_token.npz"),
+                        q=qr.transpose(1, 2).numpy(), k=kk.transpose(1, 2).numpy(),
+                        v=vr.transpose(1, 2).numpy(), k_hat=res["k_hat"].transpose(1, 2).numpy(),
+                        v_hat=res["v_hat"].transpose(1, 2).numpy(), top_k=kr)
     print("golden fixtures written to", HERE)
 
 

@@ -333,3 +333,31 @@ def test_layer_shared_indexer(gather, monkeypatch):
     idx_h = np.repeat(idx.cpu().numpy(), cfg.H, axis=1)
     want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx_h, ro, x["mix"])
     assert oracle.rel_l2(out.float().cpu().numpy(), want) < 2e-3
+
+
+def test_sparse_retrieve_reference_fixture():
+    z = np.load("tests/golden/retriever_token.npz")
+    t = lambda a: torch.from_numpy(a).float().cuda()
+    idx = ops.indexer_topk(t(z["q"]), t(z["k"]), int(z["top_k"]))
+    kh, vh = ops.sparse_retrieve(t(z["q"]), t(z["k"]), t(z["v"]), idx)
+    assert oracle.rel_l2(kh.cpu().numpy(), z["k_hat"]) < 1e-5
+    assert oracle.rel_l2(vh.cpu().numpy(), z["v_hat"]) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_sparse_write_block_matches_oracle(dtype):
+    """Retrieval (q . k top-k), k_hat / v_hat, then the delta rule with the sparse write."""
+    x = rand_case(2, 300, 2, 64, dtype, seed=21, sparse=True, init=True)
+    K = 32
+    d = dev(x)
+    o, st = ops.sgsa_sparse_write_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["alpha"],
+                                      K, initial_state=d["initial_state"],
+                                      output_final_state=True)
+    idx, kth = oracle.indexer_topk(x["q"], x["k"], K, return_kth=True)
+    kh, vh = oracle.sparse_retrieve(x["k"], x["v"], idx, x["q"])
+    kh = torch.from_numpy(kh).to(dtype)
+    vh = torch.from_numpy(vh).to(dtype)
+    ro, rs = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], kh, vh,
+                                   x["alpha"], x["initial_state"])
+    assert oracle.rel_l2(o.float().cpu().numpy(), ro) < TOL[dtype] * (1 if dtype == torch.float32 else 2)
+    assert oracle.rel_l2(st.float().cpu().numpy(), rs) < TOL[dtype] * (1 if dtype == torch.float32 else 2)

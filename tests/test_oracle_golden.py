@@ -78,3 +78,11 @@ def test_topk_edge_cases():
     np.testing.assert_array_equal(got, [[0, 1], [1, 2], [0, -1]])
     got = oracle.topk_select(sc, np.array([4, 4, 4], np.int32), 8)
     assert (got[:, :4] >= 0).all() and (got[:, 4:] == -1).all()
+
+
+def test_retriever_token_path_matches_reference():
+    z = load("retriever_token.npz")
+    idx = oracle.indexer_topk(z["q"], z["k"], int(z["top_k"]))
+    kh, vh = oracle.sparse_retrieve(z["k"], z["v"], idx, z["q"])
+    assert oracle.rel_l2(kh, z["k_hat"]) < 1e-6
+    assert oracle.rel_l2(vh, z["v_hat"]) < 1e-6
