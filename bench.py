@@ -359,6 +359,136 @@ def run_decode(args):
         "retrieval_hit_rate": hit, "dtype": "bf16", "data": "synthetic planted retrieval"}))
 
 
+HYBRID_B, HYBRID_T = 8, 4096
+HYBRID_METRIC = "hybrid model prefill tokens/s"
+
+
+def cpu_hybrid_reference(cores: int, T: int = 512):
+    """Time the CPU restatement of the configs[3] model (all 24 layers, full width)
+    on one sequence of T tokens, float32 outside the SGSA core; returns (tokens/s,
+    sample text, seconds)."""
+    from oracle import hybrid as ohybrid
+    from oracle import oracle
+    from sgsa_b200.hybrid import CONFIG_B200, HybridSGSAModel
+
+    oracle.set_num_threads(cores)
+    torch.set_num_threads(cores)
+    m = HybridSGSAModel(CONFIG_B200, device="cpu", dtype=torch.bfloat16, seed=0)
+    ids = torch.randint(1, CONFIG_B200.vocab_size, (1, T), generator=torch.Generator().manual_seed(0))
+    t0 = time.perf_counter()
+    ohybrid.model_forward(ids, m.weights, CONFIG_B200, dtype=torch.float32)
+    secs = time.perf_counter() - t0
+    sample = (f"one sequence of {T} tokens through the full configs[3] model (24 layers, "
+              f"hidden 2048, vocab 32000), float32 torch + float64 SGSA oracle, {cores} threads; "
+              f"tokens/s = {T} / seconds")
+    return T / secs, sample, secs
+
+
+def run_hybrid(args, ws, rank, local):
+    """hybrid model prefill, B=8 x T=4096, batch sharded over the ranks
+    (B/N sequences each; strong scaling, no communication)."""
+    from sgsa_b200.hybrid import CONFIG_B200, HybridSGSAModel
+
+    if HYBRID_B % ws:
+        raise SystemExit("--gpus must divide the batch of 8")
+    Bl, T, cfg = HYBRID_B // ws, HYBRID_T, CONFIG_B200
+    m = HybridSGSAModel(cfg, device="cuda", dtype=torch.bfloat16, seed=0)
+    g = torch.Generator().manual_seed(0)
+    ids_all = torch.randint(0, cfg.vocab_size, (HYBRID_B, T), generator=g)
+    ids_host = ids_all[rank * Bl:(rank + 1) * Bl].contiguous()
+    ids = ids_host.cuda()
+
+    def step():
+        return m(ids)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier(ws)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(ws)
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        barrier(ws)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws)
+
+    # end to end: pinned token ids -> device, full prefill, last-position logits -> host
+    pinned = ids_host.pin_memory()
+    out_host = torch.empty(Bl, cfg.vocab_size, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        d = pinned.to("cuda", non_blocking=True)
+        logits = m(d)
+        out_host.copy_(logits[:, -1], non_blocking=True)
+
+    e2e_step()
+    barrier(ws)
+    e2e_steps = max(1, min(args.steps, 5))
+    e0.record(st)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(st)
+    barrier(ws)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws)
+
+    # per-part device times of one more forward
+    marks = []
+    m(ids, marks=marks)
+    torch.cuda.synchronize()
+    parts = {}
+    for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
+        parts[name] = parts.get(name, 0.0) + a.elapsed_time(b)
+    flops = m.flops_per_token(T) * Bl * T
+    _, tfl, src = peaks()
+    if rank == 0:
+        cores = os.cpu_count() or 1
+        cpu_v, sample, secs = cpu_hybrid_reference(cores)
+        tokens = HYBRID_B * T
+        print(json.dumps({
+            "metric": HYBRID_METRIC, "workload": "hybrid_prefill (configs[3])",
+            "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic token ids (uniform over the vocab), random init std 0.02",
+            "config": {"workload": "hybrid_prefill", "B": HYBRID_B, "T": T,
+                       "layers": cfg.num_layers, "hidden": cfg.hidden_size,
+                       "heads": cfg.num_heads, "mlp": cfg.intermediate_size,
+                       "vocab": cfg.vocab_size, "top_k": cfg.top_k, "d_idx": cfg.indexer_dim,
+                       "layer_order": "dense at layer % 4 == 0, SGSA otherwise",
+                       "parallelism": f"batch-shard x{ws}",
+                       "l2": "activations > L2, no flush"},
+            "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": pinned.numel() * 8 * ws,
+                    "d2h_bytes_per_step": out_host.numel() * 2 * ws, "ms_per_step": e2e_ms},
+            "part_ms": parts,
+            "matrix_tflops": flops / (ms / 1e3) / 1e12,
+            "matrix_flops_per_step_rank": flops, "peak_tflops": tfl, "peak_source": src,
+            "cpu_baseline": {"value": cpu_v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample, "seconds": secs},
+            "clocks": clk.summary()}), flush=True)
+
+
+def run_hybrid_reference(args, ws, rank):
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    v, sample, secs = cpu_hybrid_reference(cores)
+    print(json.dumps({
+        "impl": "reference", "metric": HYBRID_METRIC, "workload": "hybrid_prefill (configs[3])",
+        "value": v, "unit": "tokens/s", "n_gpus": ws, "steps": 1, "warmup": 0,
+        "ms_per_step": HYBRID_B * HYBRID_T / v * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic token ids, random init std 0.02",
+        "config": {"workload": "hybrid_prefill", "B": HYBRID_B, "T": HYBRID_T},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample, "seconds": secs},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def run_only(args):
     """Run a single stage on a scaled configuration (for ncu captures)."""
     from sgsa_b200.inputs import CONFIGS, make_inputs
@@ -475,10 +605,12 @@ def main():
     ap.add_argument("--only", default=None, choices=["delta", "indexer_topk", "sparse_attn_mix", "indexer_thresholds",
                              "sparse_attn_tc"],
                     help="profiling aid: run one stage --steps times on a (scaled) config, no JSON")
-    ap.add_argument("--workload", default="layer", choices=["layer", "decode", "long"],
+    ap.add_argument("--workload", default="layer", choices=["layer", "decode", "long", "hybrid"],
                     help="decode: configs[4] (batch 64, 32768-token cache, top-k 1024 reused "
                          "every 4 steps, planted retrieval); long: configs[2] (T 65536, "
-                         "sequence parallel for N > 1); layer (default): configs[1]")
+                         "sequence parallel for N > 1); hybrid: configs[3] (24-layer "
+                         "hybrid model prefill, B 8 x T 4096, batch sharded); layer "
+                         "(default): configs[1]")
     ap.add_argument("--B", type=int, default=None)
     ap.add_argument("--T", type=int, default=None)
     ap.add_argument("--H", type=int, default=None)
@@ -492,12 +624,17 @@ def main():
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
-        run_reference(args, ws, rank)
+        if args.workload == "hybrid":
+            run_hybrid_reference(args, ws, rank)
+        else:
+            run_reference(args, ws, rank)
         return
     ws, rank, local = setup_dist()
     try:
         if args.workload == "long":
             run_long(args, ws, rank, local)
+        elif args.workload == "hybrid":
+            run_hybrid(args, ws, rank, local)
         else:
             run_ours(args, ws, rank, local)
     finally:

@@ -242,6 +242,37 @@ int sgsa_decode_attn_mix(const void *q, const void *k_cache, const void *v_cache
                          int B, int H, int Tc, int D, int top_k, float scale, int mix_per_channel,
                          int dtype, void *stream);
 
+/* ---- Hybrid model (the layers around the SGSA layer; 16-byte aligned rows) ---- */
+
+/* out = weight * x / sqrt(mean(x^2) + eps) per row of N (N % 8 == 0).
+ * Replaces RMSNorm.forward (modelings/hybrid_dense_delta_topk.py:97-106). */
+int sgsa_rmsnorm(const void *x, const void *weight, void *out, long long rows, int N, float eps,
+                 int dtype, void *stream);
+
+/* out [rows, I] = silu(gate_up[:, :I]) * gate_up[:, I:]  (I % 8 == 0).
+ * Replaces the activation of SwiGLUMLP.forward (modelings/hybrid_dense_delta_topk.py:117-119). */
+int sgsa_swiglu(const void *gate_up, void *out, long long rows, int I, int dtype, void *stream);
+
+/* qkv [B*T, 3*H*D] -> q, k rotated by RoPE and v, all [B, T, H, D].  cos_sin float32
+ * [pos0 + T, D/2, 2] holds (cos, sin) of position t and frequency theta^(-2j/D).
+ * Replaces _apply_rope on q and k (modelings/hybrid_dense_delta_topk.py:127-151, :210-211). */
+int sgsa_rope_qkv(const void *qkv, const float *cos_sin, void *q, void *k, void *v, int B, int T,
+                  int H, int D, int pos0, int dtype, void *stream);
+
+/* Epilogue of an SGSA layer's fused input projection proj [rows, ld] whose column
+ * blocks are q | k | v | mix (H*D each) | iq | ik (H*DI each) | beta | gamma (H each):
+ * q, k l2-normalised per head, mix = sigmoid, beta = max(sigmoid, 1e-4), gamma =
+ * sigmoid (SGSAStateLayer, modelings/modeling_sgsa.py:538-539; mix gate of
+ * modelings/hybrid_dense_delta_topk.py:389).  Outputs [rows, H, *]. */
+int sgsa_layer_proj(const void *proj, int ld, void *q, void *k, void *v, void *mix, void *iq,
+                    void *ik, void *beta, void *gamma, long long rows, int H, int D, int DI,
+                    int dtype, void *stream);
+
+/* out [rows, N] = table[ids]; ids outside [0, vocab) give zero rows.
+ * Replaces embed_tokens (modelings/hybrid_dense_delta_topk.py:447). */
+int sgsa_embed(const int64_t *ids, const void *table, void *out, long long rows, int N, int vocab,
+               int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

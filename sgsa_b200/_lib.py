@@ -36,6 +36,11 @@ SIGNATURES = {
     "sgsa_sparse_attn_thresholds": (_i, [_vp] * 7 + [_i] + [_vp] * 3 + [_i] * 6 +
                                     [ctypes.c_float, _i, _i, _vp]),
     "sgsa_sparse_retrieve": (_i, [_vp] * 6 + [_i] * 6 + [ctypes.c_float, _i, _vp]),
+    "sgsa_rmsnorm": (_i, [_vp] * 3 + [ctypes.c_longlong, _i, ctypes.c_float, _i, _vp]),
+    "sgsa_swiglu": (_i, [_vp] * 2 + [ctypes.c_longlong, _i, _i, _vp]),
+    "sgsa_rope_qkv": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),
+    "sgsa_layer_proj": (_i, [_vp, _i] + [_vp] * 8 + [ctypes.c_longlong] + [_i] * 4 + [_vp]),
+    "sgsa_embed": (_i, [_vp] * 3 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_gate_mix": (_i, [_vp] * 4 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
     "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),

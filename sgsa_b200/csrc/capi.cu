@@ -349,4 +349,65 @@ int sgsa_decode_attn_mix(const void *q, const void *k_cache, const void *v_cache
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+// ---- hybrid model kernels ----
+
+int sgsa_rmsnorm(const void *x, const void *weight, void *out, long long rows, int N, float eps,
+                 int dtype, void *stream) {
+    if (rows < 0 || N <= 0 || N % 8) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (rows == 0) return SGSA_OK;
+    if (!x || !weight || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_rmsnorm(x, weight, out, rows, N, eps, dtype, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_swiglu(const void *gate_up, void *out, long long rows, int I, int dtype, void *stream) {
+    if (rows < 0 || I <= 0 || I % 8) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (rows == 0) return SGSA_OK;
+    if (!gate_up || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_swiglu(gate_up, out, rows, I, dtype, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_rope_qkv(const void *qkv, const float *cos_sin, void *q, void *k, void *v, int B, int T,
+                  int H, int D, int pos0, int dtype, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || pos0 < 0 || D <= 0 || D % 8) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!qkv || !cos_sin || !q || !k || !v) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_rope_qkv(qkv, cos_sin, q, k, v, B, T, H, D, pos0, dtype,
+                                          (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_layer_proj(const void *proj, int ld, void *q, void *k, void *v, void *mix, void *iq,
+                    void *ik, void *beta, void *gamma, long long rows, int H, int D, int DI,
+                    int dtype, void *stream) {
+    if (rows < 0 || H <= 0 || H > 256 || D <= 0 || DI <= 0) return SGSA_ERR_SHAPE;
+    if ((H * D) % 8 || (H * DI) % 8 || ld % 8 || ld < 4 * H * D + 2 * H * DI + 2 * H)
+        return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (rows == 0) return SGSA_OK;
+    if (!proj || !q || !k || !v || !mix || !iq || !ik || !beta || !gamma) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_sgsa_proj(proj, ld, q, k, v, mix, iq, ik, beta, gamma, rows, H,
+                                           D, DI, dtype, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_embed(const int64_t *ids, const void *table, void *out, long long rows, int N, int vocab,
+               int dtype, void *stream) {
+    if (rows < 0 || N <= 0 || N % 8 || vocab <= 0) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if (rows == 0) return SGSA_OK;
+    if (!ids || !table || !out) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_embed(ids, table, out, rows, N, vocab, dtype, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
 }  // extern "C"

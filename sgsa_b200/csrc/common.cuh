@@ -40,6 +40,17 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
 cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
                                    void *khat, void *vhat, int B, int T, int H, int D, int K,
                                    float scale, int HI, int dtype, cudaStream_t st);
+cudaError_t launch_rmsnorm(const void *x, const void *w, void *out, long long rows, int N,
+                           float eps, int dtype, cudaStream_t st);
+cudaError_t launch_swiglu(const void *gu, void *out, long long rows, int I, int dtype,
+                          cudaStream_t st);
+cudaError_t launch_rope_qkv(const void *qkv, const float *cs, void *q, void *k, void *v, int B,
+                            int T, int H, int D, int pos0, int dtype, cudaStream_t st);
+cudaError_t launch_sgsa_proj(const void *P, int ld, void *q, void *k, void *v, void *mix,
+                             void *iq, void *ik, void *beta, void *gamma, long long rows, int H,
+                             int D, int DI, int dtype, cudaStream_t st);
+cudaError_t launch_embed(const int64_t *ids, const void *table, void *out, long long rows, int N,
+                         int vocab, int dtype, cudaStream_t st);
 cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
                             long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
 unsigned int read_attn_watchdog(cudaStream_t st);

@@ -15,6 +15,8 @@ writes small ``.npz`` fixtures next to this script:
   iq . ik^T of the fp32 CPU configuration (top-k 128, indexer dim 32).
 * ``retriever_token.npz``  -- ``SparseRetriever._token_only`` (modelings/modeling_sgsa.py:113-142):
   the retrieval k_hat / v_hat of the sparse-write SGSA block.
+* ``dense_block_ref.npz``  -- ``HybridDenseDeltaTopKBlock`` layer 0 (a dense block:
+  RMSNorm, RoPE, causal softmax attention, SwiGLU; hybrid_dense_delta_topk.py:97-243,394-431).
 * ``sparse_attn_ref.npz``  -- ``TopKSparseKVReuseAttention.forward``
   (modelings/hybrid_dense_delta_topk.py:330-358) with identity projections and
   identity RoPE, then the gate of hybrid_dense_delta_topk.py:389-390.
@@ -149,6 +151,25 @@ def main(ref_root: str) -> None:
                         q=qr.transpose(1, 2).numpy(), k=kk.transpose(1, 2).numpy(),
                         v=vr.transpose(1, 2).numpy(), k_hat=res["k_hat"].transpose(1, 2).numpy(),
                         v_hat=res["v_hat"].transpose(1, 2).numpy(), top_k=kr)
+
+    # (7) one dense block of the hybrid model (RMSNorm, RoPE, causal softmax attention,
+    #     SwiGLU, residuals): HybridDenseDeltaTopKBlock layer 0, float64, weights std 0.1
+    from modelings.hybrid_dense_delta_topk import (HybridDenseDeltaTopKBlock,
+                                                    HybridDenseDeltaTopKCache,
+                                                    _build_rope_cache)
+    torch.manual_seed(4)
+    cfgd = HybridDenseDeltaTopKConfig(vocab_size=64, hidden_size=64, intermediate_size=96,
+                                      num_hidden_layers=1, num_attention_heads=2)
+    blk = HybridDenseDeltaTopKBlock(cfgd, 0).double()
+    with torch.no_grad():
+        for prm in blk.parameters():
+            prm.copy_(torch.randn_like(prm) * 0.1 + (1.0 if prm.dim() == 1 else 0.0))
+        xd = torch.randn(2, 40, 64, dtype=torch.float64)
+        rope = _build_rope_cache(40, cfgd.head_dim, cfgd.rope_theta, xd.device, xd.dtype)
+        yd = blk(xd, rope, None, HybridDenseDeltaTopKCache(), False)
+    w = {n.replace(".", "_"): prm.detach().numpy() for n, prm in blk.named_parameters()}
+    np.savez_compressed(os.path.join(HERE, "dense_block_ref.npz"), x=xd.numpy(), y=yd.numpy(),
+                        heads=2, eps=cfgd.layer_norm_eps, theta=cfgd.rope_theta, **w)
     print("golden fixtures written to", HERE)
 
 

@@ -1,0 +1,99 @@
+"""The hybrid model (dense + SGSA layers) on the GPU against the CPU oracle.
+
+Kernel tolerances: float32 1e-5 relative L2; bf16 8e-3 (one rounding of the output).
+Whole-model logits: float32 1e-4 (two dozen chained GEMMs); bf16 models are checked
+against the oracle run on the same bf16 weights at 4e-2 (bf16 activations between
+every op, and top-k sets that can change where bf16 rounding reorders near ties).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hybrid as ohybrid
+from oracle import oracle
+from sgsa_b200 import hybrid
+from sgsa_b200.hybrid import HybridConfig, HybridSGSAModel
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+TOL = {torch.float32: 1e-5, torch.bfloat16: 8e-3}
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rmsnorm_swiglu_embed(dtype):
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(37, 256, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(256, generator=g)).to(dtype)
+    y = hybrid.rmsnorm(x.cuda(), w.cuda(), 1e-6).cpu()
+    ref = ohybrid.rmsnorm(x.double(), w.double(), 1e-6)
+    assert oracle.rel_l2(y.float().numpy(), ref.numpy()) < TOL[dtype]
+    gu = torch.randn(19, 2 * 96, generator=g).to(dtype)
+    y = hybrid.swiglu(gu.cuda()).cpu()
+    gd = gu.double()
+    ref = torch.nn.functional.silu(gd[:, :96]) * gd[:, 96:]
+    assert oracle.rel_l2(y.float().numpy(), ref.numpy()) < TOL[dtype]
+    tab = torch.randn(50, 64, generator=g).to(dtype)
+    ids = torch.tensor([[3, 0, 49, 7], [50, -1, 1, 2]])
+    e = hybrid.embed(ids.cuda(), tab.cuda()).cpu()
+    assert torch.equal(e[0], tab[[3, 0, 49, 7]])
+    assert torch.equal(e[1, 2:], tab[[1, 2]]) and float(e[1, :2].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rope_qkv(dtype):
+    g = torch.Generator().manual_seed(1)
+    B, T, H, D = 2, 33, 3, 64
+    qkv = torch.randn(B, T, 3 * H * D, generator=g).to(dtype)
+    cs = hybrid.rope_table(T, D, 10000.0, "cuda")
+    q, k, v = hybrid.rope_qkv(qkv.cuda(), cs, H)
+    cos, sin = ohybrid.rope_tables(T, D, 10000.0)
+    x = qkv.double().view(B, T, 3, H, D)
+    assert oracle.rel_l2(q.float().cpu().numpy(), ohybrid.apply_rope(x[:, :, 0], cos, sin).numpy()) < TOL[dtype]
+    assert oracle.rel_l2(k.float().cpu().numpy(), ohybrid.apply_rope(x[:, :, 1], cos, sin).numpy()) < TOL[dtype]
+    assert torch.equal(v.cpu(), qkv.view(B, T, 3, H, D)[:, :, 2])
+
+
+def test_layer_proj_matches_oracle():
+    g = torch.Generator().manual_seed(2)
+    H, D, DI = 4, 32, 32
+    cfg = HybridConfig(hidden_size=H * D, num_heads=H, indexer_dim=DI)
+    P = torch.randn(2, 9, cfg.proj_width, generator=g)
+    a = hybrid.layer_proj(P.cuda(), H, D, DI)
+    n = 4 * H * D + 2 * H * DI + 2 * H
+    ref = ohybrid.sgsa_projection(P.double()[..., :n], torch.eye(n, dtype=torch.float64),
+                                  torch.zeros(n, dtype=torch.float64), H, D, DI)
+    for name, r in ref.items():
+        assert oracle.rel_l2(a[name].cpu().numpy(), r.numpy()) < 1e-6, name
+
+
+def test_dense_block_matches_reference_fixture():
+    z = np.load(os.path.join(GOLDEN, "dense_block_ref.npz"))
+    cfg = HybridConfig(vocab_size=64, hidden_size=64, intermediate_size=96, num_layers=1,
+                       num_heads=int(z["heads"]), eps=float(z["eps"]))
+    m = HybridSGSAModel(cfg, device="cuda", dtype=torch.float32)
+    t = lambda n: torch.from_numpy(z[n]).float().cuda()
+    lw = dict(norm1=t("input_norm_weight"), norm2=t("post_attention_norm_weight"),
+              w_qkv=torch.cat([t("attention_q_proj_weight"), t("attention_k_proj_weight"),
+                               t("attention_v_proj_weight")]),
+              w_o=t("attention_o_proj_weight"),
+              w_gu=torch.cat([t("mlp_gate_proj_weight"), t("mlp_up_proj_weight")]),
+              w_down=t("mlp_down_proj_weight"))
+    x = t("x")
+    with torch.no_grad():
+        h = hybrid.rmsnorm(x, lw["norm1"], cfg.eps)
+        y = m.mlp(m.dense_attention(h, lw, x), lw)
+    assert oracle.rel_l2(y.cpu().numpy(), z["y"]) < 1e-5
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-4), (torch.bfloat16, 4e-2)])
+def test_tiny_model_logits_match_oracle(dtype, tol):
+    cfg = hybrid.TINY
+    m = HybridSGSAModel(cfg, device="cuda", dtype=dtype, seed=3)
+    ids = torch.randint(1, cfg.vocab_size, (2, 256), generator=torch.Generator().manual_seed(5))
+    logits = m(ids.cuda()).float().cpu()
+    ref = ohybrid.model_forward(ids, m.weights, cfg)
+    assert oracle.rel_l2(logits.numpy(), ref.numpy()) < tol
+    last = m(ids.cuda(), last_only=True).float().cpu()
+    assert oracle.rel_l2(last.numpy(), logits[:, -1].numpy()) < (1e-6 if dtype == torch.float32 else 1e-2)
