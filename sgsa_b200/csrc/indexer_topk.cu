@@ -215,6 +215,10 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 static __device__ unsigned int g_index_watchdog;
 
 constexpr int kFastBase = 0x800 + (111 << 3);  // key>>20 of 2^-16
+// Rows whose k-th score is expected below the median (K > half the row) bin the
+// negative scores instead: the order-preserving key of -v for v in (2^-16, 2^16]
+// has key>>20 in [kFastBaseNeg, kFastBaseNeg + 255].
+constexpr int kFastBaseNeg = 0x7ff - ((142 << 3) | 7);
 constexpr int kEpiThreads = 256;
 
 struct RowSel {
@@ -224,6 +228,8 @@ struct RowSel {
     bool done;
     bool plain;  // the row left the fast window: full order-preserving keys
     bool exact;  // resolved with every key of the final group selected (no tie cut)
+    int cnt;     // keys in the bin chosen by the last pass
+    bool cand;   // this pass gathers the row's remaining candidate keys instead of counting
 };
 
 // Key of a score for a row whose k-th score is a positive float: the raw bits
@@ -241,7 +247,8 @@ __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, in
 // Choose the bin holding the need-th largest remaining key.  FAST: the
 // first-pass clamped 12-bit digit.
 template <bool PACKED, bool FAST>
-__device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int col, int K) {
+__device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int col, int K,
+                                           bool neg = false) {
     const int w = FAST ? 8 : min(8, s.top);
     int cum = 0, chosen = 0, cnt = 0;
     for (int bin = (1 << w) - 1; bin >= 0; --bin) {
@@ -252,12 +259,14 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
     if (FAST) {
         if (chosen == 0 || chosen == 255) {  // outside the fast window: plain radix
             s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32; s.plain = true;
+            s.cnt = 0x7fffffff;
             return;
         }
         s.need -= cum;
-        s.prefix = (uint32_t)(kFastBase + chosen) << 20;
+        s.prefix = (uint32_t)((neg ? kFastBaseNeg : kFastBase) + chosen) << 20;
         s.mask = 0xfff00000u;
         s.top = 20;
+        s.plain = neg;  // the negative window continues on the order-preserving keys
     } else {
         const int shift = s.top - w;
         s.need -= cum;
@@ -265,8 +274,109 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
         s.mask |= ((1u << w) - 1u) << shift;
         s.top = shift;
     }
+    s.cnt = cnt;
     if (cnt == s.need) s.exact = true;
     if (cnt == s.need || s.top == 0) s.done = true;
+}
+
+// Candidate mode.  Once the chosen bin of a row holds at most kCandCap keys, the
+// next pass stores those keys (the row's two threads from the two ends of the
+// row's histogram column) instead of counting a digit, and the row's k-th key is
+// then found among them: bit by bit from the highest unknown bit, keep a bit if at
+// least `need` candidates are >= the prefix with it set.  Exact, and it replaces
+// the remaining digit passes (usually two or three) by one.
+__device__ __forceinline__ void epi_bar() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
+}
+
+template <bool PACKED>
+struct Cand {
+    static constexpr int kCap = PACKED ? 128 : 256;  // 32-bit slots of a histogram column
+};
+
+__device__ __forceinline__ void st_shared_if(uint32_t addr, uint32_t v, bool pred) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p st.shared.u32 [%0], %1;\n\t}" ::"r"(addr),
+                 "r"(v), "r"((uint32_t)pred)
+                 : "memory");
+}
+
+// Candidate gathering of one 32-column chunk: predicated stores, no branches.
+// `slot` is the shared-memory address of this thread's next slot and `step` the
+// byte step between slots (+/- one histogram row); n counts the stored keys.
+template <bool PLAIN, bool FULL, int CAP>
+__device__ __forceinline__ void cand_chunk(const float (&v)[32], uint32_t &slot, int step, int jb,
+                                           int nvalid, const RowSel &s, int &n) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t u = PLAIN ? float_key(v[i]) : fast_key(v[i]);
+        const bool in = (FULL || jb + i < nvalid) && (u & s.mask) == s.prefix && n < CAP;
+        st_shared_if(slot, u, in);
+        slot += in ? step : 0;
+        n += in;
+    }
+}
+
+// The need-th largest of a row's candidates, found two bits at a time from the top
+// unknown bit: both threads of the row count their own list against the three
+// extensions of the prefix, swap the counts through shared memory and take the
+// largest extension that still has `need` keys at or above it.  All epilogue
+// threads run every step (the barriers are CTA-wide); rows not in candidate mode
+// only take part in the barriers.
+template <int CAP>
+__device__ __forceinline__ void cand_resolve(RowSel &s, bool act_row, const uint32_t *col, int n,
+                                             int half, uint32_t (*xch)[2][kRows], int row) {
+    const int cstep = half ? -kRows : kRows;
+    const uint32_t *first = col + (half ? (CAP - 1) * kRows : 0);
+    uint32_t x = s.prefix;
+    int it = 0;
+    for (int gb = 30; gb >= 0; gb -= 2, ++it) {
+        const bool act = act_row && gb + 2 <= s.top;
+        uint32_t pk = 0;
+        if (act) {
+            const uint32_t c1 = x | (1u << gb), c2 = x | (2u << gb), c3 = x | (3u << gb);
+            int k1 = 0, k2 = 0, k3 = 0;
+            for (int i = 0; i < n; ++i) {
+                const uint32_t v = first[i * cstep];
+                k1 += v >= c1;
+                k2 += v >= c2;
+                k3 += v >= c3;
+            }
+            pk = (uint32_t)k1 | ((uint32_t)k2 << 10) | ((uint32_t)k3 << 20);
+            xch[it & 1][half][row] = pk;
+        }
+        epi_bar();
+        if (act) {
+            const uint32_t o = xch[it & 1][half ^ 1][row];
+            const int need = s.need;
+            const int k3 = (int)((pk >> 20) + (o >> 20));
+            const int k2 = (int)(((pk >> 10) & 1023u) + ((o >> 10) & 1023u));
+            const int k1 = (int)((pk & 1023u) + (o & 1023u));
+            x |= (k3 >= need ? 3u : k2 >= need ? 2u : k1 >= need ? 1u : 0u) << gb;
+        }
+    }
+    uint32_t pk = 0;
+    if (act_row) {
+        int gt = 0, eq = 0;
+        for (int i = 0; i < n; ++i) {
+            const uint32_t v = first[i * cstep];
+            gt += v > x;
+            eq += v == x;
+        }
+        pk = (uint32_t)gt | ((uint32_t)eq << 10);
+        xch[it & 1][half][row] = pk;
+    }
+    epi_bar();
+    if (act_row) {
+        const uint32_t o = xch[it & 1][half ^ 1][row];
+        const int gt = (int)((pk & 1023u) + (o & 1023u));
+        const int eq = (int)((pk >> 10) + (o >> 10));
+        s.need -= gt;
+        s.prefix = x;
+        s.mask = 0xffffffffu;
+        s.top = 0;
+        s.done = true;
+        s.exact = eq == s.need;
+    }
 }
 
 template <int DI, bool PACKED>
@@ -294,9 +404,6 @@ __device__ __forceinline__ void red_shared_if(uint32_t *addr, uint32_t inc, bool
                  : "memory");
 }
 
-__device__ __forceinline__ void epi_bar() {
-    asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
-}
 
 // Histogram update of one 32-column chunk.  FAST: clamped 12-bit first digit
 // (taken from the arithmetic shift of the raw bits: negative scores land in
@@ -316,7 +423,10 @@ __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol,
         uint32_t d;
         bool in;
         if (FAST) {
-            d = (uint32_t)min(max((__float_as_int(v[i]) >> 20) - (kFastBase - 0x800), 0), 255);
+            if (PLAIN)  // negative window (PLAIN selects it in the first pass)
+                d = (uint32_t)min(max((int)(float_key(v[i]) >> 20) - kFastBaseNeg, 0), 255);
+            else
+                d = (uint32_t)min(max((__float_as_int(v[i]) >> 20) - (kFastBase - 0x800), 0), 255);
             in = ok;
         } else {
             const uint32_t u = PLAIN ? float_key(v[i]) : fast_key(v[i]);
@@ -365,6 +475,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     uint64_t *full = bars, *empty = bars + C::kStages, *tfull = bars + 2 * C::kStages,
              *tempty = tfull + C::kAcc, *qbar = tempty + C::kAcc;
     __shared__ uint32_t s_tmem;
+    __shared__ uint32_t s_xch[2][2][kRows];
+    constexpr int kCap = Cand<PACKED>::kCap;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int BH = B * H;
@@ -383,6 +495,9 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
     const bool has_row = epi && t < T;
+    // first-pass window of this warp's rows (warp-uniform): the negative one when
+    // K exceeds half of the warp's middle row
+    const bool neg_w = 2 * K > q0 + quad * 32 + 16 + 1;
     int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
     uint4 *thr_row = (has_row && thr) ? thr + (size_t)bh * T + t : nullptr;
     RowSel s{0u, 0u, K, 32, true, false, true};
@@ -421,6 +536,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     constexpr int kChunksPerHalf = C::kN / 64;
     uint32_t it_p = 0, it_m = 0, it_e = 0;
     bool collecting = false;
+    bool cand_pass = false;  // CTA-uniform: some row gathers candidates in this pass
     for (int pass = 0;; ++pass) {
         if (warp == 0) {
             if (lane == 0) {
@@ -471,12 +587,15 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             uint32_t *hcol = hist + row;
             const bool collect = collecting && half == 0 && has_row && nvalid > K;
             if (!collecting) {
-                if (half == 0 && active)
+                if (half == 0 && active && !s.cand)
                     for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
                 epi_bar();
             }
             uint32_t *ring = hist + row;  // the histogram is idle during the collect pass
-            int pos = 0, taken = 0, flushed = 0, lastj = -1;
+            int pos = 0, taken = 0, flushed = 0, lastj = -1, ncand = 0;
+            // candidate slots: half 0 from the front of the row's column, half 1 from the back
+            uint32_t cslot = (uint32_t)__cvta_generic_to_shared(hcol + (half ? (kCap - 1) * kRows : 0));
+            const int cstep = half ? -(int)(kRows * 4) : (int)(kRows * 4);
             for (int kt = 0; kt < nkt; ++kt, ++it_e) {
                 const uint32_t buf = it_e % C::kAcc, bph = (it_e / C::kAcc) & 1;
                 mbar_wait(&tfull[buf], bph, wd, 16u);
@@ -490,9 +609,22 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         tmem_ld32(taddr + c * 32, v);
                         const int jb = kt * C::kN + c * 32;
                         if (!active || jb >= nvalid) continue;
-                        if (pass == 0) {
-                            if (full_tile) hist_chunk<true, false, true, PACKED>(v, hcol, jb, nvalid, s);
-                            else hist_chunk<true, false, false, PACKED>(v, hcol, jb, nvalid, s);
+                        if (s.cand) {
+                            if (!s.plain) {
+                                if (full_tile) cand_chunk<false, true, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
+                                else cand_chunk<false, false, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
+                            } else {
+                                if (full_tile) cand_chunk<true, true, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
+                                else cand_chunk<true, false, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
+                            }
+                        } else if (pass == 0) {
+                            if (neg_w) {
+                                if (full_tile) hist_chunk<true, true, true, PACKED>(v, hcol, jb, nvalid, s);
+                                else hist_chunk<true, true, false, PACKED>(v, hcol, jb, nvalid, s);
+                            } else {
+                                if (full_tile) hist_chunk<true, false, true, PACKED>(v, hcol, jb, nvalid, s);
+                                else hist_chunk<true, false, false, PACKED>(v, hcol, jb, nvalid, s);
+                            }
                         } else if (!s.plain) {
                             if (full_tile) hist_chunk<false, false, true, PACKED>(v, hcol, jb, nvalid, s);
                             else hist_chunk<false, false, false, PACKED>(v, hcol, jb, nvalid, s);
@@ -526,11 +658,16 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
             if (!collecting) {
-                epi_bar();  // every reduction of the pass has landed
-                if (active) {
-                    if (pass == 0) row_choose<PACKED, true>(s, hist, row, K);
+                epi_bar();  // every reduction / candidate of the pass has landed
+                if (cand_pass) cand_resolve<kCap>(s, active && s.cand, hcol, ncand, half, s_xch, row);
+                if (active && !s.cand) {
+                    if (pass == 0) row_choose<PACKED, true>(s, hist, row, K, neg_w);
                     else row_choose<PACKED, false>(s, hist, row, K);
                 }
+                // candidate mode only for whole warps: a warp mixing the two kinds of
+                // pass would run both code paths
+                const bool fits = __all_sync(0xffffffffu, s.done || s.cnt <= kCap);
+                if (!s.done && fits) s.cand = true;
             } else if (collect) {
                 if (out_row)
                     for (int i = min(pos, K); i < K; ++i) out_row[i] = -1;
@@ -539,12 +676,13 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             }
         }
         const int more = __syncthreads_or(epi && !s.done);
+        cand_pass = __syncthreads_or(epi && !s.done && s.cand);
         if (collecting) break;
         if (!more || pass + 1 >= kMaxDigitPasses) {
             // Without index rows to write, the collect pass only finds the tie cut of
             // rows whose k-th key is an exact tie; if there is none, it is skipped.
             if (!idx) {
-                const bool ties = __syncthreads_or(epi && has_row && nvalid > K && !s.exact);
+                const bool ties = __syncthreads_or(epi && half == 0 && has_row && nvalid > K && !s.exact);
                 if (!ties) {
                     if (epi && half == 0 && thr_row && nvalid > K)
                         *thr_row = make_uint4(s.prefix, s.mask, 0x7fffffffu, 1u);
