@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "../../include/sgsa_b200.h"
+#include "select_keys.cuh"
 
 namespace sgsa {
 
@@ -21,13 +22,6 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
     return __float2bfloat16_rn(x);
 }
 
-// Orderable 32-bit key of a float: a > b  <=>  key(a) > key(b) (no NaNs);
-// -0.0 and +0.0 compare equal, as they do as floats.
-__device__ __forceinline__ uint32_t float_key(float f) {
-    uint32_t u = __float_as_uint(f);
-    if ((u << 1) == 0u) u = 0u;
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
 

@@ -214,11 +214,6 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 // no returned values, and the two threads of a row may share a counter.
 static __device__ unsigned int g_index_watchdog;
 
-constexpr int kFastBase = 0x800 + (111 << 3);  // key>>20 of 2^-16
-// Rows whose k-th score is expected below the median (K > half the row) bin the
-// negative scores instead: the order-preserving key of -v for v in (2^-16, 2^16]
-// has key>>20 in [kFastBaseNeg, kFastBaseNeg + 255].
-constexpr int kFastBaseNeg = 0x7ff - ((142 << 3) | 7);
 constexpr int kEpiThreads = 256;
 
 struct RowSel {
@@ -230,13 +225,15 @@ struct RowSel {
     bool exact;  // resolved with every key of the final group selected (no tie cut)
     int cnt;     // keys in the bin chosen by the last pass
     bool cand;   // this pass gathers the row's remaining candidate keys instead of counting
+    bool fast;   // this pass bins the fast digit (mode, pb)
+    int mode;
+    int pb;
 };
 
 // Key of a score for a row whose k-th score is a positive float: the raw bits
 // with the sign flipped order every positive score correctly and put every
 // negative one (and -0.0) below any positive prefix, which is all the
 // comparisons against such a prefix need.
-__device__ __forceinline__ uint32_t fast_key(float f) { return __float_as_uint(f) ^ 0x80000000u; }
 
 template <bool PACKED>
 __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, int col) {
@@ -245,10 +242,9 @@ __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, in
 }
 
 // Choose the bin holding the need-th largest remaining key.  FAST: the
-// first-pass clamped 12-bit digit.
+// fast-digit pass of the row's window.
 template <bool PACKED, bool FAST>
-__device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int col, int K,
-                                           bool neg = false) {
+__device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int col, int K) {
     const int w = FAST ? 8 : min(8, s.top);
     int cum = 0, chosen = 0, cnt = 0;
     for (int bin = (1 << w) - 1; bin >= 0; --bin) {
@@ -257,16 +253,27 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
         cum += cnt;
     }
     if (FAST) {
-        if (chosen == 0 || chosen == 255) {  // outside the fast window: plain radix
-            s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32; s.plain = true;
+        if (chosen == 0 || chosen == 255 || (s.mode == 2 && chosen == 127)) {
+            // outside the window: towards zero, retry with both signs; else plain radix
+            const bool toward_zero = s.mode == 0 ? chosen == 0 : s.mode == 1 ? chosen == 255 : false;
+            if (toward_zero) {
+                s.mode = 2;
+                s.fast = true;
+            } else {
+                s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32; s.plain = true;
+                s.fast = false;
+            }
             s.cnt = 0x7fffffff;
             return;
         }
         s.need -= cum;
-        s.prefix = (uint32_t)((neg ? kFastBaseNeg : kFastBase) + chosen) << 20;
-        s.mask = 0xfff00000u;
-        s.top = 20;
-        s.plain = neg;  // the negative window continues on the order-preserving keys
+        s.prefix = fast_prefix(chosen, s.mode, s.pb);
+        const bool two = s.mode == 2;
+        s.mask = two ? 0xfff00000u : 0xfff80000u;
+        s.top = two ? 20 : 19;
+        // negative k-th: continue on the order-preserving keys
+        s.plain = s.mode == 1 || (two && chosen < 128);
+        s.fast = false;
     } else {
         const int shift = s.top - w;
         s.need -= cum;
@@ -329,11 +336,16 @@ __device__ __forceinline__ void cand_resolve(RowSel &s, bool act_row, const uint
     const uint32_t *first = col + (half ? (CAP - 1) * kRows : 0);
     uint32_t x = s.prefix;
     int it = 0;
-    for (int gb = 30; gb >= 0; gb -= 2, ++it) {
-        const bool act = act_row && gb + 2 <= s.top;
+    for (; it < 16; ++it) {
+        // bits [lo, lo + 2) of this row (lo = -1: only bit 0 is left)
+        const int lo = s.top - 2 * (it + 1);
+        const bool act = act_row && lo >= -1;
+        const int gb = max(lo, 0);
+        const uint32_t one = lo < 0 ? 0u : 1u;  // a single bit: only c2 (= bit 0) counts
         uint32_t pk = 0;
         if (act) {
-            const uint32_t c1 = x | (1u << gb), c2 = x | (2u << gb), c3 = x | (3u << gb);
+            const uint32_t c1 = x | (one << gb), c2 = x | (2u << gb >> (1 - one)),
+                           c3 = x | (3u << gb >> (1 - one));
             int k1 = 0, k2 = 0, k3 = 0;
             for (int i = 0; i < n; ++i) {
                 const uint32_t v = first[i * cstep];
@@ -351,7 +363,10 @@ __device__ __forceinline__ void cand_resolve(RowSel &s, bool act_row, const uint
             const int k3 = (int)((pk >> 20) + (o >> 20));
             const int k2 = (int)(((pk >> 10) & 1023u) + ((o >> 10) & 1023u));
             const int k1 = (int)((pk & 1023u) + (o & 1023u));
-            x |= (k3 >= need ? 3u : k2 >= need ? 2u : k1 >= need ? 1u : 0u) << gb;
+            if (one)
+                x |= (k3 >= need ? 3u : k2 >= need ? 2u : k1 >= need ? 1u : 0u) << gb;
+            else
+                x |= k2 >= need ? 1u : 0u;
         }
     }
     uint32_t pk = 0;
@@ -405,11 +420,11 @@ __device__ __forceinline__ void red_shared_if(uint32_t *addr, uint32_t inc, bool
 }
 
 
-// Histogram update of one 32-column chunk.  FAST: clamped 12-bit first digit
-// (taken from the arithmetic shift of the raw bits: negative scores land in
-// bin 0); else the row's next digit among keys matching its prefix, with keys
-// from float_key (PLAIN) or fast_key.  FULL skips the causal bound check.
-template <bool FAST, bool PLAIN, bool FULL, bool PACKED>
+// Histogram update of one 32-column chunk.  FAST: the fast digit of the row's
+// window (fast_digit); else the row's next digit among keys
+// matching its prefix, with keys from float_key (PLAIN) or fast_key.  FULL skips
+// the causal bound check.
+template <bool FAST, bool PLAIN, bool FULL, bool PACKED, int MODE = 0>
 __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol, int jb,
                                            int nvalid, const RowSel &s) {
     // u >> shift as a high multiply (no variable-amount shift in the loop)
@@ -423,10 +438,7 @@ __device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol,
         uint32_t d;
         bool in;
         if (FAST) {
-            if (PLAIN)  // negative window (PLAIN selects it in the first pass)
-                d = (uint32_t)min(max((int)(float_key(v[i]) >> 20) - kFastBaseNeg, 0), 255);
-            else
-                d = (uint32_t)min(max((__float_as_int(v[i]) >> 20) - (kFastBase - 0x800), 0), 255);
+            d = fast_digit_m<MODE>(v[i], s.pb);
             in = ok;
         } else {
             const uint32_t u = PLAIN ? float_key(v[i]) : fast_key(v[i]);
@@ -476,6 +488,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
              *tempty = tfull + C::kAcc, *qbar = tempty + C::kAcc;
     __shared__ uint32_t s_tmem;
     __shared__ uint32_t s_xch[2][2][kRows];
+    __shared__ uint32_t s_amax;  // largest |score| bits of the first key tile's sample
     constexpr int kCap = Cand<PACKED>::kCap;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -495,12 +508,9 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
     const bool has_row = epi && t < T;
-    // first-pass window of this warp's rows (warp-uniform): the negative one when
-    // K exceeds half of the warp's middle row
-    const bool neg_w = 2 * K > q0 + quad * 32 + 16 + 1;
     int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
     uint4 *thr_row = (has_row && thr) ? thr + (size_t)bh * T + t : nullptr;
-    RowSel s{0u, 0u, K, 32, true, false, true};
+    RowSel s{0u, 0u, K, 32, true, false, true, 0, false, false, 0, (kDefaultEtop - 16) << 4};
     if (epi && nvalid > K) {
         s.done = false;
         s.exact = false;
@@ -513,6 +523,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     if (q_last + 1 <= K) return;  // every row of the tile keeps all its columns
 
     if (warp == 0 && lane == 0) {
+        s_amax = 0u;
         for (int i = 0; i < C::kStages; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -532,8 +543,10 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    constexpr int kMaxDigitPasses = 5;  // fast digit + 4 plain digits after a fallback
+    // fast digit, the other-sign retry, 4 plain digits after a fallback, spare
+    constexpr int kMaxDigitPasses = 7;
     constexpr int kChunksPerHalf = C::kN / 64;
+    static_assert(kChunksPerHalf == 1, "the first-tile sample assumes one chunk per thread and tile");
     uint32_t it_p = 0, it_m = 0, it_e = 0;
     bool collecting = false;
     bool cand_pass = false;  // CTA-uniform: some row gathers candidates in this pass
@@ -608,6 +621,35 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         float v[32];
                         tmem_ld32(taddr + c * 32, v);
                         const int jb = kt * C::kN + c * 32;
+                        if (pass == 0 && kt == 0) {
+                            // sample of the first key tile: place every row's fast window
+                            uint32_t amax = 0u;
+                            int np = 0, nv = 0;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                const bool ok = active && jb + i < nvalid;
+                                amax = max(amax, ok ? (__float_as_uint(v[i]) & 0x7fffffffu) : 0u);
+                                np += ok && v[i] > 0.f;
+                                nv += ok;
+                            }
+                            amax = __reduce_max_sync(0xffffffffu, amax);
+                            if (lane == 0) atomicMax(&s_amax, amax);
+                            s_xch[0][half][row] = (uint32_t)np | ((uint32_t)nv << 16);
+                            epi_bar();
+                            const uint32_t o = s_xch[0][half ^ 1][row];
+                            const int npos = np + (int)(o & 0xffffu), nval = nv + (int)(o >> 16);
+                            const int etop = min(max((int)(s_amax >> 23) + 3, 17), 255);  // bottom above 0 and denormals
+                            s.pb = (etop - 16) << 4;
+                            // estimated positives p*(t+1) against need: clear margins pick a sign
+                            const float p = nval ? (float)npos / (float)nval : 0.5f;
+                            const float q = (float)s.need / (float)nvalid;
+                            const int m = p > q + 0.15f ? 0 : p < q - 0.15f ? 1 : 2;
+                            // one formula per warp: a sign only if every active row agrees
+                            const bool all0 = __all_sync(0xffffffffu, !active || m == 0);
+                            const bool all1 = __all_sync(0xffffffffu, !active || m == 1);
+                            s.mode = all0 ? 0 : all1 ? 1 : 2;
+                            s.fast = true;
+                        }
                         if (!active || jb >= nvalid) continue;
                         if (s.cand) {
                             if (!s.plain) {
@@ -617,13 +659,16 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                                 if (full_tile) cand_chunk<true, true, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
                                 else cand_chunk<true, false, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
                             }
-                        } else if (pass == 0) {
-                            if (neg_w) {
-                                if (full_tile) hist_chunk<true, true, true, PACKED>(v, hcol, jb, nvalid, s);
-                                else hist_chunk<true, true, false, PACKED>(v, hcol, jb, nvalid, s);
+                        } else if (s.fast) {
+                            if (s.mode == 0) {
+                                if (full_tile) hist_chunk<true, false, true, PACKED, 0>(v, hcol, jb, nvalid, s);
+                                else hist_chunk<true, false, false, PACKED, 0>(v, hcol, jb, nvalid, s);
+                            } else if (s.mode == 1) {
+                                if (full_tile) hist_chunk<true, false, true, PACKED, 1>(v, hcol, jb, nvalid, s);
+                                else hist_chunk<true, false, false, PACKED, 1>(v, hcol, jb, nvalid, s);
                             } else {
-                                if (full_tile) hist_chunk<true, false, true, PACKED>(v, hcol, jb, nvalid, s);
-                                else hist_chunk<true, false, false, PACKED>(v, hcol, jb, nvalid, s);
+                                if (full_tile) hist_chunk<true, false, true, PACKED, 2>(v, hcol, jb, nvalid, s);
+                                else hist_chunk<true, false, false, PACKED, 2>(v, hcol, jb, nvalid, s);
                             }
                         } else if (!s.plain) {
                             if (full_tile) hist_chunk<false, false, true, PACKED>(v, hcol, jb, nvalid, s);
@@ -661,7 +706,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 epi_bar();  // every reduction / candidate of the pass has landed
                 if (cand_pass) cand_resolve<kCap>(s, active && s.cand, hcol, ncand, half, s_xch, row);
                 if (active && !s.cand) {
-                    if (pass == 0) row_choose<PACKED, true>(s, hist, row, K, neg_w);
+                    if (s.fast) row_choose<PACKED, true>(s, hist, row, K);
                     else row_choose<PACKED, false>(s, hist, row, K);
                 }
                 // candidate mode only for whole warps: a warp mixing the two kinds of

@@ -203,8 +203,14 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         float *xmax = (float *)(sm + L::kBar + 256);  // [2 tiles][kParts][128 rows]
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
         if (valid_row) th = thr[((size_t)b * HI + hi) * T + t];
+        // The threshold as a float: key(s) & mask > prefix, or == prefix and j <= cut, is
+        // s > a || (s == a && j <= cut) with a the float whose key is the prefix (its
+        // unmasked bits are zero; a partial mask always comes with cut = max, which makes
+        // both forms "key(s) >= prefix").  mask 0 selects every column (a = -inf).
         const uint32_t prefix = th.x, mask = th.y;
         const int cut = (int)th.z;
+        const float a_thr = mask == 0u ? -INFINITY
+                                       : __uint_as_float((prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix);
         float m_used = -INFINITY, l = 0.f;
         for (int j = 0; j < nkt; ++j) {
             const int buf = j & 1;
@@ -219,8 +225,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 #pragma unroll
             for (int i = 0; i < kCP; ++i) {
                 const int jj = jb + i;
-                const uint32_t mk = float_key(si[i]) & mask;
-                const bool sel = (full || jj <= t) && (mk > prefix || (mk == prefix && jj <= cut));
+                const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
                 const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
                 x[i] = xv;
                 mt = fmaxf(mt, xv);
