@@ -227,6 +227,7 @@ def stage_times(cfg, d, reps=3, only=None):
                                             st.cuda_stream), "attn")
 
     thr = torch.empty(B, H, T, 4, device="cuda", dtype=torch.int32)
+    norms = torch.empty(2 * B * H, device="cuda", dtype=torch.int32)
 
     def index_thr():
         _lib.check(lib.sgsa_indexer_thresholds(P(d["iq"]), P(d["ik"]), None, P(thr), None, 0, B,
@@ -237,7 +238,8 @@ def stage_times(cfg, d, reps=3, only=None):
         _lib.check(lib.sgsa_sparse_attn_thresholds(P(d["q"]), P(d["k"]), P(d["v"]), P(d["iq"]),
                                                    P(d["ik"]), P(thr), None, 0, P(od), P(d["mix"]),
                                                    P(out), B, T, H, D, cfg.d_idx, H,
-                                                   1.0 / math.sqrt(D), 1, 0, st.cuda_stream),
+                                                   1.0 / math.sqrt(D), 1, 0, P(norms),
+                                                   st.cuda_stream),
                    "attn_tc")
 
     res = {}

@@ -160,6 +160,9 @@ int sgsa_indexer_thresholds(const void *iq, const void *ik, int32_t *indices,
  * [B,T,1,DI] and thresholds [B,1,T,4] are shared by all heads (the DeepSeek-style
  * shared indexer of modelings/deepseek_v3_2.py:435-487, an option: it changes the
  * selection semantics from per-head to per-token).
+ * norm_scratch (optional, 8*B*H bytes, 4-byte aligned): with it the call first
+ * takes max|q|, max|k| per (b,h) and, where their product bounds the scores
+ * tightly enough, runs the softmax against that fixed bound (no running maximum).
  * Replaces modelings/hybrid_dense_delta_topk.py:343-356 and :389-390.
  */
 int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, const void *iq,
@@ -167,7 +170,7 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
                                 const int32_t *q_tiles, int n_tiles, const float *o_delta,
                                 const void *mix, void *out, int B, int T, int H, int D, int DI,
                                 int idx_heads, float scale, int mix_per_channel, int out_f32,
-                                void *stream);
+                                void *norm_scratch, void *stream);
 
 /*
  * Retrieval of the sparse-write SGSA block: k_hat, v_hat [B,T,H,D] (dtype) are

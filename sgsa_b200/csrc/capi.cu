@@ -178,7 +178,7 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
                                 const int32_t *q_tiles, int n_tiles, const float *o_delta,
                                 const void *mix, void *out, int B, int T, int H, int D, int DI,
                                 int idx_heads, float scale, int mix_per_channel, int out_f32,
-                                void *stream) {
+                                void *norm_scratch, void *stream) {
     if (B < 0 || T < 0 || H < 0 || n_tiles < 0) return SGSA_ERR_SHAPE;
     if (idx_heads != 1 && idx_heads != H) return SGSA_ERR_SHAPE;
     if (!sgsa::sparse_attn_tc_eligible(T, D, DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
@@ -187,7 +187,8 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
     if (int s = check_device()) return s;
     cudaError_t e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thresholds, o_delta, mix, out,
                                                 B, T, H, scale, mix_per_channel, q_tiles, n_tiles,
-                                                out_f32 != 0, idx_heads, (cudaStream_t)stream);
+                                                out_f32 != 0, idx_heads, (uint32_t *)norm_scratch,
+                                                (cudaStream_t)stream);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
@@ -225,6 +226,7 @@ size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top
     n += align256((size_t)B * T * H * D * sizeof(float));       // o_delta
     n += align256((size_t)B * H * T * top_k * sizeof(int32_t));  // indices
     n += align256((size_t)B * H * T * 16);                       // per-row selection thresholds
+    n += align256((size_t)B * H * 2 * sizeof(uint32_t));         // max |q|^2, |k|^2 per head
     return n;
 }
 
@@ -248,6 +250,7 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     float *od = (float *)(w + cws);
     int32_t *ix = (int32_t *)(w + cws + align256((size_t)B * T * H * D * sizeof(float)));
     uint32_t *thr = (uint32_t *)((char *)ix + align256((size_t)B * H * T * top_k * sizeof(int32_t)));
+    uint32_t *qkmax = (uint32_t *)((char *)thr + align256((size_t)B * H * T * 16));
     const bool fused = sgsa::indexer_tc_eligible(DI, dtype) &&
                        sgsa::sparse_attn_tc_eligible(T, D, DI, dtype) && fused_attn_enabled();
     if (indices) ix = indices;
@@ -285,7 +288,7 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
         }
         if (e != cudaSuccess) return fail_cuda(e);
         e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
-                                        mix_per_channel, nullptr, 0, false, idx_heads, st);
+                                        mix_per_channel, nullptr, 0, false, idx_heads, qkmax, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
     e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr, initial_state,

@@ -24,9 +24,12 @@
 // the DeepSeek indexer of modelings/deepseek_v3_2.py:435-487) every head reads
 // indexer head 0's vectors and thresholds.
 //
-// Warp roles (96 + 128 kParts threads, one CTA per (b, h, 128-query tile)): warp 0 TMA,
-// warp 1 TMEM owner + MMA issuer, warp 2 TMA of the values, warps 3.. kParts
-// threads per query row.
+// Warp roles (96 + 128 kParts kGroups threads, one CTA per (b, h, 128-query tile)):
+// warp 0 TMA, warp 1 TMEM owner + MMA issuer, warp 2 TMA of the values, warps 3..
+// softmax: two groups that take alternate key tiles (each with its own S and P
+// buffers and its own O accumulator in TMEM, an online softmax each, merged at the
+// end), so that one group's softmax overlaps the other's and the MMAs; kParts
+// threads per query row in each group.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -37,11 +40,11 @@ namespace {
 static __device__ unsigned int g_attn_watchdog;
 
 constexpr int kRowsA = 128;
-constexpr int kNk = 64;  // keys per tile
-constexpr int kParts = 4;              // softmax threads per query row
+constexpr int kNk = 64;                // keys per tile
+constexpr int kGroups = 2;             // softmax groups: alternate key tiles, one O each
+constexpr int kParts = 2;              // threads per query row within a group
 constexpr int kCP = kNk / kParts;      // key columns per thread
-constexpr int kOP = 128 / kParts;      // O columns per thread
-constexpr int kAttnThreads = 96 + 128 * kParts;
+constexpr int kAttnThreads = 96 + 128 * kParts * kGroups;
 constexpr int kKS = 3;                 // stages of the (indexer key, key) ring
 constexpr int kVS = 2;                 // stages of the value ring
 namespace L {
@@ -51,11 +54,15 @@ constexpr int kKStage = kIQ + 16384;     // kKS stages x 24 KB: IK 8 KB | K 2 x 
 constexpr int kKBytes = 24576;
 constexpr int kVStage = kKStage + kKS * kKBytes;  // kVS stages x 16 KB: V 2 x 8 KB
 constexpr int kVBytes = 16384;
-constexpr int kP = kVStage + kVS * kVBytes;  // 2 buffers x (hi 16 KB | lo 16 KB)
-constexpr int kBar = kP + 2 * 32768;
-constexpr int kBytes = kBar + 256 + 2 * kParts * 128 * 4;  // barriers | tile maxima
+constexpr int kP = kVStage + kVS * kVBytes;  // one P buffer per group: hi 16 KB | lo 16 KB
+constexpr int kBar = kP + kGroups * 32768;
+constexpr int kXmax = kBar + 256;                            // [group][slot][part][row] floats
+constexpr int kMrow = kXmax + kGroups * 2 * kParts * 128 * 4;  // [group][row]
+constexpr int kLrow = kMrow + kGroups * 128 * 4;             // [group][part][row]
+constexpr int kBytes = kLrow + kGroups * kParts * 128 * 4;
 constexpr size_t kSmem = 1024 + kBytes;
 }  // namespace L
+static_assert(L::kSmem <= 232448, "shared memory");
 
 template <typename Tmix, typename Tout>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -66,7 +73,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_ik, const uint4 *__restrict__ thr,
                       const float *__restrict__ od, const Tmix *__restrict__ mix,
                       Tout *__restrict__ out, int B, int T, int H, float scale_log2,
-                      int mix_pc, int nqt, const int32_t *__restrict__ q_tiles, int HI) {
+                      int mix_pc, int nqt, const int32_t *__restrict__ q_tiles, int HI,
+                      const uint32_t *__restrict__ qkmax) {
     using namespace sm100;
     constexpr int D = 128;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -97,7 +105,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_init(&vfull[i], 1);
             mbar_init(&vempty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < 2; ++i) {  // per group (= per S / P buffer)
             mbar_init(&sfull[i], 1);
             mbar_init(&sfree[i], 4 * kParts);
             mbar_init(&pfull[i], 4 * kParts);
@@ -110,7 +118,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    // TMEM columns: Sidx[2] at 0/64, S[2] at 128/192, O at 256..383
+    // TMEM columns: Sidx[g] at 0/64, S[g] at 128/192, O[g] at 256/384
     const uint32_t tSidx = tmem, tS = tmem + 128, tO = tmem + 256;
 
     if (warp == 0) {  // producer of the query tiles and the (indexer key, key) ring
@@ -150,57 +158,81 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             constexpr uint32_t id_pv = idesc_bf16_f32_bmn(128, D);
             const uint32_t aq = smem_u32(sm + L::kQ), aiq = smem_u32(sm + L::kIQ);
             mbar_wait(qfull, 0, wd, 2u);
-            auto issue_pv = [&](int jj) {
-                const int pb = jj & 1;
-                const int vs = jj % kVS;
-                mbar_wait(&vfull[vs], (jj / kVS) & 1, wd, 4u);
-                mbar_wait(&pfull[pb], (jj >> 1) & 1, wd, 4u);
-                tc_fence_after();
-                const uint32_t ph = smem_u32(sm + L::kP + pb * 32768);
-                const uint32_t vq = smem_u32(sm + L::kVStage + vs * L::kVBytes);
+            // Event-driven issue: S(js) as soon as its key tile has landed and its group has
+            // read S(js - 2); PV(jp), in order, as soon as P(jp) and V(jp) are there.  S can
+            // so run ahead of a group's softmax instead of waiting behind the other's PV.
+            int js = 0, jp = 0;
+            uint32_t idle = 0;
+            while (jp < nkt) {
+                bool progress = false;
+                if (js < nkt) {
+                    const int st = js % kKS, buf = js & 1;
+                    if (mbar_test_wait(&kfull[st], (js / kKS) & 1) &&
+                        mbar_test_wait(&sfree[buf], ((js >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+                        const uint32_t stg = smem_u32(sm + L::kKStage + st * L::kKBytes);
 #pragma unroll
-                for (int part = 0; part < 2; ++part)
+                        for (int kk = 0; kk < 4; ++kk)  // indexer scores: same sequence as the indexer
+                            mma_bf16(tSidx + buf * kNk, sdesc_kmajor_sw128(aiq + kk * 32),
+                                     sdesc_kmajor_sw128(stg + kk * 32), id_s, kk ? 1u : 0u);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = sdesc_kmajor_sw128(ph + part * 16384 + kk * 32);
-                        const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
-                        mma_bf16(tO, ad, bd, id_pv, (jj | part | kk) ? 1u : 0u);
+                        for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk)
+                                mma_bf16(tS + buf * kNk, sdesc_kmajor_sw128(aq + kb * 16384 + kk * 32),
+                                         sdesc_kmajor_sw128(stg + 8192 + kb * 8192 + kk * 32), id_s,
+                                         (kb | kk) ? 1u : 0u);
+                        mma_commit(&sfull[buf]);
+                        mma_commit(&kempty[st]);
+                        ++js;
+                        progress = true;
                     }
-                mma_commit(&pfree[pb]);
-                mma_commit(&vempty[vs]);
-            };
-            for (int j = 0; j < nkt; ++j) {
-                const int st = j % kKS, buf = j & 1;
-                mbar_wait(&kfull[st], (j / kKS) & 1, wd, 8u);
-                mbar_wait(&sfree[buf], ((j >> 1) & 1) ^ 1, wd, 16u);
-                tc_fence_after();
-                const uint32_t stg = smem_u32(sm + L::kKStage + st * L::kKBytes);
+                }
+                if (jp < js) {  // PV of tile jp into the O of its group (jp & 1)
+                    const int g = jp & 1, vs = jp % kVS;
+                    if (mbar_test_wait(&vfull[vs], (jp / kVS) & 1) &&
+                        mbar_test_wait(&pfull[g], (jp >> 1) & 1)) {
+                        tc_fence_after();
+                        const uint32_t ph = smem_u32(sm + L::kP + g * 32768);
+                        const uint32_t vq = smem_u32(sm + L::kVStage + vs * L::kVBytes);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)  // indexer scores: same sequence as the indexer
-                    mma_bf16(tSidx + buf * kNk, sdesc_kmajor_sw128(aiq + kk * 32),
-                             sdesc_kmajor_sw128(stg + kk * 32), id_s, kk ? 1u : 0u);
+                        for (int part = 0; part < 2; ++part)
 #pragma unroll
-                for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_bf16(tS + buf * kNk, sdesc_kmajor_sw128(aq + kb * 16384 + kk * 32),
-                                 sdesc_kmajor_sw128(stg + 8192 + kb * 8192 + kk * 32), id_s,
-                                 (kb | kk) ? 1u : 0u);
-                mma_commit(&sfull[buf]);
-                mma_commit(&kempty[st]);
-                if (j > 0) issue_pv(j - 1);
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const uint64_t ad = sdesc_kmajor_sw128(ph + part * 16384 + kk * 32);
+                                const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
+                                mma_bf16(tO + g * 128, ad, bd, id_pv, ((jp >> 1) | part | kk) ? 1u : 0u);
+                            }
+                        mma_commit(&pfree[g]);
+                        mma_commit(&vempty[vs]);
+                        ++jp;
+                        progress = true;
+                    }
+                }
+                if (progress) {
+                    idle = 0;
+                } else if (++idle > kSpinLimit) {  // nothing moved for a long time: give up
+                    atomicOr(wd, 8u);
+                    break;
+                } else if ((idle & 1023u) == 1023u && *(volatile unsigned int *)wd) {
+                    break;
+                }
             }
-            issue_pv(nkt - 1);
         }
         __syncwarp();
     } else {
-        // kParts threads per query row: warps w, w+4, w+8, ... share a TMEM lane
-        // quarter; `part` picks kCP of the tile's 64 key columns (and kOP of O's).
-        const int quad = warp & 3, r = quad * 32 + lane, part = (warp - 3) >> 2;
+        // Two groups of kParts threads per query row: group g takes key tiles j = g, g+2, ...
+        // into its own S/P buffers and its own O (an online softmax each, merged at the end).
+        // Warps 3 + 8 g + 4 p + i: TMEM lane quarter (warp & 3), part p of the tile's columns.
+        const int sw = warp - 3, g = sw >> 3, part = (sw >> 2) & 1;
+        const int quad = warp & 3, r = quad * 32 + lane;
         const int t = q0 + r;
         const bool valid_row = t < T;
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
-        float *xmax = (float *)(sm + L::kBar + 256);  // [2 tiles][kParts][128 rows]
+        float *xmax = (float *)(sm + L::kXmax);
+        float *mrow = (float *)(sm + L::kMrow);
+        float *lrow_s = (float *)(sm + L::kLrow);
+        const uint32_t gbar = 1 + g;  // named barrier of the group (kParts * 128 threads)
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
         if (valid_row) th = thr[((size_t)b * HI + hi) * T + t];
         // The threshold as a float: key(s) & mask > prefix, or == prefix and j <= cut, is
@@ -212,57 +244,82 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         const float a_thr = mask == 0u ? -INFINITY
                                        : __uint_as_float((prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix);
         float m_used = -INFINITY, l = 0.f;
-        for (int j = 0; j < nkt; ++j) {
-            const int buf = j & 1;
-            mbar_wait(&sfull[buf], (j >> 1) & 1, wd, 32u);
+        // Fixed reference maximum: with |s| <= max|q| max|k| (Cauchy-Schwarz, per head),
+        // bound = max|q| max|k| * scale * log2(e) is >= every x, and when it is <= 60,
+        // p = 2^(x - bound) stays in [2^-120, ~1]: no running maximum, no exchange
+        // between the row's threads, no rescaling of O.
+        bool use_bound = false;
+        if (qkmax) {
+            const float qm2 = __uint_as_float(qkmax[2 * bh]), km2 = __uint_as_float(qkmax[2 * bh + 1]);
+            const float bound = sqrtf(qm2) * sqrtf(km2) * scale_log2;
+            if (bound <= 60.f) {
+                use_bound = true;
+                m_used = bound;
+            }
+        }
+        int n_mine = 0;  // tiles of this group
+        for (int j = g; j < nkt; j += 2, ++n_mine) {
+            const int slot = (j >> 1) & 1;
+            mbar_wait(&sfull[g], (j >> 1) & 1, wd, 32u);
             tc_fence_after();
-            float x[kCP], si[kCP], sv[kCP];
+            float x[kCP];
             float mt = -INFINITY;
-            tmem_ld16(tSidx + lrow + buf * kNk + part * kCP, si);
-            tmem_ld16(tS + lrow + buf * kNk + part * kCP, sv);
-            const int jb = j * kNk + part * kCP;
-            const bool full = jb + kCP - 1 <= q0;  // every row of the tile sees all columns
+            const int jb0 = j * kNk + part * kCP;
+            const bool full = jb0 + kCP - 1 <= q0;  // every row of the tile sees all columns
 #pragma unroll
-            for (int i = 0; i < kCP; ++i) {
-                const int jj = jb + i;
-                const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
-                const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
-                x[i] = xv;
-                mt = fmaxf(mt, xv);
+            for (int hf = 0; hf < kCP / 16; ++hf) {
+                float si[16], sv[16];
+                tmem_ld16(tSidx + lrow + g * kNk + part * kCP + hf * 16, si);
+                tmem_ld16(tS + lrow + g * kNk + part * kCP + hf * 16, sv);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int jj = jb0 + hf * 16 + i;
+                    const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
+                    const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
+                    x[hf * 16 + i] = xv;
+                    mt = fmaxf(mt, xv);
+                }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sfree[buf]);
-            xmax[(buf * kParts + part) * 128 + r] = mt;
-            asm volatile("bar.sync 1, %0;" ::"r"(kParts * 128) : "memory");
+            if (lane == 0) mbar_arrive(&sfree[g]);
+            if (!use_bound) {
+                xmax[((g * 2 + slot) * kParts + part) * 128 + r] = mt;
+                asm volatile("bar.sync %0, %1;" ::"r"(gbar), "r"(kParts * 128) : "memory");
 #pragma unroll
-            for (int p2 = 0; p2 < kParts; ++p2) mt = fmaxf(mt, xmax[(buf * kParts + p2) * 128 + r]);
-            // lazy maximum: rescale only when this tile's maximum is > m_used + 8
-            const bool grow = mt > m_used + 8.f || (m_used == -INFINITY && mt != -INFINITY);
-            if (__any_sync(0xffffffffu, grow)) {
-                const float m_new = grow ? mt : m_used;
-                const float f = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
-                l *= (grow ? f : 1.f);
-                if (j > 0) {  // O holds tiles < j: wait for the last PV into it
-                    mbar_wait(&pfree[(j - 1) & 1], ((j - 1) >> 1) & 1, wd, 64u);
-                    tc_fence_after();
-                    float o[32];
-                    tmem_ld32(tO + lrow + part * kOP, o);
-                    const float g = grow ? f : 1.f;
+                for (int p2 = 0; p2 < kParts; ++p2)
+                    mt = fmaxf(mt, xmax[((g * 2 + slot) * kParts + p2) * 128 + r]);
+                // lazy maximum: rescale only when this tile's maximum is > m_used + 8
+                const bool grow = mt > m_used + 8.f || (m_used == -INFINITY && mt != -INFINITY);
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float m_new = grow ? mt : m_used;
+                    const float f = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
+                    l *= (grow ? f : 1.f);
+                    if (n_mine > 0) {  // this group's O holds its earlier tiles
+                        mbar_wait(&pfree[g], ((j >> 1) - 1) & 1, wd, 64u);
+                        tc_fence_after();
+                        const float gsc = grow ? f : 1.f;
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            float o[16];
+                            const uint32_t oa = tO + g * 128 + lrow + part * 64 + c * 16;
+                            tmem_ld16(oa, o);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= g;
-                    tmem_st32(tO + lrow + part * kOP, o);
-                    tc_fence_before();
+                            for (int i = 0; i < 16; ++i) o[i] *= gsc;
+                            tmem_st16(oa, o);
+                        }
+                        tc_fence_before();
+                    }
+                    if (grow) m_used = m_new;
                 }
-                if (grow) m_used = m_new;
             }
             // P = exp2(x - m_used) as bf16 hi + lo, K-major rows of 64 keys
             const float mref = (m_used == -INFINITY) ? 0.f : m_used;  // x = -inf -> p = 0
-            if (j >= 2) mbar_wait(&pfree[buf], ((j >> 1) & 1) ^ 1, wd, 128u);
-            unsigned char *ph = sm + L::kP + buf * 32768;
+            if (n_mine > 0) mbar_wait(&pfree[g], ((j >> 1) & 1) ^ 1, wd, 128u);
+            unsigned char *ph = sm + L::kP + g * 32768;
 #pragma unroll
             for (int c8 = 0; c8 < kCP / 8; ++c8) {
-                uint32_t hi[4], lo[4];
+                uint32_t hw[4], lw[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float p0 = exp2f(x[c8 * 8 + 2 * u] - mref);
@@ -271,39 +328,73 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
                     const float2 hf = __bfloat1622float2(h2);
                     const __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
-                    hi[u] = *reinterpret_cast<const uint32_t *>(&h2);
-                    lo[u] = *reinterpret_cast<const uint32_t *>(&l2);
+                    hw[u] = *reinterpret_cast<const uint32_t *>(&h2);
+                    lw[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
                 const int chunk = part * (kCP / 8) + c8;
                 const uint32_t off = (uint32_t)r * 128 + (uint32_t)((chunk ^ (r & 7)) << 4);
-                *(uint4 *)(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *(uint4 *)(ph + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *(uint4 *)(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *(uint4 *)(ph + 16384 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
             }
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&pfull[buf]);
+            if (lane == 0) mbar_arrive(&pfull[g]);
         }
-        // epilogue: out = mix * O / l + (1 - mix) * o_delta, l summed over the parts
-        xmax[part * 128 + r] = l;
-        asm volatile("bar.sync 1, %0;" ::"r"(kParts * 128) : "memory");
-        l = 0.f;
+        // merge the groups: out = mix * (sum_g 2^(m_g - m) O_g) / (sum_g 2^(m_g - m) l_g)
+        //                        + (1 - mix) * o_delta
+        lrow_s[(g * kParts + part) * 128 + r] = l;
+        if (part == 0) mrow[g * 128 + r] = m_used;
+        // (named barriers: 1 and 2 are the groups' per-tile exchanges, 3 this merge)
+        asm volatile("bar.sync 3, %0;" ::"r"(kGroups * kParts * 128) : "memory");
+        float mg[kGroups], lg[kGroups];
+        float m_all = -INFINITY;
 #pragma unroll
-        for (int p2 = 0; p2 < kParts; ++p2) l += xmax[p2 * 128 + r];
-        mbar_wait(&pfree[(nkt - 1) & 1], ((nkt - 1) >> 1) & 1, wd, 256u);
+        for (int g2 = 0; g2 < kGroups; ++g2) {
+            mg[g2] = mrow[g2 * 128 + r];
+            lg[g2] = 0.f;
+#pragma unroll
+            for (int p2 = 0; p2 < kParts; ++p2) lg[g2] += lrow_s[(g2 * kParts + p2) * 128 + r];
+            m_all = fmaxf(m_all, mg[g2]);
+        }
+        float wgt[kGroups], lsum = 0.f;
+#pragma unroll
+        for (int g2 = 0; g2 < kGroups; ++g2) {
+            // a group without tiles (nkt == 1) or without selected keys has l = 0
+            wgt[g2] = (lg[g2] > 0.f) ? exp2f(mg[g2] - m_all) : 0.f;
+            lsum += wgt[g2] * lg[g2];
+        }
+        const float inv = (lsum > 0.f) ? 1.f / lsum : 0.f;
+        // wait for the last PV of each group
+#pragma unroll
+        for (int g2 = 0; g2 < kGroups; ++g2) {
+            const int last = (nkt - 1 - g2) >= 0 ? ((nkt - 1 - g2) / 2) * 2 + g2 : -1;
+            if (last >= 0) mbar_wait(&pfree[g2], (last >> 1) & 1, wd, 256u);
+        }
         tc_fence_after();
-        const float inv = (l > 0.f) ? 1.f / l : 0.f;
         const size_t rowq = ((size_t)b * T + t) * H + h;
-        {
-            float o[32];
-            const int c0 = part * kOP;
-            tmem_ld32(tO + lrow + c0, o);
-            if (valid_row) {
-                Tout *dst = out + rowq * D + c0;
+        const int c0 = (g * kParts + part) * 32;  // this thread's 32 output columns
+#pragma unroll 1
+        for (int hc = 0; hc < 2; ++hc) {
+            const int cc = c0 + hc * 16;
+            float o[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
+            for (int i = 0; i < 16; ++i) o[i] = 0.f;
+#pragma unroll
+            for (int g2 = 0; g2 < kGroups; ++g2) {
+                if (g2 < nkt) {  // the group's O was written
+                    float og[16];
+                    tmem_ld16(tO + g2 * 128 + lrow + cc, og);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = fmaf(wgt[g2], og[i], o[i]);
+                }
+            }
+            if (valid_row) {
+                Tout *dst = out + rowq * D + cc;
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
                     float r0 = o[i] * inv, r1 = o[i + 1] * inv;
                     if (od) {
-                        const size_t e = rowq * D + c0 + i;
+                        const size_t e = rowq * D + cc + i;
                         const float m0 = mix ? to_f32(mix_pc ? mix[e] : mix[rowq]) : 1.f;
                         const float m1 = mix ? to_f32(mix_pc ? mix[e + 1] : mix[rowq]) : 1.f;
                         r0 = m0 * r0 + (1.f - m0) * od[e];
@@ -324,6 +415,48 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// max_t |q_t|^2 and max_t |k_t|^2 of each (b, h) (D = 128, bf16) into out[2 (b H + h) + {0, 1}]
+// as float bits (non-negative floats order as unsigned integers).  One block per
+// (kNormRows tokens, b h), a warp per token row.
+constexpr int kNormRows = 256;
+__global__ void __launch_bounds__(256) qk_norm_max_kernel(const __nv_bfloat16 *__restrict__ q,
+                                                          const __nv_bfloat16 *__restrict__ k,
+                                                          uint32_t *__restrict__ out, int T, int H) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, bh = blockIdx.y;
+    const int b = bh / H, h = bh % H;
+    float mq = 0.f, mk = 0.f;
+    for (int t = blockIdx.x * kNormRows + warp; t < min(T, (blockIdx.x + 1) * kNormRows); t += 8) {
+        const size_t off = (((size_t)b * T + t) * H + h) * 128 + lane * 4;
+        const uint2 uq = *reinterpret_cast<const uint2 *>(q + off);
+        const uint2 uk = *reinterpret_cast<const uint2 *>(k + off);
+        const float2 q0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&uq.x));
+        const float2 q1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&uq.y));
+        const float2 k0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&uk.x));
+        const float2 k1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&uk.y));
+        float sq = q0.x * q0.x + q0.y * q0.y + q1.x * q1.x + q1.y * q1.y;
+        float sk = k0.x * k0.x + k0.y * k0.y + k1.x * k1.x + k1.y * k1.y;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            sk += __shfl_xor_sync(0xffffffffu, sk, o);
+        }
+        mq = fmaxf(mq, sq);
+        mk = fmaxf(mk, sk);
+    }
+    __shared__ float red[2][8];
+    if (lane == 0) {
+        red[0][warp] = mq;
+        red[1][warp] = mk;
+    }
+    __syncthreads();
+    if (threadIdx.x < 2) {
+        float m = 0.f;
+        for (int w = 0; w < 8; ++w) m = fmaxf(m, red[threadIdx.x][w]);
+        // a little headroom over the fp32 sums of squares
+        atomicMax(&out[2 * bh + threadIdx.x], __float_as_uint(m * 1.0001f));
+    }
+}
+
 }  // namespace
 
 bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype) {
@@ -335,7 +468,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  int HI, cudaStream_t st) {
+                                  int HI, uint32_t *qkmax, cudaStream_t st) {
     CUtensorMap mq, mk, mv, miq, mik;
     if (!make_tmap_rows_bf16(&mq, q, B, T, H, 128, 128) ||
         !make_tmap_rows_bf16(&mk, k, B, T, H, 128, kNk) ||
@@ -347,6 +480,15 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
     const int ntiles = q_tiles ? n_tiles : nqt;
     if (ntiles <= 0) return cudaSuccess;
     const float sl = scale * 1.4426950408889634f;
+    if (B * H > 65535) qkmax = nullptr;  // grid limit of the norm pass: running maximum instead
+    if (qkmax) {
+        cudaError_t e = cudaMemsetAsync(qkmax, 0, (size_t)B * H * 2 * sizeof(uint32_t), st);
+        if (e != cudaSuccess) return e;
+        qk_norm_max_kernel<<<dim3(ceil_div(T, kNormRows), B * H), 256, 0, st>>>(
+            (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, qkmax, T, H);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     if (out_f32) {
         auto kern = sparse_attn_tc_kernel<__nv_bfloat16, float>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -354,7 +496,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
             mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
-            (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI);
+            (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
     } else {
         auto kern = sparse_attn_tc_kernel<__nv_bfloat16, __nv_bfloat16>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -362,7 +504,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
             mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
-            (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI);
+            (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
     }
     return cudaGetLastError();
 }

@@ -300,10 +300,11 @@ def sparse_attn_thresholds(q, k, v, iq, ik, thresholds, o_delta=None, mix=None, 
     sc = float(scale) if scale is not None else 1.0 / math.sqrt(D)
     qt = None if q_tiles is None else q_tiles.to(device=q.device, dtype=torch.int32).contiguous()
     nt = 0 if qt is None else qt.numel()
+    norms = torch.empty(2 * B * H, device=q.device, dtype=torch.int32)  # max |q|^2, |k|^2 per head
     st = _lib.load().sgsa_sparse_attn_thresholds(
         _ptr(q), _ptr(k), _ptr(v), _ptr(iq), _ptr(ik), _ptr(thresholds), _ptr(qt), nt, _ptr(od),
         _ptr(mx), _ptr(out), B, T, H, D, DI, iq.shape[2], sc, per_channel,
-        int(out.dtype == torch.float32), _stream(q))
+        int(out.dtype == torch.float32), _ptr(norms), _stream(q))
     _lib.check(st, "sgsa_sparse_attn_thresholds")
     return out
 

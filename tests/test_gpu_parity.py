@@ -304,6 +304,23 @@ def test_layer_fused_attention_with_exact_score_ties(monkeypatch):
     assert oracle.rel_l2(fused.float().cpu().numpy(), gather.float().cpu().numpy()) < 2e-3
 
 
+@pytest.mark.parametrize("norm", [1.0, 30.0])
+def test_fused_attention_bound_and_running_max(norm):
+    """Unit-norm q, k take the fixed-bound softmax; norms of 30 (scores up to ~114 in
+    log2 units) take the per-group running maximum.  Both against the oracle on the
+    device's own index sets."""
+    cfg = CONFIGS["b200_bf16"].scaled(name="bound", B=1, T=1000, H=2, top_k=128)
+    x = make_inputs(cfg, seed=12)
+    x["q"] = (x["q"].float() * norm).bfloat16()
+    x["k"] = (x["k"].float() * norm).bfloat16()
+    d = dev(x)
+    thr = ops.indexer_thresholds(d["iq"], d["ik"], cfg.top_k)
+    got = ops.sparse_attn_thresholds(d["q"], d["k"], d["v"], d["iq"], d["ik"], thr, out_f32=True)
+    idx = ops.indexer_topk(d["iq"], d["ik"], cfg.top_k).cpu().numpy()
+    want = oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx)
+    assert oracle.rel_l2(got.cpu().numpy(), want) < 1e-4
+
+
 def test_layer_from_host_matches_device_call():
     cfg = CONFIGS["b200_bf16"].scaled(name="host", B=2, T=1024, H=2, top_k=128)
     x = make_inputs(cfg, seed=6)
