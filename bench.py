@@ -589,7 +589,7 @@ def run_ours(args, ws, rank, local):
                        "parallelism": f"bh-shard x{ws}", "l2": "inputs 470 MB > L2, no flush"},
             "e2e": {"value": ws * cfg.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": 6 * args.steps,  # prep, scan, q/k norms, indexer, attention, gate
             "roofline": roof,
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": sample, "seconds": secs},

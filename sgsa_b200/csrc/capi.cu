@@ -227,6 +227,7 @@ size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top
     n += align256((size_t)B * H * T * top_k * sizeof(int32_t));  // indices
     n += align256((size_t)B * H * T * 16);                       // per-row selection thresholds
     n += align256((size_t)B * H * 2 * sizeof(uint32_t));         // max |q|^2, |k|^2 per head
+    n += align256((size_t)B * T * H * D * sizeof(float));       // o_s (attention before the gate)
     return n;
 }
 
@@ -251,6 +252,7 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     int32_t *ix = (int32_t *)(w + cws + align256((size_t)B * T * H * D * sizeof(float)));
     uint32_t *thr = (uint32_t *)((char *)ix + align256((size_t)B * H * T * top_k * sizeof(int32_t)));
     uint32_t *qkmax = (uint32_t *)((char *)thr + align256((size_t)B * H * T * 16));
+    float *os_ws = (float *)((char *)qkmax + align256((size_t)B * H * 2 * sizeof(uint32_t)));
     const bool fused = sgsa::indexer_tc_eligible(DI, dtype) &&
                        sgsa::sparse_attn_tc_eligible(T, D, DI, dtype) && fused_attn_enabled();
     if (indices) ix = indices;
@@ -259,8 +261,9 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     const float scale = 1.0f / sqrtf((float)D);
     cudaError_t e;
     if (fused) {
-        // The delta stage runs on a side stream beside the indexer (neither reads the
-        // other's output); the attention, which gates with the delta output, joins.
+        // The delta stage runs on a side stream beside the indexer and the attention
+        // (neither reads its output); the attention writes o_s in fp32 and the gate,
+        // which needs the delta output, joins the two streams.
         cudaStream_t side = side_stream();
         cudaEvent_t fork = nullptr, join = nullptr;
         if (!side || cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
@@ -282,13 +285,17 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
             e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, idx_heads, DI, top_k,
                                               nullptr, 0, st);
+        if (e == cudaSuccess)
+            e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, nullptr, nullptr, os_ws, B, T, H,
+                                            scale, mix_per_channel, nullptr, 0, true, idx_heads,
+                                            qkmax, st);
         if (side != st) {
             cudaStreamWaitEvent(st, join, 0);
             cudaEventDestroy(join);
         }
         if (e != cudaSuccess) return fail_cuda(e);
-        e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
-                                        mix_per_channel, nullptr, 0, false, idx_heads, qkmax, st);
+        e = sgsa::launch_gate_mix(os_ws, od, mix, out, (long long)B * T * H, D, mix_per_channel,
+                                  dtype, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
     e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr, initial_state,

@@ -277,7 +277,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
                     const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
                     x[hf * 16 + i] = xv;
-                    mt = fmaxf(mt, xv);
+                    if (!use_bound) mt = fmaxf(mt, xv);
                 }
             }
             tc_fence_before();
