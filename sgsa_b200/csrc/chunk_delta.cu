@@ -571,7 +571,7 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
     uint64_t *bars = (uint64_t *)(sm + ptc::kBar);
     uint64_t *ldbar = bars, *mma1 = bars + 1, *mma2 = bars + 2;
     __shared__ uint32_t s_tmem;
-    __shared__ float sG[128], sLam[128];
+    __shared__ float sG[128], sLam[128], sEq[128], sEk[128];
     unsigned int *wd = &g_scan_watchdog;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -635,13 +635,18 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
     __syncthreads();
     mbar_wait(mma1, 0, wd, 0x200u);
     tc_fence_after();
-    float *Ablk = (float *)(sm + ptc::kA);  // [2][64 i][64 j]
+    // A blocks [2][64 i][64 j], 16-byte column groups XOR-swizzled by (i & 7): the epilogue
+    // stores 32 rows at once (conflict-free), the solve reads rows as broadcasts
+    float *Ablk = (float *)(sm + ptc::kA);
+    auto a_off = [](int i, int j) { return i * 64 + ((((j >> 2) ^ (i & 7))) << 2) + (j & 3); };
     {   // A (warps 0-3) and Aqk (warps 4-7), one row per thread, its own 64-column block
         const int quad = warp & 3, i = quad * 32 + lane, cb = i >> 6, tau = i & 63;
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (warp < 4 ? 0 : 128) + cb * 64;
         const bool vi = valid(i);
+        const float lam_i = sLam[i];
         float *aqk = a.Aqk + (((size_t)bh * NC + c0 + cb) * kC + tau) * kC;
         const bool chunk_ok = c0 + cb < NC;
+        float *astg = (float *)(sm + ptc::kX) + (warp & 3) * (32 * 68);  // T' area, not yet used
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
             float d[32];
@@ -654,13 +659,28 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
                 for (int u = 0; u < 4; ++u) {
                     const int m = hf * 32 + jj + u, j = cb * 64 + m;
                     const bool vj = valid(j);
+                    // branch-free: the exponent is clamped at 0 (its value only matters where
+                    // m <= tau, where G_i <= G_j) and the mask selects
+                    const float e = __expf(fminf(sG[i] - sG[j], 0.f)) * d[jj + u];
                     if (warp < 4)
-                        r[u] = (vi && vj && m < tau) ? sLam[i] * __expf(sG[i] - sG[j]) * d[jj + u] : 0.f;
+                        r[u] = (vi && vj && m < tau) ? lam_i * e : 0.f;
                     else
-                        r[u] = (vi && vj && m <= tau) ? __expf(sG[i] - sG[j]) * d[jj + u] : 0.f;
+                        r[u] = (vi && vj && m <= tau) ? e : 0.f;
                 }
-                if (warp < 4) *(float4 *)(Ablk + (cb * 64 + tau) * 64 + hf * 32 + jj) = r4;
-                else if (chunk_ok) *(float4 *)(aqk + hf * 32 + jj) = r4;
+                if (warp < 4) *(float4 *)(Ablk + cb * 4096 + a_off(tau, hf * 32 + jj)) = r4;
+                else *(float4 *)(astg + lane * 68 + hf * 32 + jj) = r4;
+            }
+        }
+        if (warp >= 4) {  // the warp's 32 Aqk rows are contiguous: whole 256-byte rows per store
+            __syncwarp();
+            if (chunk_ok) {
+                float *dst = aqk - (size_t)lane * kC;  // row of lane 0
+                const int cq = lane & 15;
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const int r = (lane >> 4) + 2 * k;
+                    *(float4 *)(dst + (size_t)r * kC + cq * 4) = *(const float4 *)(astg + r * 68 + cq * 4);
+                }
             }
         }
     }
@@ -673,57 +693,92 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
         const float *Ab = Ablk + blk * 4096;
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-            float s = (i == c) ? 1.f : 0.f;
+            // four partial sums: a chain of i/4 dependent FMAs instead of i
+            float s0 = (i == c) ? 1.f : 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
             for (int j = 0; j < i; j += 4) {
-                const float4 a4 = *(const float4 *)(Ab + i * 64 + j);  // broadcast
-                s -= a4.x * tcol[j];
-                if (j + 1 < i) s -= a4.y * tcol[j + 1];
-                if (j + 2 < i) s -= a4.z * tcol[j + 2];
-                if (j + 3 < i) s -= a4.w * tcol[j + 3];
+                const float4 a4 = *(const float4 *)(Ab + a_off(i, j));  // broadcast
+                s0 -= a4.x * tcol[j];
+                if (j + 1 < i) s1 -= a4.y * tcol[j + 1];
+                if (j + 2 < i) s2 -= a4.z * tcol[j + 2];
+                if (j + 3 < i) s3 -= a4.w * tcol[j + 3];
             }
-            tcol[i] = s;
+            tcol[i] = (s0 + s1) + (s2 + s3);
         }
     } else {
         // operands of the scan: Qt = e^{G} q (row-major), Kt^T = e^{G_last - G} k ([dk][tok]),
-        // read from the swizzled Q and K tiles; G
+        // read from the swizzled Q and K tiles 16 bytes at a time; G
         const int u = tid - 128;
         const unsigned char *Kt = sm + ptc::kK, *Qt = sm + ptc::kQ;
+        {  // the per-token factors, once
+            const bool ok = valid(u);
+            const float glast = sG[(u >> 6) * 64 + 63];
+            sEq[u] = ok ? __expf(sG[u]) : 0.f;
+            sEk[u] = ok ? __expf(glast - sG[u]) : 0.f;
+        }
+        asm volatile("bar.sync 2, 128;" ::: "memory");
         for (int cb = 0; cb < 2; ++cb) {
             if (c0 + cb >= NC) break;
             const size_t cix = (size_t)bh * NC + c0 + cb;
-            const float glast = sG[cb * 64 + 63];
-            for (int e = u; e < kC * D; e += 128) {  // Qt: d fastest (coalesced)
-                const int m = e / D, d = e % D, j = cb * 64 + m;
-                const float qv = __bfloat162float(*(const __nv_bfloat16 *)(Qt + sw128_bf16(j, d)));
-                a.Qt[(cix * kC + m) * D + d] = valid(j) ? __expf(sG[j]) * qv : 0.f;
+            for (int e = u; e < kC * D / 8; e += 128) {  // Qt: 8 consecutive d of one token
+                const int m = e >> 4, d0 = (e & 15) * 8, j = cb * 64 + m;
+                const uint4 raw = *(const uint4 *)(Qt + sw128_bf16(j, d0));
+                const __nv_bfloat162 *h2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+                const float f = sEq[j];
+                float4 lo, hi;
+                float2 x0 = __bfloat1622float2(h2[0]), x1 = __bfloat1622float2(h2[1]),
+                       x2 = __bfloat1622float2(h2[2]), x3 = __bfloat1622float2(h2[3]);
+                lo = make_float4(f * x0.x, f * x0.y, f * x1.x, f * x1.y);
+                hi = make_float4(f * x2.x, f * x2.y, f * x3.x, f * x3.y);
+                float *dst = a.Qt + (cix * kC + m) * D + d0;
+                *(float4 *)dst = lo;
+                *(float4 *)(dst + 4) = hi;
             }
-            for (int e = u; e < kC * D; e += 128) {  // Kt^T: m fastest (coalesced)
-                const int d = e / kC, m = e % kC, j = cb * 64 + m;
-                const float kv = __bfloat162float(*(const __nv_bfloat16 *)(Kt + sw128_bf16(j, d)));
-                a.KtT[(cix * D + d) * kC + m] = valid(j) ? __expf(glast - sG[j]) * kv : 0.f;
+            for (int e = u; e < kC * D / 8; e += 128) {  // Kt^T: 8 consecutive tokens of one d
+                // lanes take consecutive d of the same 8 tokens: conflict-free tile reads
+                const int d = e & (D - 1), m0 = (e / D) * 8;
+                float v[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int j = cb * 64 + m0 + i;
+                    v[i] = sEk[j] * __bfloat162float(*(const __nv_bfloat16 *)(Kt + sw128_bf16(j, d)));
+                }
+                float *dst = a.KtT + (cix * D + d) * kC + m0;
+                *(float4 *)dst = make_float4(v[0], v[1], v[2], v[3]);
+                *(float4 *)(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
             }
             if (u < 64) a.G[cix * kC + u] = sG[cb * 64 + u];
         }
     }
     __syncthreads();  // the Q tile and the A blocks are dead from here
     if (tid < 128) {
-        // T' = T diag(lam e^G) into kX (hi | lo), T'' = T diag(lam) into kQ.. (hi | lo);
-        // rows of the other block are zero
+        // T' = T diag(lam e^G) into kX (hi | lo), T'' = T diag(lam) into kQ.. (hi | lo):
+        // this thread's column over its block's 64 rows
         const int blk = tid >> 6, c = tid & 63, col = blk * 64 + c;
         const float s1 = sLam[col] * __expf(sG[col]), s2 = sLam[col];
         unsigned char *X = sm + ptc::kX, *Y = sm + ptc::kQ;
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-            const int li = i - blk * 64;
-            const float tv = (li >= 0 && li < 64) ? tcol[li & 63] : 0.f;
-            const float v1 = tv * s1, v2 = tv * s2;
+        for (int li = 0; li < 64; ++li) {
+            const int i = blk * 64 + li;
+            const float v1 = tcol[li] * s1, v2 = tcol[li] * s2;
             const __nv_bfloat16 h1 = __float2bfloat16_rn(v1), h2 = __float2bfloat16_rn(v2);
             const uint32_t off = sw128_bf16(i, col);
             *(__nv_bfloat16 *)(X + off) = h1;
             *(__nv_bfloat16 *)(X + 32768 + off) = __float2bfloat16_rn(v1 - __bfloat162float(h1));
             *(__nv_bfloat16 *)(Y + off) = h2;
             *(__nv_bfloat16 *)(Y + 32768 + off) = __float2bfloat16_rn(v2 - __bfloat162float(h2));
+        }
+    } else {
+        // the off-diagonal blocks of T' and T'' are zero: 16-byte chunks
+        unsigned char *X = sm + ptc::kX, *Y = sm + ptc::kQ;
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        for (int e = tid - 128; e < 128 * 8; e += 128) {
+            const int i = e >> 3, col0 = ((1 - (i >> 6)) * 8 + (e & 7)) * 8;
+            const uint32_t off = sw128_bf16(i, col0);
+            *(uint4 *)(X + off) = z;
+            *(uint4 *)(X + 32768 + off) = z;
+            *(uint4 *)(Y + off) = z;
+            *(uint4 *)(Y + 32768 + off) = z;
         }
     }
     fence_proxy_async();
@@ -751,18 +806,31 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
     mbar_wait(mma2, 0, wd, 0x400u);
     tc_fence_after();
     {
-        const int quad = warp & 3, i = quad * 32 + lane, cb = i >> 6, tau = i & 63;
+        // W (warps 0-3) / Uh (warps 4-7): a warp's 32 rows are 32 consecutive rows of the
+        // output; 32 x 32 blocks go through shared memory (the dead T' area) so that every
+        // store instruction writes whole 128-byte row segments
+        const int quad = warp & 3, i0 = quad * 32, cb = i0 >> 6, tau0 = i0 & 63;
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (warp < 4 ? 0 : 128);
-        float *dst = (warp < 4 ? a.W : a.U) + (((size_t)bh * NC + c0 + cb) * kC + tau) * D;
+        float *dst = (warp < 4 ? a.W : a.U) + (((size_t)bh * NC + c0 + cb) * kC + tau0) * D;
         const bool ok = c0 + cb < NC;
-#pragma unroll
+        float *stg = (float *)(sm + ptc::kX) + warp * (32 * 36);
+#pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
             float d[32];
             tmem_ld32(taddr + cc * 32, d);
-            if (ok)
 #pragma unroll
-                for (int jj = 0; jj < 32; jj += 4)
-                    *(float4 *)(dst + cc * 32 + jj) = make_float4(d[jj], d[jj + 1], d[jj + 2], d[jj + 3]);
+            for (int q = 0; q < 8; ++q)
+                *(float4 *)(stg + lane * 36 + q * 4) = make_float4(d[4 * q], d[4 * q + 1], d[4 * q + 2], d[4 * q + 3]);
+            __syncwarp();
+            if (ok) {
+                const int cq = lane & 7;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int r = (lane >> 3) + 4 * k;
+                    *(float4 *)(dst + (size_t)r * D + cc * 32 + cq * 4) = *(const float4 *)(stg + r * 36 + cq * 4);
+                }
+            }
+            __syncwarp();
         }
     }
     tc_fence_before();
