@@ -489,36 +489,49 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
             const float gl = __expf(a.G[cix * kC + kC - 1]);
             mbar_wait(d23done, ph, wd, 32u);
             tc_fence_after();
+            // o^T leaves TMEM first (the next chunk's MMAs overwrite it once S is released),
+            // then S (it gates those MMAs), then the o stores; TMEM loads are issued in pairs
+            // and the state is read ahead of the FMAs
+            uint32_t ro0[32], ro1[32];
+            tmem_ld32_issue(trow + 64, ro0);
+            tmem_ld32_issue(trow + 96, ro1);
+            tmem_ld_wait(ro0);
+            tmem_ld_wait(ro1);
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float d[32];
-                tmem_ld32(trow + 64 + half * 32, d);
+            for (int q = 0; q < 4; q += 2) {
+                uint32_t r0[32], r1[32];
+                tmem_ld32_issue(trow + 128 + q * 32, r0);
+                tmem_ld32_issue(trow + 128 + (q + 1) * 32, r1);
+                float4 x[16];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = half * 32 + j;
-                    if (t < L && !a.transition)
-                        o[(((size_t)b * a.T + t0 + t) * a.H + h) * tc::kD + v] = from_f32<Tout>(d[j]);
-                }
-            }
+                for (int j = 0; j < 16; ++j)
+                    x[j] = *(const float4 *)((unsigned char *)ST + sw128_f32(128, v, q * 32 + 4 * j));
+                tmem_ld_wait(r0);
+                tmem_ld_wait(r1);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float d[32];
-                tmem_ld32(trow + 128 + q * 32, d);
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    float4 *p = (float4 *)((unsigned char *)ST + sw128_f32(128, v, q * 32 + j));
-                    float4 x = *p;
-                    x.x = fmaf(gl, x.x, d[j]);
-                    x.y = fmaf(gl, x.y, d[j + 1]);
-                    x.z = fmaf(gl, x.z, d[j + 2]);
-                    x.w = fmaf(gl, x.w, d[j + 3]);
-                    *p = x;
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t *r = j < 8 ? r0 : r1;
+                    const int jj = (j & 7) * 4;
+                    x[j].x = fmaf(gl, x[j].x, __uint_as_float(r[jj]));
+                    x[j].y = fmaf(gl, x[j].y, __uint_as_float(r[jj + 1]));
+                    x[j].z = fmaf(gl, x[j].z, __uint_as_float(r[jj + 2]));
+                    x[j].w = fmaf(gl, x[j].w, __uint_as_float(r[jj + 3]));
+                    *(float4 *)((unsigned char *)ST + sw128_f32(128, v, q * 32 + 4 * j)) = x[j];
                 }
             }
             fence_proxy_async();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(stready);
+            if (!a.transition) {
+                Tout *op = o + (((size_t)b * a.T + t0) * a.H + h) * tc::kD + v;
+                const size_t tstride = (size_t)a.H * tc::kD;
+#pragma unroll
+                for (int t = 0; t < kC; ++t)
+                    if (t < L) op[t * tstride] = from_f32<Tout>(__uint_as_float(t < 32 ? ro0[t] : ro1[t - 32]));
+            }
+            tc_fence_before();
+            __syncwarp();
         }
         if (a.sT) {
             float *sT = a.sT + (size_t)bh * tc::kD * tc::kD + v;
