@@ -573,7 +573,13 @@ def run_ours(args, ws, rank, local):
     roof["gather_equiv_gbs"] = cnt["bytes_gather"] / (stages["sparse_attn_tc"] / 1e3) / 1e9
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = src
-    roof["traffic"] = None
+    # DRAM bytes per launch from the ncu captures of profiles/layer_kernels_b1_t8192_h16.md
+    # (B1 T8192 H16, one launch), scaled to this launch by its (b, h) count: the traffic of
+    # these kernels grows in proportion to the heads they process
+    per_bh = {"sparse_attn_tc": (422.06e6 + 24.97e6) / 16, "indexer_thresholds": 32.69e6 / 16,
+              "delta": (101.86e6 + 244.30e6 + 302.47e6 + 54.40e6) / 16}
+    roof["traffic"] = per_bh[dom] * cfg.B * cfg.H if cfg.T == 8192 else None
+    roof["traffic_source"] = "ncu dram bytes at B1 T8192 H16, scaled by b*h"
     roof["stage_ms"] = stages
 
     if rank == 0:
