@@ -54,8 +54,7 @@ constexpr int kKStage = kIQ + 16384;     // kKS stages x 24 KB: IK 8 KB | K 2 x 
 constexpr int kKBytes = 24576;
 constexpr int kVStage = kKStage + kKS * kKBytes;  // kVS stages x 16 KB: V 2 x 8 KB
 constexpr int kVBytes = 16384;
-constexpr int kP = kVStage + kVS * kVBytes;  // one P buffer per group: hi 16 KB | lo 16 KB
-constexpr int kBar = kP + kGroups * 32768;
+constexpr int kBar = kVStage + kVS * kVBytes;
 constexpr int kXmax = kBar + 256;                            // [group][slot][part][row] floats
 constexpr int kMrow = kXmax + kGroups * 2 * kParts * 128 * 4;  // [group][row]
 constexpr int kLrow = kMrow + kGroups * 128 * 4;             // [group][part][row]
@@ -165,7 +164,9 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             uint32_t idle = 0;
             while (jp < nkt) {
                 bool progress = false;
-                if (js < nkt) {
+                // S(js) overwrites the TMEM columns that hold P(js - 2): only after PV(js - 2)
+                // has been issued (the tensor pipe runs its MMAs in order)
+                if (js < nkt && js < jp + 2) {
                     const int st = js % kKS, buf = js & 1;
                     if (mbar_test_wait(&kfull[st], (js / kKS) & 1) &&
                         mbar_test_wait(&sfree[buf], ((js >> 1) & 1) ^ 1)) {
@@ -193,16 +194,16 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     if (mbar_test_wait(&vfull[vs], (jp / kVS) & 1) &&
                         mbar_test_wait(&pfull[g], (jp >> 1) & 1)) {
                         tc_fence_after();
-                        const uint32_t ph = smem_u32(sm + L::kP + g * 32768);
                         const uint32_t vq = smem_u32(sm + L::kVStage + vs * L::kVBytes);
+                        // P from TMEM (the group's index-score columns): keys [32 p, 32 p + 32)
+                        // as 16 columns of bf16 pairs, hi at +0, lo at +16 of column 32 p
 #pragma unroll
-                        for (int part = 0; part < 2; ++part)
-#pragma unroll
-                            for (int kk = 0; kk < 4; ++kk) {
-                                const uint64_t ad = sdesc_kmajor_sw128(ph + part * 16384 + kk * 32);
-                                const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
-                                mma_bf16(tO + g * 128, ad, bd, id_pv, ((jp >> 1) | part | kk) ? 1u : 0u);
-                            }
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const uint32_t a_hi = tSidx + g * kNk + (kk >> 1) * 32 + (kk & 1) * 8;
+                            const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
+                            mma_bf16_ts(tO + g * 128, a_hi, bd, id_pv, ((jp >> 1) | kk) ? 1u : 0u);
+                            mma_bf16_ts(tO + g * 128, a_hi + 16, bd, id_pv, 1u);
+                        }
                         mma_commit(&pfree[g]);
                         mma_commit(&vempty[vs]);
                         ++jp;
@@ -313,17 +314,15 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     if (grow) m_used = m_new;
                 }
             }
-            // P = exp2(x - m_used) as bf16 hi + lo, K-major rows of 64 keys
+            // P = exp2(x - m_used) as bf16 hi + lo pairs into this thread's own index-score
+            // columns (read above): the A operand of PV, straight from TMEM
             const float mref = (m_used == -INFINITY) ? 0.f : m_used;  // x = -inf -> p = 0
-            if (n_mine > 0) mbar_wait(&pfree[g], ((j >> 1) & 1) ^ 1, wd, 128u);
-            unsigned char *ph = sm + L::kP + g * 32768;
+            {
+                uint32_t hw[16], lw[16];
 #pragma unroll
-            for (int c8 = 0; c8 < kCP / 8; ++c8) {
-                uint32_t hw[4], lw[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float p0 = exp2f(x[c8 * 8 + 2 * u] - mref);
-                    const float p1 = exp2f(x[c8 * 8 + 2 * u + 1] - mref);
+                for (int u = 0; u < 16; ++u) {
+                    const float p0 = exp2f(x[2 * u] - mref);
+                    const float p1 = exp2f(x[2 * u + 1] - mref);
                     l += p0 + p1;
                     const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
                     const float2 hf = __bfloat1622float2(h2);
@@ -331,12 +330,11 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     hw[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lw[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                const int chunk = part * (kCP / 8) + c8;
-                const uint32_t off = (uint32_t)r * 128 + (uint32_t)((chunk ^ (r & 7)) << 4);
-                *(uint4 *)(ph + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-                *(uint4 *)(ph + 16384 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                const uint32_t pcol = tSidx + lrow + g * kNk + part * kCP;
+                tmem_st16u(pcol, hw);
+                tmem_st16u(pcol + 16, lw);
             }
-            fence_proxy_async();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfull[g]);
         }
