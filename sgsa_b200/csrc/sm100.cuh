@@ -178,6 +178,14 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// 2^x with the hardware approximation (ex2.approx.ftz: relative error ~2^-22, results
+// below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Arrive on `bar` once all previously issued tcgen05 ops of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile(

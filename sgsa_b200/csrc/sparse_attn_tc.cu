@@ -258,6 +258,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 m_used = bound;
             }
         }
+        // no row of this warp has a tie cut (the common case): selection is s >= a
+        const bool tie_free = __all_sync(0xffffffffu, cut == 0x7fffffff);
         int n_mine = 0;  // tiles of this group
         for (int j = g; j < nkt; j += 2, ++n_mine) {
             const int slot = (j >> 1) & 1;
@@ -267,19 +269,30 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             float mt = -INFINITY;
             const int jb0 = j * kNk + part * kCP;
             const bool full = jb0 + kCP - 1 <= q0;  // every row of the tile sees all columns
+            // x = the raw score where selected, -inf elsewhere (scaled inside the exponent);
+            // off the diagonal and without tie cuts in the warp the test is one compare
+            const bool simple = full && tie_free;
 #pragma unroll
             for (int hf = 0; hf < kCP / 16; ++hf) {
                 float si[16], sv[16];
                 tmem_ld16(tSidx + lrow + g * kNk + part * kCP + hf * 16, si);
                 tmem_ld16(tS + lrow + g * kNk + part * kCP + hf * 16, sv);
+                if (simple) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const int jj = jb0 + hf * 16 + i;
-                    const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
-                    const float xv = sel ? sv[i] * scale_log2 : -INFINITY;
-                    x[hf * 16 + i] = xv;
-                    if (!use_bound) mt = fmaxf(mt, xv);
+                    for (int i = 0; i < 16; ++i) x[hf * 16 + i] = si[i] >= a_thr ? sv[i] : -INFINITY;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int jj = jb0 + hf * 16 + i;
+                        const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
+                        x[hf * 16 + i] = sel ? sv[i] : -INFINITY;
+                    }
                 }
+            }
+            if (!use_bound) {
+#pragma unroll
+                for (int i = 0; i < kCP; ++i) mt = fmaxf(mt, x[i]);
+                mt *= scale_log2;  // scale > 0: the maximum of the scaled scores
             }
             tc_fence_before();
             __syncwarp();
@@ -321,8 +334,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 uint32_t hw[16], lw[16];
 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
-                    const float p0 = exp2f(x[2 * u] - mref);
-                    const float p1 = exp2f(x[2 * u + 1] - mref);
+                    const float p0 = ex2_approx(fmaf(x[2 * u], scale_log2, -mref));
+                    const float p1 = ex2_approx(fmaf(x[2 * u + 1], scale_log2, -mref));
                     l += p0 + p1;
                     const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
                     const float2 hf = __bfloat1622float2(h2);
@@ -330,9 +343,13 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     hw[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lw[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                const uint32_t pcol = tSidx + lrow + g * kNk + part * kCP;
-                tmem_st16u(pcol, hw);
-                tmem_st16u(pcol + 16, lw);
+                float pw[32];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    pw[u] = __uint_as_float(hw[u]);
+                    pw[16 + u] = __uint_as_float(lw[u]);
+                }
+                tmem_st32(tSidx + lrow + g * kNk + part * kCP, pw);
             }
             tc_fence_before();
             __syncwarp();
