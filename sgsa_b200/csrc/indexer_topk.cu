@@ -228,6 +228,7 @@ struct RowSel {
     bool fast;   // this pass bins the fast digit (mode, pb)
     int mode;
     int pb;
+    int etop;
 };
 
 // Key of a score for a row whose k-th score is a positive float: the raw bits
@@ -258,6 +259,7 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
             const bool toward_zero = s.mode == 0 ? chosen == 0 : s.mode == 1 ? chosen == 255 : false;
             if (toward_zero) {
                 s.mode = 2;
+                s.pb = fast_base(2, s.etop);
                 s.fast = true;
             } else {
                 s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32; s.plain = true;
@@ -269,8 +271,8 @@ __device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int 
         s.need -= cum;
         s.prefix = fast_prefix(chosen, s.mode, s.pb);
         const bool two = s.mode == 2;
-        s.mask = two ? 0xfff00000u : 0xfff80000u;
-        s.top = two ? 20 : 19;
+        s.mask = fast_mask(s.mode);
+        s.top = fast_top(s.mode);
         // negative k-th: continue on the order-preserving keys
         s.plain = s.mode == 1 || (two && chosen < 128);
         s.fast = false;
@@ -510,7 +512,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const bool has_row = epi && t < T;
     int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
     uint4 *thr_row = (has_row && thr) ? thr + (size_t)bh * T + t : nullptr;
-    RowSel s{0u, 0u, K, 32, true, false, true, 0, false, false, 0, (kDefaultEtop - 16) << 4};
+    RowSel s{0u, 0u, K, 32, true, false, true, 0, false, false, 0, fast_base(0, kDefaultEtop),
+             kDefaultEtop};
     if (epi && nvalid > K) {
         s.done = false;
         s.exact = false;
@@ -639,7 +642,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const uint32_t o = s_xch[0][half ^ 1][row];
                             const int npos = np + (int)(o & 0xffffu), nval = nv + (int)(o >> 16);
                             const int etop = min(max((int)(s_amax >> 23) + 3, 17), 255);  // bottom above 0 and denormals
-                            s.pb = (etop - 16) << 4;
+                            s.etop = etop;
                             // estimated positives p*(t+1) against need: clear margins pick a sign
                             const float p = nval ? (float)npos / (float)nval : 0.5f;
                             const float q = (float)s.need / (float)nvalid;
@@ -648,6 +651,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const bool all0 = __all_sync(0xffffffffu, !active || m == 0);
                             const bool all1 = __all_sync(0xffffffffu, !active || m == 1);
                             s.mode = all0 ? 0 : all1 ? 1 : 2;
+                            s.pb = fast_base(s.mode, etop);
                             s.fast = true;
                         }
                         if (!active || jb >= nvalid) continue;

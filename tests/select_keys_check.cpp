@@ -20,8 +20,8 @@ int main() {
     long bad = 0, n = 0;
     for (int etop = 17; etop <= 255; ++etop)
         for (int mode = 0; mode < 3; ++mode) {
-            const int pb = (etop - 16) << 4;
-            const uint32_t mask = mode == 2 ? 0xfff00000u : 0xfff80000u;
+            const int pb = fast_base(mode, etop);
+            const uint32_t mask = fast_mask(mode);
             auto clamp_bin = [&](uint32_t d) { return d == 0 || d == 255 || (mode == 2 && d == 127); };
             std::vector<float> vals = {0.f, -0.f};
             for (int i = 0; i < 4000; ++i) {
