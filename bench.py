@@ -51,7 +51,8 @@ def peaks():
 
 
 def algorithmic_counts(cfg):
-    """Per-layer-forward FLOPs and bytes of each stage (formulas in DESIGN.md)."""
+    """Per-layer-forward FLOPs and bytes of each stage: delta 6 D^2 + 2C(3D + 2D) per
+    token-head, indexer 2 DI per causal pair, gathered rows 2 D bf16 values per selected pair."""
     B, T, H, D, K, DI = cfg.B, cfg.T, cfg.H, cfg.D, cfg.top_k, cfg.d_idx
     C = cfg.chunk
     f_delta = B * T * H * (6 * D * D + 2 * C * (3 * D + 2 * D))
