@@ -6,11 +6,12 @@
 // scores ordered by the lower j first.  Output indices are ascending, the
 // remaining slots are -1.
 //
-// Algorithm: one thread owns one query row.  An MSB-first radix select over
-// the 32-bit order-preserving key of the fp32 score runs in up to four 8-bit
-// digit passes; pass p counts, in a per-thread 256-bin histogram held in
-// shared memory as hist[bin][thread] (bank = thread, so conflict free), the
-// scores whose higher digits match the prefix chosen so far.  A row is
+// Algorithm: an MSB-first radix select over the 32-bit order-preserving key of
+// the fp32 score (the CUDA-core path: one thread per query row, up to four 8-bit
+// digit passes; the tensor-core path below: a sampled first digit and a candidate
+// pass); each pass counts, in a per-row 256-bin histogram held in shared memory as
+// hist[bin][row] (bank = row, so conflict free), the scores whose higher digits
+// match the prefix chosen so far.  A row is
 // resolved as soon as the chosen bin holds exactly the number of elements
 // still needed.  A final pass emits, in index order, every column whose masked
 // key is above the prefix plus the first `need` columns equal to it -- which
@@ -202,16 +203,19 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 // The key stream is replayed once per pass; the tensor cores recompute the
 // identical fp32 scores each time.
 //
-// Digits.  The first pass bins the top 12 bits of the order-preserving key
-// (sign, exponent, 3 mantissa bits: 1/8-octave bins) of positive scores in
-// [2^-16, 2^16), clamping the rest into bins 0 and 255.  If a row's k-th score
-// falls in an interior bin, its 12-bit prefix is known after one pass and the
-// remaining 20 bits follow as 8-, 8- and 4-bit digits; if it falls in a clamp
-// bin, the row restarts with plain 8-bit digits from the top.  Either way the
-// selection is exact.  Rows shorter than 65536 use 16-bit counters packed two
-// per 32-bit word (64 KB), so the CTA needs ~105 KB and two CTAs share an SM.
-// Counters are bumped with predicated shared-memory reductions: no branches,
-// no returned values, and the two threads of a row may share a counter.
+// Digits.  The first pass bins a fast digit of each score over a window placed
+// from a sample of the first key tile (select_keys.cuh: 1/32-octave bins of one
+// sign, or 1/8-octave bins of both signs when the sample leaves the k-th score's
+// sign unclear).  A row whose k-th score lands in an interior bin knows the top
+// 13-14 bits of its key; if the bin then holds at most 128 keys for every row of
+// the warp, the next pass stores those keys (candidate mode) and the k-th is found
+// among them in shared memory; otherwise 8-bit digits follow.  A k-th score in a
+// clamp bin retries the other window once or restarts with plain 8-bit digits
+// from the top.  Every path is exact.  Rows shorter than 65536 use 16-bit
+// counters packed two per 32-bit word (64 KB), so the CTA needs ~105 KB and two
+// CTAs share an SM.  Counters are bumped with predicated shared-memory
+// reductions: no branches, no returned values, and the two threads of a row may
+// share a counter.
 static __device__ unsigned int g_index_watchdog;
 
 constexpr int kEpiThreads = 256;
