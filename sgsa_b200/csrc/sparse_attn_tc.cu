@@ -16,9 +16,13 @@
 // reads each K/V tile once per 128 queries instead of once per query.
 //
 // P is fed to the PV MMA as bf16 hi + lo parts (p = hi + lo to ~2^-16), so the
-// result keeps fp32-level accuracy with V in bf16.  The running maximum is
-// updated lazily: O and the row sum are rescaled only when a tile's maximum
-// exceeds the one in use by more than 2^8, which keeps p <= 256 and is exact.
+// result keeps fp32-level accuracy with V in bf16; the parts are written with
+// tcgen05.st over the index-score columns the thread has just read and enter the
+// MMA as a tensor-memory A operand.  The softmax reference is a fixed bound
+// (max|q| max|k| scale, from a norm pre-pass) when that keeps p within 2^-120;
+// otherwise the running maximum is updated lazily: O and the row sum are
+// rescaled only when a tile's maximum exceeds the one in use by more than 2^8,
+// which keeps p <= 256 and is exact.
 //
 // With HI == 1 (a shared-across-heads indexer, one index set per token as in
 // the DeepSeek indexer of modelings/deepseek_v3_2.py:435-487) every head reads
@@ -26,10 +30,12 @@
 //
 // Warp roles (96 + 128 kParts kGroups threads, one CTA per (b, h, 128-query tile)):
 // warp 0 TMA, warp 1 TMEM owner + MMA issuer, warp 2 TMA of the values, warps 3..
-// softmax: two groups that take alternate key tiles (each with its own S and P
+// softmax: two groups that take alternate key tiles (each with its own score
 // buffers and its own O accumulator in TMEM, an online softmax each, merged at the
 // end), so that one group's softmax overlaps the other's and the MMAs; kParts
-// threads per query row in each group.
+// threads per query row in each group.  The MMA warp issues event-driven: the
+// scores of a tile once its keys have landed, its buffer is free and the PV two
+// tiles back (whose P shares those TMEM columns) has been issued; PV in order.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
