@@ -5,20 +5,28 @@
 One step = one SGSA layer forward (chunked delta stage, causal top-k
 indexer, sparse attention over the selected rows, gate) over the
 ``b200_bf16`` configuration: B=4, T=8192, H=16, d=128, top-k 512, indexer dim
-64, bf16 inputs with fp32 accumulation.  Multi-GPU runs are (batch x head)
-shards with no communication (weak scaling): rank r processes its own
-configuration-sized shard drawn with seed r.
+64, bf16 inputs with fp32 accumulation.  Multi-GPU runs split that one
+workload (strong scaling): rank r takes a contiguous block of the B*H = 64
+(batch, head) pairs, which need no communication.  The line also carries
+``long_ctx``: configs[2] (T 65536, H32, top-k 2048) on one GPU and, for N > 1,
+sequence parallel over the N ranks (NCCL all-gather of the keys, all-to-all of
+the query and output tiles) with its efficiency against the one-GPU time and
+per-phase times.
 
 ``value`` is whole-job tokens/s with inputs resident in HBM (CUDA events on
 the launching stream, max over ranks).  ``e2e`` is the same metric through the
 public op with host (pinned) inputs: the host->device copies of all inputs and
 the device->host copy of the output are inside its timed region.  The inputs
 (q, k, v, iq, ik, mix: 470 MB per step) are larger than the 126 MB L2, so no
-extra flush is done between steps.
+extra flush is done between steps.  ``gpu_launches`` is the library's own
+launch counter over the timed region.
 
-``--impl reference`` times the CPU restatement of the reference's algorithm
-(oracle/, float64, OpenMP over all host threads) on a bounded sample of the
-same workload, on rank 0 only.
+``--impl reference`` times the reference's CPU PyTorch path (its
+naive_recurrent_sgsa from the install under baseline/_ref, plus the top-k
+attention tensor operations of its hybrid model, blocked over queries) on
+bounded samples of the same workload, on rank 0 only; each timed step is one
+sample (2 heads of batch row 0, every query).  Without the install it times the
+float64 C restatement under oracle/ and says so.
 """
 from __future__ import annotations
 
@@ -66,6 +74,16 @@ def algorithmic_counts(cfg):
     return dict(f_delta=f_delta, f_idx=f_idx, f_sp=f_sp, f_attn_tc=f_attn_tc,
                 bytes_gather=bytes_gather,
                 bytes_io=bytes_io, selected=B * H * sel)
+
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per (batch, head) of one
+# launch at T = 8192, from ncu captures of the launches at B1 T8192 H16 (the command
+# of each is in TRAFFIC_SOURCE); the traffic of these kernels grows in proportion to
+# the (batch, head) pairs a launch processes.
+TRAFFIC_PER_BH = {"sparse_attn_tc": (422.06e6 + 24.97e6) / 16, "indexer_thresholds": 32.69e6 / 16,
+                  "delta": (101.86e6 + 244.30e6 + 302.47e6 + 54.40e6) / 16}
+TRAFFIC_SOURCE = ("ncu dram bytes of one launch at B1 T8192 H16 (python bench.py --only <stage> "
+                  "--steps 1 --B 1 --H 16), scaled by the launch's (b, h) count")
 
 
 class ClockSampler:
@@ -149,23 +167,124 @@ def barrier(ws):
     torch.cuda.synchronize()
 
 
-def cpu_reference(cfg, cores: int):
-    """Time the oracle port on batch row 0 of the workload (all heads, all T queries:
-    exactly 1/B of it) with `cores` threads; returns (tokens/s, sample text, seconds)."""
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+REF_HEADS_PER_STEP = 2
+
+
+def reference_available() -> bool:
+    return os.path.isdir(os.path.join(REF_DIR, "modelings"))
+
+
+def _reference_naive():
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    from modelings.sgsa_ops.naive import naive_recurrent_sgsa
+    return naive_recurrent_sgsa
+
+
+def reference_cpu_sample(x, h0, h1, top_k, q_block=512):
+    """One bounded sample of the reference's CPU PyTorch path, float32, on batch row 0
+    and heads [h0, h1) of the workload, every query: the delta stage by the
+    reference's own naive_recurrent_sgsa (modelings/sgsa_ops/naive.py:10-57); the
+    selection, sparse attention and gate by the tensor operations of
+    modelings/hybrid_dense_delta_topk.py:343-356,389-390 (score matmul, causal
+    finfo.min mask, torch.topk, float32 softmax, gather, weighted sum, sigmoid-gate
+    mix) with the indexer iq . ik choosing the rows and q . k / sqrt(d) weighting
+    them, run over blocks of q_block queries (the reference's single [B,H,T,k,D]
+    gather would need 137 GB at this size).  Returns (seconds, output)."""
+    naive = _reference_naive()
+    sl = {n: t[:1, :, h0:h1].float().contiguous() for n, t in x.items()}
+    T, Hs, D = sl["q"].shape[1], sl["q"].shape[2], sl["q"].shape[3]
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        o_delta, _ = naive(sl["q"], sl["k"], sl["v"], sl["beta"], sl["gamma"])
+        q, k, v = (sl[n][0].transpose(0, 1) for n in ("q", "k", "v"))     # [H, T, D]
+        iq, ik = (sl[n][0].transpose(0, 1) for n in ("iq", "ik"))
+        scale = 1.0 / math.sqrt(D)
+        out = torch.empty(Hs, T, D)
+        neg = torch.finfo(torch.float32).min
+        for s0 in range(0, T, q_block):
+            s1 = min(T, s0 + q_block)
+            pos = torch.arange(s0, s1)[:, None]
+            causal = torch.arange(s1)[None, :] <= pos                       # [Q, s1]
+            idx_scores = (iq[:, s0:s1] @ ik[:, :s1].transpose(1, 2)).masked_fill(~causal, neg)
+            kk = min(top_k, s1)
+            _, sel = torch.topk(idx_scores, k=kk, dim=-1)                   # [H, Q, kk]
+            att = (q[:, s0:s1] @ k[:, :s1].transpose(1, 2)) * scale
+            att = att.gather(-1, sel).masked_fill(sel > pos, float("-inf"))
+            p = torch.softmax(att, dim=-1)
+            vsel = torch.gather(v[:, None].expand(-1, s1 - s0, -1, -1), 2,
+                                sel[..., None].expand(-1, -1, -1, D))
+            out[:, s0:s1] = (p[..., None] * vsel).sum(2)
+        m = sl["mix"][0].transpose(0, 1)
+        res = m * out + (1.0 - m) * o_delta[0].transpose(0, 1)
+    return time.perf_counter() - t0, res
+
+
+def reference_chunk_sample(x, h0, h1):
+    """Seconds of the reference's own chunk_sgsa (torch path, modelings/sgsa_ops/chunk.py)
+    on the same sample's delta stage; reported beside the baseline only: at this
+    decay its clamped cumprods make it numerically wrong (rel-L2 ~0.8 at configs[0])."""
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    from modelings.sgsa_ops import chunk_sgsa
+    sl = {n: t[:1, :, h0:h1].float().contiguous() for n, t in x.items()}
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        chunk_sgsa(sl["q"], sl["k"], sl["v"], sl["beta"], sl["gamma"], use_triton=False)
+    return time.perf_counter() - t0
+
+
+def cpu_port_sample(cfg, x, h0, h1):
+    """Seconds of the repository's float64 C restatement (oracle/) on the same sample."""
     from oracle import oracle
+
+    oracle.set_num_threads(os.cpu_count() or 1)
+    sl = {n: t[:1, :, h0:h1].contiguous() for n, t in x.items()}
+    t0 = time.perf_counter()
+    od, _ = oracle.sgsa_recurrent(sl["q"], sl["k"], sl["v"], sl["beta"], sl["gamma"])
+    idx = oracle.indexer_topk(sl["iq"], sl["ik"], cfg.top_k)
+    oracle.sparse_attn_mix(sl["q"], sl["k"], sl["v"], idx, od, sl["mix"])
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(cfg, steps: int, warmup: int):
+    """Times `steps` samples (after `warmup` untimed ones) of the reference's CPU path,
+    each REF_HEADS_PER_STEP heads of batch row 0 over all T queries, so one sample is
+    T * REF_HEADS_PER_STEP / H tokens' worth of the workload.  Returns the
+    cpu_baseline object (value in tokens/s) and the per-step seconds."""
     from sgsa_b200.inputs import make_inputs
 
-    oracle.set_num_threads(cores)
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
     x = make_inputs(cfg.scaled(B=1), seed=0)
-    t0 = time.perf_counter()
-    od, _ = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"])
-    idx = oracle.indexer_topk(x["iq"], x["ik"], cfg.top_k)
-    oracle.sparse_attn_mix(x["q"], x["k"], x["v"], idx, od, x["mix"])
-    secs = time.perf_counter() - t0
-    sample = (f"batch row 0 of the workload (T={cfg.T}, all {cfg.H} heads, every query: delta "
-              f"recurrence, causal top-{cfg.top_k} indexer, sparse attention, gate), float64, "
-              f"{cores} threads; tokens/s = T / seconds")
-    return cfg.T / secs, sample, secs
+    hs = REF_HEADS_PER_STEP
+    heads = [(i * hs) % cfg.H for i in range(warmup + steps)]
+    tok = cfg.T * hs / cfg.H
+    if reference_available():
+        for i in range(warmup):
+            reference_cpu_sample(x, heads[i], heads[i] + hs, cfg.top_k)
+        secs = [reference_cpu_sample(x, h, h + hs, cfg.top_k)[0] for h in heads[warmup:]]
+        kind = "reference"
+        what = ("the reference's CPU PyTorch path (naive_recurrent_sgsa + the top-k "
+                "attention/gate tensor ops of hybrid_dense_delta_topk.py:343-356,389-390, "
+                f"blocked over 512 queries), float32")
+        extra = {"chunk_sgsa_s": reference_chunk_sample(x, 0, hs),
+                 "chunk_sgsa_note": "reference chunk_sgsa on the same delta sample; "
+                                    "numerically wrong at this decay, not the baseline"}
+    else:
+        for i in range(warmup):
+            cpu_port_sample(cfg, x, heads[i], heads[i] + hs)
+        secs = [cpu_port_sample(cfg, x, h, h + hs) for h in heads[warmup:]]
+        kind = "port"
+        what = "the float64 C restatement of the reference maths (oracle/)"
+        extra = {"note": "reference not installed under baseline/_ref"}
+    mean = statistics.mean(secs)
+    sample = (f"{what} on batch row 0, {hs} of {cfg.H} heads per step (heads cycle), all "
+              f"T={cfg.T} queries, top-{cfg.top_k}; {cores} threads; tokens/s = "
+              f"T*{hs}/{cfg.H} / seconds per step")
+    return dict(value=tok / mean, unit=UNIT, cores=cores, kind=kind, sample=sample,
+                seconds_per_step=mean, steps=len(secs), **extra), secs
 
 
 def run_reference(args, ws, rank):
@@ -174,23 +293,19 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     cfg = CONFIGS[CONFIG_NAME]
-    cores = os.cpu_count() or 1
-    vals, sample = [], ""
-    # every step is one batch row of the workload (~10 s of CPU work); at most 3 are
-    # timed so that the run stays within a few minutes whatever --steps is
-    for _ in range(min(max(args.steps, 1), 3)):
-        v, sample, _ = cpu_reference(cfg, cores)
-        vals.append(v)
-    v = statistics.median(vals)
+    warm = min(args.warmup, 1)
+    base, secs = cpu_baseline(cfg, max(args.steps, 1), warm)
+    v = base["value"]
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": ws,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cfg.tokens / v * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "steps": len(secs), "warmup": warm, "ms_per_step": statistics.mean(secs) * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, configs[1] shapes/distributions)",
         "config": {"workload": CONFIG_NAME, "B": cfg.B, "T": cfg.T, "H": cfg.H, "d": cfg.D,
-                   "top_k": cfg.top_k, "d_idx": cfg.d_idx, "chunk": cfg.chunk},
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample},
+                   "top_k": cfg.top_k, "d_idx": cfg.d_idx, "chunk": cfg.chunk,
+                   "parallelism": "cpu, rank 0", "l2": "n/a (host)",
+                   "step": f"batch row 0, {REF_HEADS_PER_STEP} heads, all {cfg.T} queries"},
+        "cpu_baseline": {k: base[k] for k in ("kind", "cores", "sample", "value", "unit")},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -506,12 +621,84 @@ def run_only(args):
                       "config": {"B": cfg.B, "T": cfg.T, "H": cfg.H}}))
 
 
+def shard_of(cfg, ws: int, rank: int):
+    """(b0, b1, h0, h1): rank's contiguous block of the B*H (batch, head) pairs."""
+    if ws <= cfg.B:
+        if cfg.B % ws:
+            raise SystemExit(f"--gpus {ws} must divide the batch {cfg.B}")
+        nb = cfg.B // ws
+        return rank * nb, (rank + 1) * nb, 0, cfg.H
+    per_b = ws // cfg.B
+    if ws % cfg.B or cfg.H % per_b:
+        raise SystemExit(f"--gpus {ws} must split B*H = {cfg.B}*{cfg.H} evenly")
+    nh = cfg.H // per_b
+    b, j = divmod(rank, per_b)
+    return b, b + 1, j * nh, (j + 1) * nh
+
+
+def long_ctx_run(ws, rank, local, steps=3):
+    """configs[2] (B1 T65536 H32, top-k 2048): the single-GPU layer on rank 0 (the
+    1-GPU reference of the efficiency) and, for N > 1, the sequence-parallel layer
+    on all ranks with per-phase times of one step."""
+    from sgsa_b200 import ops, sp
+    from sgsa_b200.inputs import CONFIGS, make_inputs_slice
+
+    cfg = CONFIGS["long_ctx"]
+    names = ("q", "k", "v", "beta", "gamma", "iq", "ik", "mix")
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    res = {"config": {"B": cfg.B, "T": cfg.T, "H": cfg.H, "d": cfg.D, "top_k": cfg.top_k,
+                      "d_idx": cfg.d_idx}, "steps": steps}
+    ms1 = 0.0
+    if rank == 0:
+        x = make_inputs_slice(cfg, 0, cfg.T, seed=0, device="cuda")
+        args_ = [x[n] for n in names] + [cfg.top_k]
+        ops.sgsa_layer_fwd(*args_)
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(steps):
+            ops.sgsa_layer_fwd(*args_)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms1 = e0.elapsed_time(e1) / steps
+        del x, args_
+        ops.release_workspaces()
+        torch.cuda.empty_cache()
+    res["ms_1gpu"] = max_over_ranks(ms1, ws)
+    if ws == 1:
+        res["tokens_per_s_1gpu"] = cfg.tokens / (res["ms_1gpu"] / 1e3)
+        return res
+    Tl = cfg.T // ws
+    x = make_inputs_slice(cfg, rank * Tl, (rank + 1) * Tl, seed=0, device="cuda")
+    args_ = [x[n] for n in names] + [cfg.top_k]
+    sp.sp_layer_fwd(*args_)
+    barrier(ws)
+    e0.record(st)
+    for _ in range(steps):
+        sp.sp_layer_fwd(*args_)
+    e1.record(st)
+    barrier(ws)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, ws)
+    tm = {}
+    sp.sp_layer_fwd(*args_, timings=tm)
+    barrier(ws)
+    phases = {k: max_over_ranks(v, ws) for k, v in sorted(sp.phase_ms(tm).items())}
+    res.update(ms_sp=ms, parallelism=f"sp{ws}", tokens_per_s=cfg.tokens / (ms / 1e3),
+               efficiency=res["ms_1gpu"] / (ws * ms), phase_ms_max_over_ranks=phases)
+    return res
+
+
 def run_ours(args, ws, rank, local):
-    from sgsa_b200 import ops
+    from sgsa_b200 import _lib, ops
     from sgsa_b200.inputs import CONFIGS, make_inputs
 
+    lib = _lib.load()
     cfg = CONFIGS[CONFIG_NAME]
-    host = make_inputs(cfg, seed=rank)
+    b0, b1, h0, h1 = shard_of(cfg, ws, rank)
+    full = make_inputs(cfg, seed=0)  # the same workload at every N; rank r takes its shard
+    host = {n: t[b0:b1, :, h0:h1].contiguous() for n, t in full.items()}
+    del full
+    scfg = cfg.scaled(B=b1 - b0, H=h1 - h0)
     d = {n: t.cuda() for n, t in host.items()}
     names = ["q", "k", "v", "beta", "gamma", "iq", "ik", "mix"]
 
@@ -527,10 +714,12 @@ def run_ours(args, ws, rank, local):
     with ClockSampler(local) as clk:
         barrier(ws)
         t_start = time.perf_counter()
+        n0 = lib.sgsa_kernel_launches()
         e0.record(st)
         for _ in range(args.steps):
             step()
         e1.record(st)
+        n1 = lib.sgsa_kernel_launches()
         barrier(ws)
         # short timed regions: keep the same load (untimed) until the sampler has
         # seen at least ~1 s of it
@@ -538,13 +727,18 @@ def run_ours(args, ws, rank, local):
             step()
             torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, ws)
-    value = ws * cfg.tokens / (ms / 1e3)
+    value = cfg.tokens / (ms / 1e3)  # the whole configs[1] workload, split over the ranks
+    launches = n1 - n0
+    if ws > 1:
+        t = torch.tensor([launches], device="cuda", dtype=torch.int64)
+        dist.all_reduce(t)
+        launches = int(t.item())
 
     # end to end: pinned host inputs -> device -> layer -> host output
     pinned = {n: host[n].pin_memory() for n in names}
-    out_host = torch.empty(cfg.B, cfg.T, cfg.H, cfg.D, dtype=cfg.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in pinned.values())
-    d2h = out_host.numel() * out_host.element_size()
+    out_host = torch.empty(scfg.B, scfg.T, scfg.H, scfg.D, dtype=scfg.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in pinned.values()) * ws
+    d2h = out_host.numel() * out_host.element_size() * ws
 
     def e2e_step():
         ops.sgsa_layer_fwd_from_host(*(pinned[n] for n in names), cfg.top_k, out=out_host)
@@ -560,10 +754,9 @@ def run_ours(args, ws, rank, local):
     barrier(ws)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, ws)
 
-    stages = stage_times(cfg, d)
-    cnt = algorithmic_counts(cfg)
+    stages = stage_times(scfg, d)
+    cnt = algorithmic_counts(scfg)
     hbm, tfl, src = peaks()
-    # the dominant kernel and its roofline
     # the dominant kernel among the stages the layer runs, and its roofline
     layer_stages = ("delta", "indexer_thresholds", "sparse_attn_tc")
     dom = max(layer_stages, key=lambda n: stages[n])
@@ -571,44 +764,46 @@ def run_ours(args, ws, rank, local):
              "sparse_attn_tc": cnt["f_attn_tc"]}[dom]
     ach = flops / (stages[dom] / 1e3) / 1e12
     roof = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": tfl, "unit": "TFLOP/s"}
-    roof["gather_equiv_gbs"] = cnt["bytes_gather"] / (stages["sparse_attn_tc"] / 1e3) / 1e9
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof["peak_source"] = src
-    # DRAM bytes per launch from the ncu captures of profiles/layer_kernels_b1_t8192_h16.md
-    # (B1 T8192 H16, one launch), scaled to this launch by its (b, h) count: the traffic of
-    # these kernels grows in proportion to the heads they process
-    per_bh = {"sparse_attn_tc": (422.06e6 + 24.97e6) / 16, "indexer_thresholds": 32.69e6 / 16,
-              "delta": (101.86e6 + 244.30e6 + 302.47e6 + 54.40e6) / 16}
-    roof["traffic"] = per_bh[dom] * cfg.B * cfg.H if cfg.T == 8192 else None
-    roof["traffic_source"] = "ncu dram bytes at B1 T8192 H16, scaled by b*h"
+    roof["traffic"] = (TRAFFIC_PER_BH[dom] * scfg.B * scfg.H
+                       if scfg.T == 8192 and dom in TRAFFIC_PER_BH else None)
+    roof["traffic_source"] = TRAFFIC_SOURCE
     roof["stage_ms"] = stages
+    roof["gather_equiv_gbs"] = cnt["bytes_gather"] / (stages["sparse_attn_tc"] / 1e3) / 1e9
     if dom == "indexer_thresholds":
         roof["note"] = ("the indexer's tensor work is 2*DI FLOPs per causal pair; it is bound by the "
-                        "CUDA-core selection (ALU pipe ~77% in ncu), not by the tensor cores")
-    # the tensor-bound kernel of the step, for reference
+                        "CUDA-core selection, not by the tensor cores")
     ach_attn = cnt["f_attn_tc"] / (stages["sparse_attn_tc"] / 1e3) / 1e12
     roof["sparse_attn_tc"] = {"achieved": ach_attn, "peak": tfl, "unit": "TFLOP/s",
-                              "frac": ach_attn / tfl}
+                              "frac": ach_attn / tfl,
+                              "useful_frac": cnt["f_sp"] / (stages["sparse_attn_tc"] / 1e3) / 1e12 / tfl,
+                              "note": "frac counts every causal pair the kernel computes; "
+                                      "useful_frac only the selected pairs (F_sp)"}
+    long_ctx = long_ctx_run(ws, rank, local) if not args.no_long else None
 
     if rank == 0:
-        cores = os.cpu_count() or 1
-        cpu_v, sample, secs = cpu_reference(cfg, cores)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded, configs[1] shapes/distributions; rank r uses seed r)",
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded, configs[1] shapes/distributions; one workload at every N)",
             "config": {"workload": CONFIG_NAME, "B": cfg.B, "T": cfg.T, "H": cfg.H, "d": cfg.D,
                        "top_k": cfg.top_k, "d_idx": cfg.d_idx, "chunk": cfg.chunk,
-                       "parallelism": f"bh-shard x{ws}", "l2": "inputs 470 MB > L2, no flush"},
-            "e2e": {"value": ws * cfg.tokens / (e2e_ms / 1e3), "unit": UNIT,
+                       "parallelism": "single" if ws == 1 else f"bh-shard x{ws}",
+                       "shard_rank0": {"B": scfg.B, "H": scfg.H},
+                       "l2": "inputs 470 MB > L2, no flush"},
+            "e2e": {"value": cfg.tokens / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": 6 * args.steps,  # prep, scan, q/k norms, indexer, attention, gate
+            "gpu_launches": launches,
+            "gpu_launches_source": "sgsa_kernel_launches() counter, timed region, all ranks",
             "roofline": roof,
-            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": sample, "seconds": secs},
             "clocks": clk.summary(),
         }
+        if long_ctx is not None:
+            line["long_ctx"] = long_ctx
+        if ws == 1 and not args.no_cpu:
+            line["cpu_baseline"], _ = cpu_baseline(cfg, 3, 1)
         print(json.dumps(line), flush=True)
 
 
@@ -627,6 +822,9 @@ def main():
                          "sequence parallel for N > 1); hybrid: configs[3] (24-layer "
                          "hybrid model prefill, B 8 x T 4096, batch sharded); layer "
                          "(default): configs[1]")
+    ap.add_argument("--no-long", action="store_true",
+                    help="skip the configs[2] long_ctx measurement of the default workload")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--B", type=int, default=None)
     ap.add_argument("--T", type=int, default=None)
     ap.add_argument("--H", type=int, default=None)

@@ -5,7 +5,10 @@
  * cudaStream_t (passed as void*), returns an int status (SGSA_OK == 0, a
  * negative SGSA_ERR_* otherwise) and never aborts or traps.  The library keeps
  * no pointers between calls and allocates nothing: outputs and workspaces are
- * owned by the caller, sized with the *_workspace_size queries.
+ * owned by the caller, sized with the *_workspace_size queries.  The library
+ * holds, per device, cached kernel attributes, the device watchdog words
+ * (sgsa_watchdog_status) and the no-allocation entry point's scratch array, and
+ * per host thread and device the side stream of sgsa_layer_fwd.
  *
  * Tensor layouts follow the reference (row-major, contiguous):
  *   q, k, v, sparse_k, sparse_v, o     [B, T, H, D]          dtype
@@ -61,6 +64,10 @@ const char *sgsa_last_error(void);
 /* Library version, e.g. 1000 for 0.1.0. */
 int sgsa_version(void);
 
+/* Number of kernels this library has launched in this process (all devices and
+ * threads).  No reference counterpart: it lets a benchmark count its launches. */
+unsigned long long sgsa_kernel_launches(void);
+
 /*
  * Synchronises `stream`, returns and clears the device watchdog word: 0 when
  * every bounded wait inside the tensor-core kernels completed, else a bitmask
@@ -68,6 +75,14 @@ int sgsa_version(void);
  * counterpart: the reference's Triton kernels have no device-side waits.
  */
 int sgsa_watchdog_status(void *stream);
+
+/*
+ * Exercises the watchdog path: launches one thread that waits, with at most
+ * spin_limit polls (1 .. 2^20), on a barrier nothing arrives at.  The wait gives
+ * up and the kernel returns; the next sgsa_watchdog_status on `stream` then
+ * reports bit 0x80.  No reference counterpart (test support).
+ */
+int sgsa_watchdog_selftest(unsigned int spin_limit, void *stream);
 
 /*
  * Chunked SGSA / gated-delta-rule forward.
@@ -94,7 +109,10 @@ int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta
  * rejected with SGSA_ERR_WORKSPACE.  The first call on each device looks up
  * the array's device address, so make it before any stream capture.  All
  * calls share the array: calls that overlap on the GPU race and must be
- * serialised by the caller.  The call allocates and frees nothing.
+ * serialised by the caller.  SGSA_FLAG_REUSE_PREP is refused with
+ * SGSA_ERR_UNSUPPORTED, since the shared array may hold another caller's
+ * operands.  A cudaDeviceReset invalidates the cached address: do not call
+ * this entry point after one.  The call allocates and frees nothing.
  */
 int sgsa_chunk_fwd_noalloc(const void *q, const void *k, const void *v, const void *beta,
                            const void *gamma, const void *sparse_k, const void *sparse_v,
@@ -112,6 +130,17 @@ int sgsa_chunk_fwd_noalloc(const void *q, const void *k, const void *v, const vo
  */
 int sgsa_indexer_topk(const void *iq, const void *ik, int32_t *indices, int B, int T, int H,
                       int DI, int top_k, int dtype, void *stream);
+
+/*
+ * Test support for the tensor-core indexer (bf16, DI 64 or 128, T <= 4096): the
+ * call of sgsa_indexer_topk that also writes the fp32 scores its selection ran on,
+ * scores[B,H,T,T] (row t: columns j <= t; rows t < top_k, which keep every
+ * column, may be left unwritten).  Selecting top_k on those very scores with the
+ * rule of modelings/modeling_sgsa.py:155-164 (ties to the lowest index) must
+ * give `indices` bit for bit.
+ */
+int sgsa_indexer_topk_scores(const void *iq, const void *ik, int32_t *indices, float *scores,
+                             int B, int T, int H, int DI, int top_k, void *stream);
 
 /*
  * Row-wise top-k of a float32 score matrix [R, S] where row r considers
@@ -196,11 +225,21 @@ int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void 
 /*
  * The composite layer forward: chunked delta stage (no sparse write),
  * indexer top-k, sparse attention and gate, in one stream-ordered call.
- * indices may be NULL (kept in the workspace).  final_state may be NULL.
+ * Replaces the core of SGSAStateLayer.forward (modelings/modeling_sgsa.py:522-619)
+ * with the top-k attention and gate of modelings/hybrid_dense_delta_topk.py:343-390.
+ * indices may be NULL.  final_state may be NULL.
  * iq, ik are [B,T,idx_heads,DI] with idx_heads == H (per-head selection) or 1
  * (one selection per token shared by all heads).
+ * The workspace depends on the path the call takes: bf16 with D == 128 and
+ * DI in {64, 128} runs the tensor-core indexer and attention and keeps 16-byte
+ * selection records per row; every other case keeps B*idx_heads*T*top_k int32
+ * index rows.  The delta stage runs on a non-blocking side stream with a fork
+ * and a join event, created on the first call of each host thread on each
+ * device and reused by that thread's later calls; the call joins it back into
+ * `stream` before the gate, so the call is stream-ordered as a whole.
  */
-size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top_k);
+size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int idx_heads,
+                                     int top_k, int dtype);
 int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta,
                    const void *gamma, const void *iq, const void *ik, const void *mix,
                    const float *initial_state, void *out, float *final_state, int32_t *indices,

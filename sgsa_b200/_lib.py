@@ -25,11 +25,14 @@ SIGNATURES = {
     "sgsa_status_string": (ctypes.c_char_p, [_i]),
     "sgsa_last_error": (ctypes.c_char_p, []),
     "sgsa_version": (_i, []),
+    "sgsa_kernel_launches": (ctypes.c_ulonglong, []),
     "sgsa_watchdog_status": (_i, [_vp]),
+    "sgsa_watchdog_selftest": (_i, [ctypes.c_uint, _vp]),
     "sgsa_chunk_fwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "sgsa_chunk_fwd": (_i, [_vp] * 11 + [_i] * 7 + [_vp, _sz, _vp]),
     "sgsa_chunk_fwd_noalloc": (_i, [_vp] * 11 + [_i] * 7 + [_vp]),
     "sgsa_indexer_topk": (_i, [_vp, _vp, _vp] + [_i] * 6 + [_vp]),
+    "sgsa_indexer_topk_scores": (_i, [_vp] * 4 + [_i] * 6 + [_vp]),
     "sgsa_topk_select": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 6 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_indexer_thresholds": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),
@@ -45,7 +48,7 @@ SIGNATURES = {
     "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
     "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),
     "sgsa_decode_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
-    "sgsa_layer_fwd_workspace_size": (_sz, [_i] * 6),
+    "sgsa_layer_fwd_workspace_size": (_sz, [_i] * 8),
     "sgsa_layer_fwd": (_i, [_vp] * 12 + [_i] * 9 + [_vp, _sz, _vp]),
 }
 
@@ -73,8 +76,27 @@ def load():
     return _lib
 
 
-def check(status: int, what: str) -> None:
+# SGSA_WATCHDOG_CHECK=1: after every op, synchronise its stream and raise if a
+# bounded wait inside a tensor-core kernel gave up (its results are then invalid).
+# Off by default: the check costs a stream synchronisation per op.
+WATCHDOG_CHECK = os.environ.get("SGSA_WATCHDOG_CHECK", "0") == "1"
+
+
+def check_watchdog(stream: int, what: str) -> None:
+    """Raise SGSAError if the device watchdog recorded a wait that gave up."""
+    w = load().sgsa_watchdog_status(stream)
+    if w != 0:
+        raise SGSAError(f"{what}: device watchdog 0x{w & 0xffffffff:x} (a bounded wait inside a "
+                        "kernel gave up; its outputs are invalid)")
+
+
+def check(status: int, what: str, tensor=None) -> None:
+    """Raise on a non-OK status (ValueError for argument errors, SGSAError for device
+    errors); with SGSA_WATCHDOG_CHECK=1 also check the watchdog of `tensor`'s stream."""
     if status == SGSA_OK:
+        if WATCHDOG_CHECK and tensor is not None:
+            import torch
+            check_watchdog(torch.cuda.current_stream(tensor.device).cuda_stream, what)
         return
     lib = load()
     msg = lib.sgsa_status_string(status).decode()

@@ -4,9 +4,19 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}  // namespace
+
+cudaError_t sgsa::launched() {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return cudaGetLastError();
+}
 
 namespace {
 
@@ -31,16 +41,32 @@ bool head_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
 bool dtype_ok(int dt) { return dt == SGSA_DTYPE_F32 || dt == SGSA_DTYPE_BF16; }
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// One non-blocking side stream per device for the layer's concurrent delta stage.
-cudaStream_t side_stream() {
-    static std::mutex mu;
-    static cudaStream_t streams[64] = {};
+// The layer's concurrent delta stage runs on a non-blocking side stream with a
+// fork and a join event.  They are created once per (host thread, device) and
+// reused, so callers on different host threads never share them and a call
+// creates or destroys nothing after the first on its thread.
+struct SideStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    bool ok = false;
+};
+
+SideStream *side_stream() {
+    thread_local SideStream per_dev[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess)
-        streams[dev] = nullptr;
-    return streams[dev];
+    SideStream &s = per_dev[dev];
+    if (!s.ok) {
+        if (!s.stream && cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess)
+            s.stream = nullptr;
+        if (!s.fork && cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess)
+            s.fork = nullptr;
+        if (!s.join && cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess)
+            s.join = nullptr;
+        s.ok = s.stream && s.fork && s.join;
+        if (!s.ok) cudaGetLastError();
+    }
+    return s.ok ? &s : nullptr;
 }
 
 // SGSA_ATTN_GATHER=1 makes the layer use the row-gather attention (A/B checks).
@@ -71,12 +97,23 @@ const char *sgsa_last_error(void) { return g_last_error; }
 
 int sgsa_version(void) { return 1000; }
 
+unsigned long long sgsa_kernel_launches(void) {
+    return g_launches.load(std::memory_order_relaxed);
+}
+
 int sgsa_watchdog_status(void *stream) {
     const cudaStream_t st = (cudaStream_t)stream;
     const unsigned int a = sgsa::read_index_watchdog(st), b = sgsa::read_scan_watchdog(st),
                        c = sgsa::read_attn_watchdog(st);
     if (a == 0xffffffffu || b == 0xffffffffu || c == 0xffffffffu) return -1;
     return (int)(a | (b << 8) | (c << 16));
+}
+
+int sgsa_watchdog_selftest(unsigned int spin_limit, void *stream) {
+    if (spin_limit == 0 || spin_limit > (1u << 20)) return SGSA_ERR_SHAPE;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_watchdog_selftest(spin_limit, (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
 size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags) {
@@ -130,6 +167,18 @@ int sgsa_indexer_topk(const void *iq, const void *ik, int32_t *indices, int B, i
     if (int s = check_device()) return s;
     cudaError_t e = sgsa::launch_indexer_topk(iq, ik, indices, B, T, H, DI, top_k, dtype,
                                               (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
+int sgsa_indexer_topk_scores(const void *iq, const void *ik, int32_t *indices, float *scores,
+                             int B, int T, int H, int DI, int top_k, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || top_k <= 0 || T > 4096) return SGSA_ERR_SHAPE;
+    if (!sgsa::indexer_tc_eligible(DI, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!iq || !ik || !indices || !scores) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_indexer_topk_debug(iq, ik, indices, scores, B, T, H, DI, top_k,
+                                                    (cudaStream_t)stream);
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
@@ -219,16 +268,47 @@ int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void 
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
-size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int top_k) {
+}  // extern "C"
+
+namespace {
+
+// Workspace carving of sgsa_layer_fwd.  The fused path (tensor-core indexer and
+// attention) keeps 16-byte threshold records per row and never an index buffer;
+// the gather path keeps the B*idx_heads*T*K int32 index rows.
+struct LayerPlan {
+    bool fused;
+    size_t chunk, od, idx, thr, qkmax, os, total;
+};
+
+bool layer_fused(int T, int D, int DI, int dtype) {
+    return sgsa::indexer_tc_eligible(DI, dtype) && sgsa::sparse_attn_tc_eligible(T, D, DI, dtype) &&
+           fused_attn_enabled();
+}
+
+LayerPlan layer_plan(int B, int T, int H, int D, int DI, int idx_heads, int top_k, int dtype) {
+    LayerPlan p{};
+    p.fused = layer_fused(T, D, DI, dtype);
+    const size_t bthd = (size_t)B * T * H * D;
+    p.chunk = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
+    p.od = align256(bthd * sizeof(float));
+    p.idx = p.fused ? 0 : align256((size_t)B * idx_heads * T * top_k * sizeof(int32_t));
+    p.thr = p.fused ? align256((size_t)B * idx_heads * T * 16) : 0;
+    p.qkmax = p.fused ? align256((size_t)B * H * 2 * sizeof(uint32_t)) : 0;
+    p.os = p.fused ? align256(bthd * sizeof(float)) : 0;
+    p.total = p.chunk + p.od + p.idx + p.thr + p.qkmax + p.os;
+    return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int idx_heads,
+                                     int top_k, int dtype) {
     if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D) || top_k <= 0) return 0;
-    (void)DI;
-    size_t n = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
-    n += align256((size_t)B * T * H * D * sizeof(float));       // o_delta
-    n += align256((size_t)B * H * T * top_k * sizeof(int32_t));  // indices
-    n += align256((size_t)B * H * T * 16);                       // per-row selection thresholds
-    n += align256((size_t)B * H * 2 * sizeof(uint32_t));         // max |q|^2, |k|^2 per head
-    n += align256((size_t)B * T * H * D * sizeof(float));       // o_s (attention before the gate)
-    return n;
+    if (idx_heads != 1 && idx_heads != H) return 0;
+    if ((DI != 32 && DI != 64 && DI != 128) || !dtype_ok(dtype)) return 0;
+    return layer_plan(B, T, H, D, DI, idx_heads, top_k, dtype).total;
 }
 
 int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta,
@@ -243,45 +323,36 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
     if (!q || !k || !v || !beta || !gamma || !iq || !ik || !mix || !out) return SGSA_ERR_NULL;
     if (int s = check_device()) return s;
-    const size_t need = sgsa_layer_fwd_workspace_size(B, T, H, D, DI, top_k);
-    if (!workspace || workspace_bytes < need || ((uintptr_t)workspace & 255)) return SGSA_ERR_WORKSPACE;
+    const LayerPlan p = layer_plan(B, T, H, D, DI, idx_heads, top_k, dtype);
+    if (!workspace || workspace_bytes < p.total || ((uintptr_t)workspace & 255))
+        return SGSA_ERR_WORKSPACE;
     cudaStream_t st = (cudaStream_t)stream;
     char *w = (char *)workspace;
-    const size_t cws = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
-    float *od = (float *)(w + cws);
-    int32_t *ix = (int32_t *)(w + cws + align256((size_t)B * T * H * D * sizeof(float)));
-    uint32_t *thr = (uint32_t *)((char *)ix + align256((size_t)B * H * T * top_k * sizeof(int32_t)));
-    uint32_t *qkmax = (uint32_t *)((char *)thr + align256((size_t)B * H * T * 16));
-    float *os_ws = (float *)((char *)qkmax + align256((size_t)B * H * 2 * sizeof(uint32_t)));
-    const bool fused = sgsa::indexer_tc_eligible(DI, dtype) &&
-                       sgsa::sparse_attn_tc_eligible(T, D, DI, dtype) && fused_attn_enabled();
+    float *od = (float *)(w + p.chunk);
+    int32_t *ix = (int32_t *)(w + p.chunk + p.od);
+    uint32_t *thr = (uint32_t *)((char *)ix + p.idx);
+    uint32_t *qkmax = (uint32_t *)((char *)thr + p.thr);
+    float *os_ws = (float *)((char *)qkmax + p.qkmax);
     if (indices) ix = indices;
     int flags = SGSA_FLAG_OUT_F32 | (initial_state ? SGSA_FLAG_HAS_INIT : 0) |
                 (final_state ? SGSA_FLAG_STORE_FINAL : 0);
     const float scale = 1.0f / sqrtf((float)D);
     cudaError_t e;
-    if (fused) {
+    if (p.fused) {
         // The delta stage runs on a side stream beside the indexer and the attention
         // (neither reads its output); the attention writes o_s in fp32 and the gate,
         // which needs the delta output, joins the two streams.
-        cudaStream_t side = side_stream();
-        cudaEvent_t fork = nullptr, join = nullptr;
-        if (!side || cudaEventCreateWithFlags(&fork, cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&join, cudaEventDisableTiming) != cudaSuccess) {
-            if (fork) cudaEventDestroy(fork);
-            side = st;  // run in order on the caller's stream
-        }
+        SideStream *ss = side_stream();
+        cudaStream_t side = ss ? ss->stream : st;  // without one: in order on the caller's stream
         if (side != st) {
-            cudaEventRecord(fork, st);
-            cudaStreamWaitEvent(side, fork, 0);
+            if ((e = cudaEventRecord(ss->fork, st)) != cudaSuccess) return fail_cuda(e);
+            if ((e = cudaStreamWaitEvent(side, ss->fork, 0)) != cudaSuccess) return fail_cuda(e);
         }
         e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
                                      initial_state, od, final_state, B, T, H, D, dtype, flags, w,
                                      side);
-        if (side != st) {
-            cudaEventRecord(join, side);
-            cudaEventDestroy(fork);
-        }
+        cudaError_t ej = cudaSuccess;
+        if (side != st) ej = cudaEventRecord(ss->join, side);
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
             e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, idx_heads, DI, top_k,
                                               nullptr, 0, st);
@@ -289,11 +360,10 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
             e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, nullptr, nullptr, os_ws, B, T, H,
                                             scale, mix_per_channel, nullptr, 0, true, idx_heads,
                                             qkmax, st);
-        if (side != st) {
-            cudaStreamWaitEvent(st, join, 0);
-            cudaEventDestroy(join);
-        }
+        // always join, so that the caller's stream never runs ahead of the side stream
+        if (side != st && ej == cudaSuccess) ej = cudaStreamWaitEvent(st, ss->join, 0);
         if (e != cudaSuccess) return fail_cuda(e);
+        if (ej != cudaSuccess) return fail_cuda(ej);
         e = sgsa::launch_gate_mix(os_ws, od, mix, out, (long long)B * T * H, D, mix_per_channel,
                                   dtype, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);

@@ -313,10 +313,10 @@ cudaError_t run(const ChunkArgs &a, cudaStream_t st) {
     e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Dm::scan_smem);
     if (e != cudaSuccess) return e;
     prep<<<dim3(a.NC, a.B * a.H), kThreads, Dm::prep_smem, st>>>(a);
-    e = cudaGetLastError();
+    e = launched();
     if (e != cudaSuccess) return e;
     scan<<<dim3(D / kBV, a.B * a.H), kThreads, Dm::scan_smem, st>>>(a);
-    return cudaGetLastError();
+    return launched();
 }
 
 // ---- tensor-core scan (bf16 inputs, D = 128, no sparse write) ---------------
@@ -878,11 +878,11 @@ cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     if (!reuse_prep) {
         prep<<<dim3((a.NC + 1) / 2, a.B * a.H), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
-        e = cudaGetLastError();
+        e = launched();
         if (e != cudaSuccess) return e;
     }
     scan<<<a.B * a.H, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
-    return cudaGetLastError();
+    return launched();
 }
 
 template <typename Tin, typename Tout, bool SPARSE>

@@ -15,6 +15,13 @@
 // race on it and must be serialised by the caller.  Nothing in the array
 // needs to start at zero: every scratch word the kernels read is written
 // earlier in the same call, so what a previous call left behind is never seen.
+// That is why SGSA_FLAG_REUSE_PREP is refused here: it would make the scan read
+// per-chunk operands that some earlier call -- possibly another caller's
+// problem -- left in the shared array.
+// The device address is cached per device number for the life of the process;
+// a cudaDeviceReset (or anything else that tears down the primary context and
+// reloads the module) invalidates it, so this entry point must not be used
+// after such a reset.
 #include <mutex>
 #include <stdio.h>
 
@@ -42,6 +49,7 @@ extern "C" int sgsa_chunk_fwd_noalloc(const void *q, const void *k, const void *
         return sgsa_chunk_fwd(q, k, v, beta, gamma, sparse_k, sparse_v, alpha, initial_state, o,
                               final_state, B, T, H, D, dtype, chunk_size, flags, nullptr, 0,
                               stream);
+    if (flags & SGSA_FLAG_REUSE_PREP) return SGSA_ERR_UNSUPPORTED;
     const size_t need = sgsa_chunk_fwd_workspace_size(B, T, H, D, flags);
     if (need == 0) return SGSA_ERR_SHAPE;
     if (need > kNoAllocScratchBytes) return SGSA_ERR_WORKSPACE;

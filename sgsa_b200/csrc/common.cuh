@@ -25,44 +25,11 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
-bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype);
-cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, const void *iq,
-                                  const void *ik, const uint32_t *thr, const float *od,
-                                  const void *mix, void *out, int B, int T, int H, float scale,
-                                  int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  int HI, uint32_t *qkmax, cudaStream_t st);
-cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
-                                   void *khat, void *vhat, int B, int T, int H, int D, int K,
-                                   float scale, int HI, int dtype, cudaStream_t st);
-cudaError_t launch_rmsnorm(const void *x, const void *w, void *out, long long rows, int N,
-                           float eps, int dtype, cudaStream_t st);
-cudaError_t launch_swiglu(const void *gu, void *out, long long rows, int I, int dtype,
-                          cudaStream_t st);
-cudaError_t launch_rope_qkv(const void *qkv, const float *cs, void *q, void *k, void *v, int B,
-                            int T, int H, int D, int pos0, int dtype, cudaStream_t st);
-cudaError_t launch_sgsa_proj(const void *P, int ld, void *q, void *k, void *v, void *mix,
-                             void *iq, void *ik, void *beta, void *gamma, long long rows, int H,
-                             int D, int DI, int dtype, cudaStream_t st);
-cudaError_t launch_embed(const int64_t *ids, const void *table, void *out, long long rows, int N,
-                         int vocab, int dtype, cudaStream_t st);
-cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, void *out,
-                            long long rows, int D, int mix_pc, int dtype, cudaStream_t st);
-unsigned int read_attn_watchdog(cudaStream_t st);
-int decode_max_cache();
-cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const void *beta,
-                             const void *gamma, const void *sk, const void *sv, const void *alpha,
-                             const float *s0, void *o, float *sT, int B, int T, int H, int D,
-                             int dtype, bool out_f32, cudaStream_t st);
-cudaError_t launch_decode_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H,
-                               int Tc, int n, int DI, int K, int dtype, cudaStream_t st);
-cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, const int32_t *idx,
-                               const float *od, const void *mix, void *out, int B, int H, int Tc,
-                               int D, int K, float scale, int mix_pc, int dtype, cudaStream_t st);
-unsigned int read_scan_watchdog(cudaStream_t st);
-}  // namespace sgsa
+// Counts one kernel launch of this library (sgsa_kernel_launches) and returns
+// cudaGetLastError(); every launch site calls it right after its <<<...>>>.
+cudaError_t launched();
 
 // Launch wrappers implemented in the .cu files (all return cudaError_t of the launch).
-namespace sgsa {
 cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, const void *beta,
                                const void *gamma, const void *sk, const void *sv,
                                const void *alpha, const float *s0, void *o, float *sT, int B,
@@ -74,6 +41,10 @@ bool chunk_tc_eligible(int D, int dtype, int flags);
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T,
                                 int H, int DI, int K, int dtype, cudaStream_t st);
 unsigned int read_index_watchdog(cudaStream_t st);
+cudaError_t launch_watchdog_selftest(uint32_t limit, cudaStream_t st);
+cudaError_t launch_indexer_topk_debug(const void *iq, const void *ik, int32_t *idx,
+                                     float *scores, int B, int T, int H, int DI, int K,
+                                     cudaStream_t st);
 // Tensor-core indexer that also writes, per query row, the exact selection as a
 // threshold {prefix, mask, cut, 1}: column j <= t is selected iff
 // (key(s_tj) & mask) > prefix, or == prefix and j <= cut.  idx may be NULL.
@@ -109,5 +80,16 @@ cudaError_t launch_decode_topk(const void *iq, const void *ikc, int32_t *idx, in
 cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, const int32_t *idx,
                                const float *od, const void *mix, void *out, int B, int H, int Tc,
                                int D, int K, float scale, int mix_pc, int dtype, cudaStream_t st);
+cudaError_t launch_rmsnorm(const void *x, const void *w, void *out, long long rows, int N,
+                           float eps, int dtype, cudaStream_t st);
+cudaError_t launch_swiglu(const void *gu, void *out, long long rows, int I, int dtype,
+                          cudaStream_t st);
+cudaError_t launch_rope_qkv(const void *qkv, const float *cs, void *q, void *k, void *v, int B,
+                            int T, int H, int D, int pos0, int dtype, cudaStream_t st);
+cudaError_t launch_sgsa_proj(const void *P, int ld, void *q, void *k, void *v, void *mix,
+                             void *iq, void *ik, void *beta, void *gamma, long long rows, int H,
+                             int D, int DI, int dtype, cudaStream_t st);
+cudaError_t launch_embed(const int64_t *ids, const void *table, void *out, long long rows, int N,
+                         int vocab, int dtype, cudaStream_t st);
 unsigned int read_scan_watchdog(cudaStream_t st);
 }  // namespace sgsa

@@ -226,7 +226,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(
     // warp run the same number of iterations (the shuffles need the whole warp)
     for (int base = 2 * warp; base < K; base += 2 * kAttnWarps) {
         const int s = base + half;
-        const int j = (s < K) ? ix[s] : -1;
+        int j = (s < K) ? ix[s] : -1;
+        if ((unsigned)j >= (unsigned)Tc) j = -1;  // out-of-range rows count as padding
         float d0 = 0.f;
         float kr[EPL], vr[EPL];
         if (j >= 0) {
@@ -293,7 +294,7 @@ cudaError_t run_rec(const void *q, const void *k, const void *v, const void *bet
     recurrent_sgsa_kernel<Tin, Tout, D><<<B * H, D, 0, st>>>(
         (const Tin *)q, (const Tin *)k, (const Tin *)v, (const Tin *)beta, (const Tin *)gamma,
         (const Tin *)sk, (const Tin *)sv, (const Tin *)alpha, s0, (Tout *)o, sT, T, H);
-    return cudaGetLastError();
+    return launched();
 }
 
 template <typename Tin, typename Tout>
@@ -318,7 +319,7 @@ cudaError_t run_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H
                                          (int)smem);
     if (e != cudaSuccess) return e;
     kern<<<B * H, kTopkThreads, smem, st>>>((const Tin *)iq, (const Tin *)ikc, idx, H, Tc, n, K);
-    return cudaGetLastError();
+    return launched();
 }
 
 template <typename T, int D>
@@ -328,7 +329,7 @@ cudaError_t run_dattn(const void *q, const void *kc, const void *vc, const int32
     decode_attn_kernel<T, D><<<B * H, kAttnWarps * 32, 0, st>>>(
         (const T *)q, (const T *)kc, (const T *)vc, idx, od, (const T *)mix, (T *)out, H, Tc, K,
         scale * 1.4426950408889634f, mix_pc);
-    return cudaGetLastError();
+    return launched();
 }
 
 }  // namespace

@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(TcCfg<DI, PACKED>::kThreads, (TcCfg<DI, PACKED
 indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx,
                        uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt,
-                       const int32_t *__restrict__ q_tiles) {
+                       const int32_t *__restrict__ q_tiles, float *__restrict__ dbg_scores) {
     using C = TcCfg<DI, PACKED>;
     using namespace sm100;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -628,6 +628,13 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         float v[32];
                         tmem_ld32(taddr + c * 32, v);
                         const int jb = kt * C::kN + c * 32;
+                        if (dbg_scores && pass == 0 && has_row) {
+                            // test support: the fp32 scores this pass selects from
+                            float *dr = dbg_scores + ((size_t)bh * T + t) * T;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (jb + i < nvalid) dr[jb + i] = v[i];
+                        }
                         if (pass == 0 && kt == 0) {
                             // sample of the first key tile: place every row's fast window
                             uint32_t amax = 0u;
@@ -753,7 +760,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
 
 template <int DI, bool PACKED>
 cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T, int H,
-                   int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st) {
+                   int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st,
+                   float *dbg_scores = nullptr) {
     using C = TcCfg<DI, PACKED>;
     CUtensorMap mq, mk;
     if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
@@ -766,8 +774,9 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int
     const int nqt = ceil_div(T, kRows);
     const int ntiles = q_tiles ? n_tiles : nqt;
     if (ntiles <= 0) return cudaSuccess;
-    kern<<<ntiles * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, thr, B, T, H, K, nqt, q_tiles);
-    return cudaGetLastError();
+    kern<<<ntiles * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, thr, B, T, H, K, nqt, q_tiles,
+                                                      dbg_scores);
+    return launched();
 }
 
 template <int DI>
@@ -788,7 +797,7 @@ cudaError_t run_simt(const void *iq, const void *ik, int32_t *idx, int B, int T,
     if (e != cudaSuccess) return e;
     const int nqt = ceil_div(T, kRows);
     kern<<<dim3(nqt, B * H), kRows, smem, st>>>((const Tin *)iq, (const Tin *)ik, idx, B, T, H, K, nqt);
-    return cudaGetLastError();
+    return launched();
 }
 
 template <typename Tin>
@@ -834,6 +843,34 @@ unsigned int read_index_watchdog(cudaStream_t st) {
     return v;
 }
 
+// Watchdog self-test: one thread waits, with a short spin limit, on an mbarrier that
+// nothing ever arrives at.  The wait gives up, records `code` in the indexer's
+// watchdog word and the kernel returns -- the path a stalled pipeline takes.
+namespace {
+__global__ void watchdog_selftest_kernel(uint32_t limit, unsigned int code) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bar, 1);
+        sm100::fence_barrier_init();
+        sm100::mbar_wait(&bar, 0, &g_index_watchdog, code, limit);
+    }
+}
+}  // namespace
+
+cudaError_t launch_watchdog_selftest(uint32_t limit, cudaStream_t st) {
+    watchdog_selftest_kernel<<<1, 32, 0, st>>>(limit, 0x80u);
+    return launched();
+}
+
+cudaError_t launch_indexer_topk_debug(const void *iq, const void *ik, int32_t *idx,
+                                     float *scores, int B, int T, int H, int DI, int K,
+                                     cudaStream_t st) {
+    if (T >= 65536) return cudaErrorInvalidValue;
+    if (DI == 64) return run_tc<64, true>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st, scores);
+    if (DI == 128) return run_tc<128, true>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st, scores);
+    return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,
                                int S, int K, cudaStream_t st) {
     const size_t smem = 256 * kRows * sizeof(uint32_t);
@@ -841,7 +878,7 @@ cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     topk_select_kernel<<<ceil_div(R, kRows), kRows, smem, st>>>(scores, valid, idx, R, S, K);
-    return cudaGetLastError();
+    return launched();
 }
 
 }  // namespace sgsa

@@ -226,7 +226,7 @@ cudaError_t launch_rmsnorm(const void *x, const void *w, void *out, long long ro
     else
         rmsnorm_kernel<__nv_bfloat16><<<grid, kRowWarps * 32, 0, st>>>(
             (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)w, (__nv_bfloat16 *)out, rows, N, eps);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_swiglu(const void *gu, void *out, long long rows, int I, int dtype,
@@ -237,7 +237,7 @@ cudaError_t launch_swiglu(const void *gu, void *out, long long rows, int I, int 
     else
         swiglu_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16 *)gu,
                                                            (__nv_bfloat16 *)out, rows, I);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_rope_qkv(const void *qkv, const float *cs, void *q, void *k, void *v, int B,
@@ -252,7 +252,7 @@ cudaError_t launch_rope_qkv(const void *qkv, const float *cs, void *q, void *k, 
         rope_qkv_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
             (const __nv_bfloat16 *)qkv, (const float2 *)cs, (__nv_bfloat16 *)q,
             (__nv_bfloat16 *)k, (__nv_bfloat16 *)v, rows, T, H, D, pos0);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_sgsa_proj(const void *P, int ld, void *q, void *k, void *v, void *mix,
@@ -268,7 +268,7 @@ cudaError_t launch_sgsa_proj(const void *P, int ld, void *q, void *k, void *v, v
             (const __nv_bfloat16 *)P, ld, (__nv_bfloat16 *)q, (__nv_bfloat16 *)k,
             (__nv_bfloat16 *)v, (__nv_bfloat16 *)mix, (__nv_bfloat16 *)iq, (__nv_bfloat16 *)ik,
             (__nv_bfloat16 *)beta, (__nv_bfloat16 *)gamma, H, D, DI);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_embed(const int64_t *ids, const void *table, void *out, long long rows, int N,
@@ -280,7 +280,7 @@ cudaError_t launch_embed(const int64_t *ids, const void *table, void *out, long 
     else
         embed_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
             ids, (const __nv_bfloat16 *)table, (__nv_bfloat16 *)out, rows, N, vocab);
-    return cudaGetLastError();
+    return launched();
 }
 
 }  // namespace sgsa

@@ -83,8 +83,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
 // Bounded wait on the given phase parity; returns false (and sets *watchdog)
 // when the spin limit is reached.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, unsigned int *watchdog,
-                                          unsigned int code) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+                                          unsigned int code, uint32_t limit = kSpinLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, phase)) return true;
         if ((i & 1023u) == 1023u && watchdog && *(volatile unsigned int *)watchdog) return false;
     }

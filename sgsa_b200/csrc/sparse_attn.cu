@@ -147,7 +147,8 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
             for (int u = 0; u < kU; ++u) {
                 const int slot = p + 2 * u + half;
                 jr[u] = __shfl_sync(0xffffffffu, my, slot & 31);
-                if (slot >= cnt) jr[u] = -1;
+                // out-of-range rows (caller-supplied indices) count as padding
+                if (slot >= cnt || (unsigned)jr[u] >= (unsigned)T_) jr[u] = -1;
                 if (jr[u] >= 0) {
                     kr[u].load(kb + (size_t)jr[u] * kvstride);
                     vr[u].load(vb + (size_t)jr[u] * kvstride);
@@ -237,7 +238,7 @@ cudaError_t run(const void *q, const void *k, const void *v, const int32_t *idx,
     sparse_attn_mix_kernel<T, D><<<grid, kWarps * 32, 0, st>>>(
         (const T *)q, (const T *)k, (const T *)v, idx, od, (const T *)mix, (T *)out, B, T_, H, K,
         scale * 1.4426950408889634f, mix_pc, HI);
-    return cudaGetLastError();
+    return launched();
 }
 
 template <typename T>
@@ -286,7 +287,7 @@ cudaError_t run_retrieve(const void *q, const void *k, const void *v, const int3
     sparse_attn_mix_kernel<T, D, true><<<grid, kWarps * 32, 0, st>>>(
         (const T *)q, (const T *)k, (const T *)v, idx, nullptr, nullptr, (T *)vhat, B, T_, H, K,
         scale * 1.4426950408889634f, 0, HI, (T *)khat);
-    return cudaGetLastError();
+    return launched();
 }
 }  // namespace
 
@@ -314,7 +315,7 @@ cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, v
     else
         gate_mix_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(os, od, (const __nv_bfloat16 *)mix,
                                                              (__nv_bfloat16 *)out, n, D, mix_pc);
-    return cudaGetLastError();
+    return launched();
 }
 
 }  // namespace sgsa

@@ -507,7 +507,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         if (e != cudaSuccess) return e;
         qk_norm_max_kernel<<<dim3(ceil_div(T, kNormRows), B * H), 256, 0, st>>>(
             (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, qkmax, T, H);
-        e = cudaGetLastError();
+        e = launched();
         if (e != cudaSuccess) return e;
     }
     if (out_f32) {
@@ -527,7 +527,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
             mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
             (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
     }
-    return cudaGetLastError();
+    return launched();
 }
 
 unsigned int read_attn_watchdog(cudaStream_t st) {

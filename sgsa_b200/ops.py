@@ -55,6 +55,27 @@ def _workspace(nbytes: int, device) -> Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
+_layer_ws = {}
+
+
+def _layer_workspace(nbytes: int, device) -> Tensor:
+    """The layer's workspace, kept across calls per (device, stream) and grown when a
+    call needs more.  Calls on one stream are ordered, so reusing it is safe; calls
+    on another stream get their own."""
+    dev = torch.device(device)
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    ws = _layer_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        _layer_ws.pop(key, None)
+        ws = _layer_ws[key] = _workspace(nbytes, dev)
+    return ws
+
+
+def release_workspaces() -> None:
+    """Drop the cached layer workspaces (their memory returns to torch's allocator)."""
+    _layer_ws.clear()
+
+
 def chunk_sgsa(
     q: Tensor,
     k: Tensor,
@@ -119,7 +140,7 @@ def chunk_sgsa(
     st = lib.sgsa_chunk_fwd(_ptr(q_), _ptr(k_), _ptr(v_), _ptr(beta_), _ptr(gamma_), _ptr(sk_),
                             _ptr(sv_), _ptr(al_), _ptr(s0), _ptr(o), _ptr(sT), B, T, H, D, dt, 64,
                             flags, _ptr(ws), ws.numel(), _stream(q))
-    _lib.check(st, "sgsa_chunk_fwd")
+    _lib.check(st, "sgsa_chunk_fwd", q)
     if sT is not None:
         sT = sT.to(q.dtype)
     return o, sT
@@ -149,7 +170,7 @@ def chunk_sgsa_fp32_state(q, k, v, beta, gamma, initial_state=None, sparse_k=Non
     st = lib.sgsa_chunk_fwd(*[_ptr(t) for t in args], *[_ptr(t) for t in sp], _ptr(s0), _ptr(o),
                             _ptr(sT), B, T, H, D, dt, 64, flags, _ptr(ws), ws.numel(),
                             _stream(q))
-    _lib.check(st, "sgsa_chunk_fwd")
+    _lib.check(st, "sgsa_chunk_fwd", q)
     return o, sT
 
 
@@ -171,7 +192,7 @@ def indexer_topk(iq: Tensor, ik: Tensor, top_k: int) -> Tensor:
     out = torch.empty(B, H, T, top_k, device=iq.device, dtype=torch.int32)
     st = _lib.load().sgsa_indexer_topk(_ptr(iq_), _ptr(ik_), _ptr(out), B, T, H, DI, top_k, dt,
                                         _stream(iq))
-    _lib.check(st, "sgsa_indexer_topk")
+    _lib.check(st, "sgsa_indexer_topk", iq)
     return out
 
 
@@ -188,7 +209,7 @@ def topk_select(scores: Tensor, valid: Tensor, top_k: int) -> Tensor:
     out = torch.empty(R, top_k, device=scores.device, dtype=torch.int32)
     st = _lib.load().sgsa_topk_select(_ptr(sc), _ptr(val), _ptr(out), R, S, top_k,
                                        _stream(scores))
-    _lib.check(st, "sgsa_topk_select")
+    _lib.check(st, "sgsa_topk_select", scores)
     return out
 
 
@@ -221,7 +242,7 @@ def sparse_attn_mix(q: Tensor, k: Tensor, v: Tensor, indices: Tensor,
     st = _lib.load().sgsa_sparse_attn_mix(_ptr(q_), _ptr(k_), _ptr(v_), _ptr(ix), _ptr(od),
                                            _ptr(mx), _ptr(out), B, T, H, D, K, idx_heads, sc,
                                            per_channel, dt, _stream(q))
-    _lib.check(st, "sgsa_sparse_attn_mix")
+    _lib.check(st, "sgsa_sparse_attn_mix", q)
     return out
 
 
@@ -252,11 +273,12 @@ def sgsa_layer_fwd(q: Tensor, k: Tensor, v: Tensor, beta: Tensor, gamma: Tensor,
     ix = torch.empty(B, idx_heads, T, top_k, device=q.device, dtype=torch.int32) \
         if return_indices else None
     lib = _lib.load()
-    ws = _workspace(lib.sgsa_layer_fwd_workspace_size(B, T, H, D, DI, top_k), q.device)
+    ws = _layer_workspace(lib.sgsa_layer_fwd_workspace_size(B, T, H, D, DI, idx_heads, top_k, dt),
+                          q.device)
     st = lib.sgsa_layer_fwd(*[_ptr(t) for t in args], _ptr(s0), _ptr(out), _ptr(sT), _ptr(ix),
                             B, T, H, D, DI, idx_heads, top_k, per_channel, dt, _ptr(ws),
                             ws.numel(), _stream(q))
-    _lib.check(st, "sgsa_layer_fwd")
+    _lib.check(st, "sgsa_layer_fwd", q)
     res = [out]
     if output_final_state:
         res.append(sT)
@@ -280,7 +302,7 @@ def indexer_thresholds(iq: Tensor, ik: Tensor, top_k: int, return_indices: bool 
     nt = 0 if qt is None else qt.numel()
     st = _lib.load().sgsa_indexer_thresholds(_ptr(iq_), _ptr(ik_), _ptr(ix), _ptr(thr), _ptr(qt),
                                               nt, B, T, H, DI, top_k, _stream(iq))
-    _lib.check(st, "sgsa_indexer_thresholds")
+    _lib.check(st, "sgsa_indexer_thresholds", iq)
     return (thr, ix) if return_indices else thr
 
 
@@ -305,7 +327,7 @@ def sparse_attn_thresholds(q, k, v, iq, ik, thresholds, o_delta=None, mix=None, 
         _ptr(q), _ptr(k), _ptr(v), _ptr(iq), _ptr(ik), _ptr(thresholds), _ptr(qt), nt, _ptr(od),
         _ptr(mx), _ptr(out), B, T, H, D, DI, iq.shape[2], sc, per_channel,
         int(out.dtype == torch.float32), _ptr(norms), _stream(q))
-    _lib.check(st, "sgsa_sparse_attn_thresholds")
+    _lib.check(st, "sgsa_sparse_attn_thresholds", q)
     return out
 
 
@@ -409,7 +431,7 @@ def fused_recurrent_sgsa(
     st = _lib.load().sgsa_recurrent_fwd(*[_ptr(t) for t in args], *[_ptr(t) for t in sp],
                                          _ptr(s0), _ptr(o), _ptr(sT), B, T, H, D, dt, flags,
                                          _stream(q))
-    _lib.check(st, "sgsa_recurrent_fwd")
+    _lib.check(st, "sgsa_recurrent_fwd", q)
     return o, sT
 
 
@@ -422,7 +444,7 @@ def decode_topk(iq: Tensor, ik_cache: Tensor, n: int, top_k: int) -> Tensor:
     out = torch.empty(B, H, top_k, device=iq.device, dtype=torch.int32)
     st = _lib.load().sgsa_decode_topk(_ptr(iq.contiguous()), _ptr(ik_cache), _ptr(out), B, H, Tc,
                                        int(n), DI, top_k, _dtype_code(iq), _stream(iq))
-    _lib.check(st, "sgsa_decode_topk")
+    _lib.check(st, "sgsa_decode_topk", iq)
     return out
 
 
@@ -442,7 +464,7 @@ def decode_attn_mix(q: Tensor, k_cache: Tensor, v_cache: Tensor, indices: Tensor
                                            _ptr(indices.to(torch.int32).contiguous()), _ptr(od),
                                            _ptr(mx), _ptr(out), B, H, Tc, D, K, sc, per_channel,
                                            _dtype_code(q), _stream(q))
-    _lib.check(st, "sgsa_decode_attn_mix")
+    _lib.check(st, "sgsa_decode_attn_mix", q)
     return out
 
 
@@ -493,7 +515,7 @@ def chunk_free_recurrent_step(q, k, v, beta, gamma, state):
                                          _ptr(cast(beta)), _ptr(cast(gamma)), None, None, None,
                                          _ptr(state), _ptr(o), _ptr(st), B, 1, H, D, dt, flags,
                                          _stream(q))
-    _lib.check(rc, "sgsa_recurrent_fwd")
+    _lib.check(rc, "sgsa_recurrent_fwd", q)
     return o, st
 
 
@@ -506,7 +528,7 @@ def gate_mix(o_s: Tensor, o_delta: Tensor, mix: Tensor, dtype=torch.bfloat16) ->
     per_channel = int(mx.numel() == o_s.numel())
     st = _lib.load().sgsa_gate_mix(_ptr(o_s.contiguous()), _ptr(o_delta.contiguous()), _ptr(mx),
                                     _ptr(out), rows, D, per_channel, _DT[dtype], _stream(o_s))
-    _lib.check(st, "sgsa_gate_mix")
+    _lib.check(st, "sgsa_gate_mix", o_s)
     return out
 
 
@@ -525,7 +547,7 @@ def sparse_retrieve(q: Tensor, k: Tensor, v: Tensor, indices: Tensor,
                                            _ptr(indices.to(torch.int32).contiguous()), _ptr(kh),
                                            _ptr(vh), B, T, H, D, K, indices.shape[1], sc,
                                            _dtype_code(q), _stream(q))
-    _lib.check(st, "sgsa_sparse_retrieve")
+    _lib.check(st, "sgsa_sparse_retrieve", q)
     return kh, vh
 
 

@@ -38,7 +38,7 @@ def test_host_only_entry_points(lib):
     n = lib.sgsa_chunk_fwd_workspace_size(4, 8192, 16, 128, 0)
     assert n == 4 * 16 * 128 * (4 * 64 * 128 + 64 * 64 + 64) * 4 + 256
     assert lib.sgsa_chunk_fwd_workspace_size(1, 64, 1, 96, 0) == 0  # unsupported head dim
-    assert lib.sgsa_layer_fwd_workspace_size(1, 1024, 4, 64, 32, 128) > 0
+    assert lib.sgsa_layer_fwd_workspace_size(1, 1024, 4, 64, 32, 4, 128, 0) > 0
 
 
 def test_bad_arguments_rejected_before_any_launch(lib):
@@ -60,3 +60,22 @@ def test_ops_refuse_cpu_tensors():
         sg.chunk_sgsa(x, x, x, g, g)
     with pytest.raises(ValueError, match="CUDA"):
         sg.indexer_topk(x, x, 4)
+
+
+def test_layer_workspace_follows_the_path(lib):
+    """The fused (tensor-core) path keeps per-row selection records, never an index
+    buffer; the gather path keeps B*idx_heads*T*K int32 rows."""
+    GB = 1 << 30
+    # configs[1]: B4 T8192 H16 d128, DI 64, k 512, bf16 -> fused
+    fused = lib.sgsa_layer_fwd_workspace_size(4, 8192, 16, 128, 64, 16, 512, 1)
+    chunk = lib.sgsa_chunk_fwd_workspace_size(4, 8192, 16, 128, 0)
+    fp32_rows = 4 * 8192 * 16 * 128 * 4
+    assert fused < chunk + 2 * fp32_rows + 4 * 16 * 8192 * 16 + 4096
+    # fp32 inputs take the gather path: the index rows are part of the workspace
+    gather = lib.sgsa_layer_fwd_workspace_size(4, 8192, 16, 128, 64, 16, 512, 0)
+    assert gather >= chunk + fp32_rows + 4 * 16 * 8192 * 512 * 4
+    # configs[2]: B1 T65536 H32 k 2048 -> no 17 GB index buffer
+    long_ctx = lib.sgsa_layer_fwd_workspace_size(1, 65536, 32, 128, 64, 32, 2048, 1)
+    assert long_ctx < 1 * 65536 * 32 * 2048 * 4
+    assert long_ctx < 8 * GB
+    assert lib.sgsa_layer_fwd_workspace_size(1, 1024, 4, 64, 32, 3, 128, 0) == 0  # bad idx_heads

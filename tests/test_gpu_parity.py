@@ -363,18 +363,26 @@ def test_sparse_retrieve_reference_fixture():
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_sparse_write_block_matches_oracle(dtype):
-    """Retrieval (q . k top-k), k_hat / v_hat, then the delta rule with the sparse write."""
+    """Retrieval (q . k top-k), k_hat / v_hat, then the delta rule with the sparse write.
+
+    The two halves are pinned separately at the plain tolerance: the retrieval
+    against the oracle's k_hat / v_hat, and the recurrence with the sparse write
+    against the oracle fed the device's own (dtype-rounded) k_hat / v_hat, so the
+    rounding of k_hat to the input dtype is not charged to the recurrence."""
     x = rand_case(2, 300, 2, 64, dtype, seed=21, sparse=True, init=True)
     K = 32
     d = dev(x)
     o, st = ops.sgsa_sparse_write_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["alpha"],
                                       K, initial_state=d["initial_state"],
                                       output_final_state=True)
+    idx_dev = ops.indexer_topk(d["q"], d["k"], K)
     idx, kth = oracle.indexer_topk(x["q"], x["k"], K, return_kth=True)
-    kh, vh = oracle.sparse_retrieve(x["k"], x["v"], idx, x["q"])
-    kh = torch.from_numpy(kh).to(dtype)
-    vh = torch.from_numpy(vh).to(dtype)
-    ro, rs = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], kh, vh,
-                                   x["alpha"], x["initial_state"])
-    assert oracle.rel_l2(o.float().cpu().numpy(), ro) < TOL[dtype] * (1 if dtype == torch.float32 else 2)
-    assert oracle.rel_l2(st.float().cpu().numpy(), rs) < TOL[dtype] * (1 if dtype == torch.float32 else 2)
+    check_index_sets(idx_dev.cpu().numpy(), idx, x["q"].float(), x["k"].float(), kth, 1e-5)
+    kh_dev, vh_dev = ops.sparse_retrieve(d["q"], d["k"], d["v"], idx_dev)
+    kh, vh = oracle.sparse_retrieve(x["k"], x["v"], idx_dev.cpu().numpy(), x["q"])
+    assert oracle.rel_l2(kh_dev.float().cpu().numpy(), kh) < TOL[dtype]
+    assert oracle.rel_l2(vh_dev.float().cpu().numpy(), vh) < TOL[dtype]
+    ro, rs = oracle.sgsa_recurrent(x["q"], x["k"], x["v"], x["beta"], x["gamma"], kh_dev.cpu(),
+                                   vh_dev.cpu(), x["alpha"], x["initial_state"])
+    assert oracle.rel_l2(o.float().cpu().numpy(), ro) < TOL[dtype]
+    assert oracle.rel_l2(st.float().cpu().numpy(), rs) < TOL[dtype]

@@ -84,3 +84,60 @@ def test_sp_emulated_matches_single_gpu(world):
     got, st = sp.sp_layer_fwd_emulated(*args, world=world, output_final_state=True)
     assert oracle.rel_l2(got.float().cpu().numpy(), ref.float().cpu().numpy()) < 2e-3
     assert oracle.rel_l2(st.cpu().numpy(), st_ref.cpu().numpy()) < 2e-3
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_exchange_plan_moves_every_tile_once(world):
+    """Simulate the two all-to-alls of the plan: every rank gets the query rows of
+    exactly its zigzag tiles, and every owner gets back the outputs of exactly its
+    own tiles, each once."""
+    n = 64 * world
+    plans = [sp.ExchangePlan(n, world, r) for r in range(world)]
+    for r, p in enumerate(plans):
+        assert sum(p.work_count) == len(p.work) == n // world
+        assert sum(p.own_count) == len(p.own) == n // world
+    # query exchange: owner o sends its `own` tiles, split by own_count, to ranks s
+    for r, p in enumerate(plans):
+        got = []
+        for o in range(world):
+            po = plans[o]
+            start = sum(po.own_count[:r])
+            got += po.own[start:start + po.own_count[r]]
+        assert got == p.work  # arrives grouped by owner, ascending = work order
+    # output exchange: rank s sends its `work` tiles, split by work_count, to owners
+    for r, p in enumerate(plans):
+        got = []
+        for s in range(world):
+            ps = plans[s]
+            start = sum(ps.work_count[:r])
+            got += ps.work[start:start + ps.work_count[r]]
+        assert got == p.own
+        assert sorted(got) == list(range(r * n // world, (r + 1) * n // world))
+
+
+def _a2a_main(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    n_tiles, B, H = 4 * world, 2, 3
+    T = n_tiles * sp.TILE
+    Tl = T // world
+    full = torch.arange(B * T * H, dtype=torch.float32).reshape(B, T, H, 1)
+    mine = full[:, rank * Tl:(rank + 1) * Tl].contiguous()
+    p = sp.ExchangePlan(n_tiles, world, rank)
+    work_rows, own_rows = p.rows(p.work, False), p.rows(p.own, True)
+    # queries: owners send, each rank receives its work tiles at their global rows
+    fq = torch.zeros(B, T, H, 1)
+    sp._all_to_all_rows(mine, own_rows, p.own_count, work_rows, p.work_count, fq, None)
+    ok = torch.equal(fq[:, work_rows], full[:, work_rows])
+    # outputs: each rank returns its work rows (of a full-size buffer) to their owners
+    back = torch.empty(B, Tl, H, 1)
+    sp._all_to_all_rows(fq, work_rows, p.work_count, own_rows, p.own_count, back, None)
+    result[rank] = ok and torch.equal(back, mine)
+    dist.destroy_process_group()
+
+
+def test_row_all_to_all_two_gloo_ranks():
+    world = 2
+    result = mp.Manager().dict()
+    mp.spawn(_a2a_main, args=(world, 29631, result), nprocs=world, join=True)
+    assert all(result[r] for r in range(world)), dict(result)

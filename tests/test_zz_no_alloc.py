@@ -69,6 +69,38 @@ def test_noalloc_matches_regular_entry_point_twice(dtype, tol):
         assert _rel(ns, rs) <= tol
 
 
+def test_noalloc_tensor_core_path_near_the_limit():
+    """bf16, D=128, no sparse write: the tensor-core chunk kernels, whose workspace
+    carries the 256-byte-aligned Qt / Kt tail, on a problem whose workspace is just
+    under the 64 MiB scratch."""
+    lib = _lib.load()
+    B, T, H, D = 1, 4096, 7, 128
+    flags = _lib.FLAG_HAS_INIT | _lib.FLAG_STORE_FINAL
+    need = lib.sgsa_chunk_fwd_workspace_size(B, T, H, D, flags)
+    assert (60 << 20) < need <= (64 << 20)
+    for seed in (2, 3):
+        x = _inputs(torch.bfloat16, B=B, T=T, H=H, D=D, seed=seed)
+        ro, rs = _call(lib, "regular", x, torch.bfloat16, flags)
+        no, ns = _call(lib, "noalloc", x, torch.bfloat16, flags)
+        assert _rel(no, ro) <= 2e-3
+        assert _rel(ns, rs) <= 2e-3
+
+
+def test_noalloc_refuses_prep_reuse():
+    """Reusing prep operands would read whatever an earlier call left in the shared
+    scratch, so the flag is refused before anything is launched."""
+    lib = _lib.load()
+    x = _inputs(torch.bfloat16, B=1, T=128, H=1, D=128)
+    p = [x[n].data_ptr() for n in ("q", "k", "v", "beta", "gamma", "sk", "sv", "alpha", "s0")]
+    o = torch.empty_like(x["q"])
+    sT = torch.empty(1, 1, 128, 128, device="cuda")
+    for extra in (_lib.FLAG_REUSE_PREP, _lib.FLAG_REUSE_PREP | _lib.FLAG_TRANSITION):
+        rc = lib.sgsa_chunk_fwd_noalloc(*p, o.data_ptr(), sT.data_ptr(), 1, 128, 1, 128,
+                                        _lib.DTYPE_BF16, 64, _lib.FLAG_STORE_FINAL | extra,
+                                        torch.cuda.current_stream().cuda_stream)
+        assert rc == -6  # SGSA_ERR_UNSUPPORTED
+
+
 def test_noalloc_rejects_problems_beyond_its_scratch():
     lib = _lib.load()
     # B*H*T large enough that the chunk workspace exceeds the 64 MiB scratch
