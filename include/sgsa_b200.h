@@ -143,6 +143,15 @@ int sgsa_indexer_topk_scores(const void *iq, const void *ik, int32_t *indices, f
                              int B, int T, int H, int DI, int top_k, void *stream);
 
 /*
+ * Test support: counters of the tensor-core indexer on the current device since
+ * the last reset -- rows that needed the refine pass, rows that restarted with
+ * the plain radix select, plain-radix candidate passes, rows whose k-th score
+ * was an exact tie (counts[0..3]).  Synchronises the device.  No reference
+ * counterpart.
+ */
+int sgsa_indexer_stats(unsigned long long *counts, int reset);
+
+/*
  * Row-wise top-k of a float32 score matrix [R, S] where row r considers
  * columns [0, valid[r]).  Same selection rule and output format as
  * sgsa_indexer_topk; it exists so that the select can be checked bit-exactly

@@ -33,6 +33,7 @@ SIGNATURES = {
     "sgsa_chunk_fwd_noalloc": (_i, [_vp] * 11 + [_i] * 7 + [_vp]),
     "sgsa_indexer_topk": (_i, [_vp, _vp, _vp] + [_i] * 6 + [_vp]),
     "sgsa_indexer_topk_scores": (_i, [_vp] * 4 + [_i] * 5 + [_vp]),
+    "sgsa_indexer_stats": (_i, [_vp, _i]),
     "sgsa_topk_select": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp]),
     "sgsa_sparse_attn_mix": (_i, [_vp] * 7 + [_i] * 6 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_indexer_thresholds": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),

@@ -182,6 +182,13 @@ int sgsa_indexer_topk_scores(const void *iq, const void *ik, int32_t *indices, f
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_indexer_stats(unsigned long long *counts, int reset) {
+    if (!counts) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    if (cudaDeviceSynchronize() != cudaSuccess) return SGSA_ERR_LAUNCH;
+    return sgsa::read_index_stats(counts, reset != 0) == 0 ? SGSA_OK : SGSA_ERR_LAUNCH;
+}
+
 int sgsa_topk_select(const float *scores, const int32_t *valid, int32_t *indices, int R, int S,
                      int top_k, void *stream) {
     if (R < 0 || S < 0 || top_k <= 0) return SGSA_ERR_SHAPE;

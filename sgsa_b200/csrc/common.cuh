@@ -42,6 +42,7 @@ cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, in
                                 int H, int DI, int K, int dtype, cudaStream_t st);
 unsigned int read_index_watchdog(cudaStream_t st);
 cudaError_t launch_watchdog_selftest(uint32_t limit, cudaStream_t st);
+int read_index_stats(unsigned long long *out, bool reset);
 cudaError_t launch_indexer_topk_debug(const void *iq, const void *ik, int32_t *idx,
                                      float *scores, int B, int T, int H, int DI, int K,
                                      cudaStream_t st);

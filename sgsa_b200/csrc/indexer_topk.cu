@@ -195,117 +195,88 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 //   warp 0  TMA producer: the query tile once, then key tiles into a ring of
 //           shared-memory stages;
 //   warp 1  TMEM owner and MMA issuer: S_tile = Q K^T, M=128 (queries) x
-//           N=kN (keys) x K=DI, into one of two TMEM accumulators;
+//           N=kN (keys) x K=DI, into one of four TMEM accumulators;
 //   warps 2-9  two threads per query row (warps w and w+4 read the same TMEM
 //           lane quarter and split the tile's columns): tcgen05.ld of their
-//           part of the row, radix histogram; the first thread of each row
-//           also runs the collect pass, which must walk the row in order.
+//           part of the row and the selection work of the pass; the first
+//           thread of each row also runs the collect pass, which must walk the
+//           row in order.
 // The key stream is replayed once per pass; the tensor cores recompute the
 // identical fp32 scores each time.
 //
-// Digits.  The first pass bins a fast digit of each score over a window placed
-// from a sample of the first key tile (select_keys.cuh: 1/32-octave bins of one
-// sign, or 1/8-octave bins of both signs when the sample leaves the k-th score's
-// sign unclear).  A row whose k-th score lands in an interior bin knows the top
-// 13-14 bits of its key; if the bin then holds at most 128 keys for every row of
-// the warp, the next pass stores those keys (candidate mode) and the k-th is found
-// among them in shared memory; otherwise 8-bit digits follow.  A k-th score in a
-// clamp bin retries the other window once or restarts with plain 8-bit digits
-// from the top.  Every path is exact.  Rows shorter than 65536 use 16-bit
-// counters packed two per 32-bit word (64 KB), so the CTA needs ~105 KB and two
-// CTAs share an SM.  Counters are bumped with predicated shared-memory
-// reductions: no branches, no returned values, and the two threads of a row may
-// share a counter.
+// Passes of a row (each row decides its own; a pass serves every kind at once):
+//   window   a 128-bin histogram of lin_bin(v) over a linear window placed from a
+//            sample (the row's scores against the first key tile: the window is
+//            2 max|s| wide, starting at 0, -W/2 or -W by the sample's sign
+//            balance).  The bin function is two fused multiply-adds and the
+//            counter address one integer multiply-add, all on the FMA pipe, then
+//            one shared-memory reduction.  The bin holding the need-th largest
+//            score is interior (else: plain radix restart) and its edges are
+//            exact keys found by bisection (lin_bin is monotone);
+//   refine   if that bin holds more than kCap keys: the same histogram over the
+//            bin's own interval, counting only its members;
+//   candidate  the members of the chosen bin (at most kCap) are stored (raw float
+//            bits) in the row's histogram column, from both ends by the row's two
+//            threads, and the k-th is found among them (cand_resolve); a chunk of
+//            32 scores is tested for members with FMA-pipe arithmetic only;
+//   plain    fallback radix select over the order-preserving key, 7-bit digits,
+//            with the same candidate step once a digit bin holds <= kCap keys.
+// A row whose chosen bin holds exactly the keys still needed is done at once: its
+// selection is "key >= the bin's lower edge".  Every path is exact; ties at the
+// k-th score go to the lowest index (collect pass).  The histogram is hist[bin][row]
+// in 32-bit counters (64 KB), so two CTAs share an SM.
 static __device__ unsigned int g_index_watchdog;
+// Test support: rows that took the refine pass, the plain restart, a plain
+// candidate pass, a tie cut (counted by the first thread of a row).
+static __device__ unsigned long long g_index_stats[4];
 
 constexpr int kEpiThreads = 256;
+constexpr int kBins = kLinTop + 1;  // histogram bins per row (32-bit counters)
+constexpr int kDigit = 7;           // bits per digit of the plain radix fallback
+constexpr int kCap = kBins;         // candidate slots of a row: its whole histogram column
+constexpr int kMaxPasses = 8;
 
 struct RowSel {
-    uint32_t prefix, mask;
-    int need;
-    int top;     // bits [top-1 : 0] of the k-th key are still unknown
+    uint32_t prefix, mask;  // the k-th key agrees with prefix on the bits of mask
+    int need;               // keys still to take at or below the prefix
+    int top;                // bits [top-1 : 0] of the k-th key are still unknown
     bool done;
-    bool plain;  // the row left the fast window: full order-preserving keys
-    bool exact;  // resolved with every key of the final group selected (no tie cut)
-    int cnt;     // keys in the bin chosen by the last pass
-    bool cand;   // this pass gathers the row's remaining candidate keys instead of counting
-    bool fast;   // this pass bins the fast digit (mode, pb)
-    int mode;
-    int pb;
-    int etop;
+    bool plain;             // radix fallback on the order-preserving keys
+    bool exact;             // resolved with every key at the prefix selected (no tie cut)
+    bool cand;              // the next pass gathers candidates
+    int lvl;                // linear mode: 0 window pass next/done, 1 refine pass next/done
+    int cnt;                // keys in the bin chosen by the last histogram pass
+    float a0, b0, a1, b1;   // the two linear windows
+    int c0, c1;             // their chosen bins
 };
 
-// Key of a score for a row whose k-th score is a positive float: the raw bits
-// with the sign flipped order every positive score correctly and put every
-// negative one (and -0.0) below any positive prefix, which is all the
-// comparisons against such a prefix need.
-
-template <bool PACKED>
 __device__ __forceinline__ uint32_t hist_count(const uint32_t *hist, int bin, int col) {
-    if (PACKED) return (hist[(bin >> 1) * kRows + col] >> ((bin & 1) << 4)) & 0xffffu;
     return hist[bin * kRows + col];
 }
 
-// Choose the bin holding the need-th largest remaining key.  FAST: the
-// fast-digit pass of the row's window.
-template <bool PACKED, bool FAST>
-__device__ __forceinline__ void row_choose(RowSel &s, const uint32_t *hist, int col, int K) {
-    const int w = FAST ? 8 : min(8, s.top);
+// Radix step of the plain fallback: choose the next 8-bit digit among keys matching
+// the prefix.
+__device__ __forceinline__ void row_choose_plain(RowSel &s, const uint32_t *hist, int col) {
+    const int w = min(kDigit, s.top);
     int cum = 0, chosen = 0, cnt = 0;
     for (int bin = (1 << w) - 1; bin >= 0; --bin) {
-        cnt = (int)hist_count<PACKED>(hist, bin, col);
+        cnt = (int)hist_count(hist, bin, col);
         if (cum + cnt >= s.need) { chosen = bin; break; }
         cum += cnt;
     }
-    if (FAST) {
-        if (chosen == 0 || chosen == 255 || (s.mode == 2 && chosen == 127)) {
-            // outside the window: towards zero, retry with both signs; else plain radix
-            const bool toward_zero = s.mode == 0 ? chosen == 0 : s.mode == 1 ? chosen == 255 : false;
-            if (toward_zero) {
-                s.mode = 2;
-                s.pb = fast_base(2, s.etop);
-                s.fast = true;
-            } else {
-                s.prefix = 0u; s.mask = 0u; s.need = K; s.top = 32; s.plain = true;
-                s.fast = false;
-            }
-            s.cnt = 0x7fffffff;
-            return;
-        }
-        s.need -= cum;
-        s.prefix = fast_prefix(chosen, s.mode, s.pb);
-        const bool two = s.mode == 2;
-        s.mask = fast_mask(s.mode);
-        s.top = fast_top(s.mode);
-        // negative k-th: continue on the order-preserving keys
-        s.plain = s.mode == 1 || (two && chosen < 128);
-        s.fast = false;
-    } else {
-        const int shift = s.top - w;
-        s.need -= cum;
-        s.prefix |= (uint32_t)chosen << shift;
-        s.mask |= ((1u << w) - 1u) << shift;
-        s.top = shift;
-    }
+    const int shift = s.top - w;
+    s.need -= cum;
+    s.prefix |= (uint32_t)chosen << shift;
+    s.mask |= ((1u << w) - 1u) << shift;
+    s.top = shift;
     s.cnt = cnt;
     if (cnt == s.need) s.exact = true;
     if (cnt == s.need || s.top == 0) s.done = true;
 }
 
-// Candidate mode.  Once the chosen bin of a row holds at most kCandCap keys, the
-// next pass stores those keys (the row's two threads from the two ends of the
-// row's histogram column) instead of counting a digit, and the row's k-th key is
-// then found among them: bit by bit from the highest unknown bit, keep a bit if at
-// least `need` candidates are >= the prefix with it set.  Exact, and it replaces
-// the remaining digit passes (usually two or three) by one.
 __device__ __forceinline__ void epi_bar() {
     asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
 }
-
-template <bool PACKED>
-struct Cand {
-    static constexpr int kCap = PACKED ? 128 : 256;  // 32-bit slots of a histogram column
-};
 
 __device__ __forceinline__ void st_shared_if(uint32_t addr, uint32_t v, bool pred) {
     asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p st.shared.u32 [%0], %1;\n\t}" ::"r"(addr),
@@ -313,159 +284,307 @@ __device__ __forceinline__ void st_shared_if(uint32_t addr, uint32_t v, bool pre
                  : "memory");
 }
 
-// Candidate gathering of one 32-column chunk: predicated stores, no branches.
-// `slot` is the shared-memory address of this thread's next slot and `step` the
-// byte step between slots (+/- one histogram row); n counts the stored keys.
-template <bool PLAIN, bool FULL, int CAP>
-__device__ __forceinline__ void cand_chunk(const float (&v)[32], uint32_t &slot, int step, int jb,
-                                           int nvalid, const RowSel &s, int &n) {
+// Shared-memory counter increments.  No memory clobber: the counters are read only
+// after the epilogue barrier (epi_bar, which has one), and volatile asm keeps its order.
+__device__ __forceinline__ void red_shared(uint32_t addr) {
+    asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(addr));
+}
+
+__device__ __forceinline__ void red_shared_if(uint32_t addr, bool pred) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %1, 0;\n\t@p red.shared.add.u32 [%0], 1;\n\t}" ::"r"(
+                     addr),
+                 "r"((uint32_t)pred));
+}
+
+// Bits of the bin computation: 0x4B000000 + lin_bin(v).  0x4B000000 * 512 is 0 mod
+// 2^32, so bits * 512 + (address of hist[0][row]) is the address of hist[bin][row].
+__device__ __forceinline__ uint32_t lin_bits(float v, float a, float b) {
+    return __float_as_uint(__fmaf_rn(__saturatef(__fmaf_rn(v, a, b)), (float)kLinTop, 8388608.f));
+}
+
+// Window-pass histogram of one 32-column chunk.
+template <bool FULL>
+__device__ __forceinline__ void lin_hist0(const float (&v)[32], uint32_t cbase, int jb, int nvalid,
+                                          float a, float b) {
+    uint32_t addr[32];  // all 32 addresses first: independent chains, then the reductions
+#pragma unroll
+    for (int i = 0; i < 32; ++i) addr[i] = lin_bits(v[i], a, b) * 512u + cbase;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const uint32_t u = PLAIN ? float_key(v[i]) : fast_key(v[i]);
-        const bool in = (FULL || jb + i < nvalid) && (u & s.mask) == s.prefix && n < CAP;
-        st_shared_if(slot, u, in);
-        slot += in ? step : 0;
-        n += in;
+        if (FULL) red_shared(addr[i]);
+        else red_shared_if(addr[i], jb + i < nvalid);
     }
 }
 
-// The need-th largest of a row's candidates, found two bits at a time from the top
-// unknown bit: both threads of the row count their own list against the three
-// extensions of the prefix, swap the counts through shared memory and take the
-// largest extension that still has `need` keys at or above it.  All epilogue
-// threads run every step (the barriers are CTA-wide); rows not in candidate mode
-// only take part in the barriers.
-template <int CAP>
+// Refine-pass histogram: members of window bin c0 only, binned in window 1.
+template <bool FULL>
+__device__ __forceinline__ void lin_hist1(const float (&v)[32], uint32_t cbase, int jb, int nvalid,
+                                          const RowSel &s) {
+    const uint32_t want = 0x4B000000u + (uint32_t)s.c0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const bool in = (FULL || jb + i < nvalid) && lin_bits(v[i], s.a0, s.b0) == want;
+        red_shared_if(lin_bits(v[i], s.a1, s.b1) * 512u + cbase, in);
+    }
+}
+
+// Candidate gathering of one 32-column chunk (linear mode): a member of the chosen
+// bin(s) is stored (raw float bits) at this thread's slot, which then advances by
+// `step` bytes -- a compare, a predicated store and a predicated add per score, no
+// branches.  The two threads of a row fill the row's column from its two ends; the
+// histogram bounds their total by the chosen bin's count (<= kCap), and the
+// membership test is the same bit-identical computation.
+template <bool FULL, bool LVL1>
+__device__ __forceinline__ void lin_cand(const float (&v)[32], uint32_t &slot, int step, int jb,
+                                         int nvalid, const RowSel &s) {
+    const uint32_t w0 = 0x4B000000u + (uint32_t)s.c0, w1 = 0x4B000000u + (uint32_t)s.c1;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t b0 = lin_bits(v[i], s.a0, s.b0);
+        if (FULL && !LVL1) {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.eq.u32 p, %2, %3;\n\t@p st.shared.u32 [%0], %1;\n\t"
+                "@p add.u32 %0, %0, %4;\n\t}"
+                : "+r"(slot)
+                : "r"(__float_as_uint(v[i])), "r"(b0), "r"(w0), "r"(step));
+        } else {
+            bool in = b0 == w0 && (FULL || jb + i < nvalid);
+            if (LVL1) in = in && lin_bits(v[i], s.a1, s.b1) == w1;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p st.shared.u32 [%0], %1;\n\t"
+                "@p add.u32 %0, %0, %3;\n\t}"
+                : "+r"(slot)
+                : "r"(__float_as_uint(v[i])), "r"((uint32_t)in), "r"(step));
+        }
+    }
+}
+
+// Plain fallback: histogram of the next 8-bit digit among keys matching the prefix.
+template <bool FULL>
+__device__ __forceinline__ void plain_hist(const float (&v)[32], uint32_t *hcol, int jb, int nvalid,
+                                           const RowSel &s) {
+    const int w = min(kDigit, s.top);
+    const int shift = s.top - w;
+    const uint32_t mul = shift ? (1u << (32 - shift)) : 0u;  // u >> shift as a high multiply
+    const uint32_t dmask = (1u << w) - 1u;
+    const uint32_t cbase = (uint32_t)__cvta_generic_to_shared(hcol);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const uint32_t u = float_key(v[i]);
+        const uint32_t d = (shift ? __umulhi(u, mul) : u) & dmask;
+        red_shared_if(cbase + d * (kRows * 4), (FULL || jb + i < nvalid) && (u & s.mask) == s.prefix);
+    }
+}
+
+// Plain fallback: candidates are the scores whose key matches the prefix.
+template <bool FULL>
+__device__ __forceinline__ void plain_cand(const float (&v)[32], uint32_t &slot, int step, int jb,
+                                           int nvalid, const RowSel &s) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const bool in = (FULL || jb + i < nvalid) && (float_key(v[i]) & s.mask) == s.prefix;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p st.shared.u32 [%0], %1;\n\t"
+            "@p add.u32 %0, %0, %3;\n\t}"
+            : "+r"(slot)
+            : "r"(__float_as_uint(v[i])), "r"((uint32_t)in), "r"(step));
+    }
+}
+
+// The need-th largest of a row's candidates.  The row's two threads stored their
+// scores (raw bits) from the two ends of the row's histogram column; after one exchange of the
+// list lengths the first thread resolves the row alone, two bits at a time from the
+// top unknown bit: count the candidates at or above the three extensions of the
+// prefix and keep the largest extension that still has `need` keys.  Called by
+// every epilogue thread (one barrier); the second thread of a row just marks it done.
 __device__ __forceinline__ void cand_resolve(RowSel &s, bool act_row, const uint32_t *col, int n,
                                              int half, uint32_t (*xch)[2][kRows], int row) {
-    const int cstep = half ? -kRows : kRows;
-    const uint32_t *first = col + (half ? (CAP - 1) * kRows : 0);
-    uint32_t x = s.prefix;
-    int it = 0;
-    for (; it < 16; ++it) {
-        // bits [lo, lo + 2) of this row (lo = -1: only bit 0 is left)
-        const int lo = s.top - 2 * (it + 1);
-        const bool act = act_row && lo >= -1;
-        const int gb = max(lo, 0);
-        const uint32_t one = lo < 0 ? 0u : 1u;  // a single bit: only c2 (= bit 0) counts
-        uint32_t pk = 0;
-        if (act) {
-            const uint32_t c1 = x | (one << gb), c2 = x | (2u << gb >> (1 - one)),
-                           c3 = x | (3u << gb >> (1 - one));
-            int k1 = 0, k2 = 0, k3 = 0;
-            for (int i = 0; i < n; ++i) {
-                const uint32_t v = first[i * cstep];
-                k1 += v >= c1;
-                k2 += v >= c2;
-                k3 += v >= c3;
-            }
-            pk = (uint32_t)k1 | ((uint32_t)k2 << 10) | ((uint32_t)k3 << 20);
-            xch[it & 1][half][row] = pk;
-        }
-        epi_bar();
-        if (act) {
-            const uint32_t o = xch[it & 1][half ^ 1][row];
-            const int need = s.need;
-            const int k3 = (int)((pk >> 20) + (o >> 20));
-            const int k2 = (int)(((pk >> 10) & 1023u) + ((o >> 10) & 1023u));
-            const int k1 = (int)((pk & 1023u) + (o & 1023u));
-            if (one)
-                x |= (k3 >= need ? 3u : k2 >= need ? 2u : k1 >= need ? 1u : 0u) << gb;
-            else
-                x |= k2 >= need ? 1u : 0u;
-        }
-    }
-    uint32_t pk = 0;
-    if (act_row) {
-        int gt = 0, eq = 0;
-        for (int i = 0; i < n; ++i) {
-            const uint32_t v = first[i * cstep];
-            gt += v > x;
-            eq += v == x;
-        }
-        pk = (uint32_t)gt | ((uint32_t)eq << 10);
-        xch[it & 1][half][row] = pk;
-    }
+    if (act_row && half == 1) xch[0][1][row] = (uint32_t)n;
     epi_bar();
-    if (act_row) {
-        const uint32_t o = xch[it & 1][half ^ 1][row];
-        const int gt = (int)((pk & 1023u) + (o & 1023u));
-        const int eq = (int)((pk >> 10) + (o >> 10));
-        s.need -= gt;
-        s.prefix = x;
+    if (!act_row) return;
+    s.done = true;
+    s.cand = false;
+    if (half == 1) return;
+    const int n1 = (int)xch[0][1][row];
+    const uint32_t *back = col + (kCap - 1) * kRows;
+    uint32_t x = s.prefix;
+    const int need = s.need;
+    for (int lo = s.top - 2; lo >= -1; lo -= 2) {
+        // bits [lo, lo + 2) (lo = -1: only bit 0 is left)
+        const int gb = max(lo, 0);
+        const uint32_t one = lo < 0 ? 0u : 1u;
+        const uint32_t c1 = x | (one << gb), c2 = x | (2u << gb >> (1 - one)),
+                       c3 = x | (3u << gb >> (1 - one));
+        int k1 = 0, k2 = 0, k3 = 0;
+#pragma unroll 4
+        for (int i = 0; i < n; ++i) {
+            const uint32_t v = float_key(__uint_as_float(col[i * kRows]));
+            k1 += v >= c1;
+            k2 += v >= c2;
+            k3 += v >= c3;
+        }
+#pragma unroll 4
+        for (int i = 0; i < n1; ++i) {
+            const uint32_t v = float_key(__uint_as_float(back[-i * kRows]));
+            k1 += v >= c1;
+            k2 += v >= c2;
+            k3 += v >= c3;
+        }
+        if (one)
+            x |= (k3 >= need ? 3u : k2 >= need ? 2u : k1 >= need ? 1u : 0u) << gb;
+        else
+            x |= k2 >= need ? 1u : 0u;
+    }
+    int gt = 0, eq = 0;
+    for (int i = 0; i < n; ++i) {
+        const uint32_t v = float_key(__uint_as_float(col[i * kRows]));
+        gt += v > x;
+        eq += v == x;
+    }
+    for (int i = 0; i < n1; ++i) {
+        const uint32_t v = float_key(__uint_as_float(back[-i * kRows]));
+        gt += v > x;
+        eq += v == x;
+    }
+    s.need -= gt;
+    s.prefix = x;
+    s.mask = 0xffffffffu;
+    s.top = 0;
+    s.exact = eq == s.need;
+}
+
+// Sets up candidate mode for keys in [klo, khi] (they share the bits above `top`).
+__device__ __forceinline__ void to_cand(RowSel &s, uint32_t klo, uint32_t khi) {
+    key_range_prefix(klo, khi, s.prefix, s.top);
+    s.mask = s.top >= 32 ? 0u : ~((1u << s.top) - 1u);
+    s.cand = true;
+}
+
+__device__ __forceinline__ void to_plain(RowSel &s, int K) {
+    s.plain = true;
+    s.cand = false;
+    s.prefix = 0u;
+    s.mask = 0u;
+    s.need = K;
+    s.top = 32;
+}
+
+// Choose the bin holding the need-th largest counted key: (bin, keys above it, its
+// count).  Group sums of 8 bins first (independent loads), then the crossing group.
+__device__ __forceinline__ void lin_choose(const uint32_t *hist, int col, int need, int &chosen,
+                                           int &cum, int &cnt) {
+    constexpr int kG = kBins / 8;
+    int gs[kG];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+        int t = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t += (int)hist_count(hist, g * 8 + i, col);
+        gs[g] = t;
+    }
+    cum = 0;
+    int g0 = 0;
+#pragma unroll
+    for (int g = kG - 1; g >= 0; --g) {
+        if (cum + gs[g] >= need) { g0 = g; break; }
+        cum += gs[g];
+    }
+    int c[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = (int)hist_count(hist, g0 * 8 + i, col);
+    chosen = g0 * 8;
+    cnt = c[0];
+#pragma unroll
+    for (int i = 7; i >= 0; --i) {
+        if (cum + c[i] >= need) { chosen = g0 * 8 + i; cnt = c[i]; break; }
+        cum += c[i];
+    }
+}
+
+// After the window pass: the chosen bin, with exact key edges by bisection.
+__device__ __forceinline__ void lin_after0(RowSel &s, const uint32_t *hist, int col, int K,
+                                           unsigned long long *stats, bool count) {
+    int c, cum, cnt;
+    lin_choose(hist, col, s.need, c, cum, cnt);
+    if (c == 0 || c == kLinTop) {  // the k-th score is outside the window
+        to_plain(s, K);
+        if (count) atomicAdd(&stats[1], 1ull);
+        return;
+    }
+    s.need -= cum;
+    s.c0 = c;
+    s.cnt = cnt;
+    const float a = s.a0, b = s.b0;
+    const uint32_t klo = min_key_near([&](float x) { return (int)lin_bin(x, a, b) >= c; },
+                                      lin_edge_guess(c, a, b));
+    if (cnt == s.need) {  // every key of the bin is taken: key >= its lower edge
+        s.prefix = klo;
         s.mask = 0xffffffffu;
         s.top = 0;
-        s.done = true;
-        s.exact = eq == s.need;
+        s.done = s.exact = true;
+        return;
     }
+    const uint32_t khi = min_key_near([&](float x) { return (int)lin_bin(x, a, b) >= c + 1; },
+                                      lin_edge_guess(c + 1, a, b));
+    if (cnt <= kCap) {
+        to_cand(s, klo, khi - 1u);
+        return;
+    }
+    // too many keys in the bin: a second window over its interval
+    s.lvl = 1;
+    const float xlo = key_float(klo), xhi = key_float(khi);
+    const float inv = 1.0f / (xhi - xlo);
+    s.a1 = inv;
+    s.b1 = -xlo * inv;
+    if (count) atomicAdd(&stats[0], 1ull);
 }
 
-template <int DI, bool PACKED>
-struct TcCfg {
-    static constexpr int kKB = DI / 64;                // 128-byte K blocks
-    // 64-key tiles in both modes: the tensor-core attention recomputes these
-    // scores with the same instruction shapes, which keeps them bit-identical
-    static constexpr int kN = 64;                      // keys per tile
-    static constexpr int kStages = 3;
-    static constexpr int kQBytes = 128 * DI * 2;
-    static constexpr int kKBytes = kN * DI * 2;
-    static constexpr int kHistBytes = (PACKED ? 128 : 256) * kRows * 4;
-    static constexpr int kAcc = 4;                     // TMEM accumulator buffers
-    static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
-    static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
-    static constexpr int kMinBlocks = (kSmem * 2 + 2048 <= 233472) ? 2 : 1;
-    static constexpr int kTmemCols = kAcc * kN;
-    static constexpr int kThreads = 64 + kEpiThreads;
-};
-
-__device__ __forceinline__ void red_shared_if(uint32_t *addr, uint32_t inc, bool pred) {
-    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t@p red.shared.add.u32 [%0], %1;\n\t}" ::"r"(
-                     (uint32_t)__cvta_generic_to_shared(addr)),
-                 "r"(inc), "r"((uint32_t)pred)
-                 : "memory");
-}
-
-
-// Histogram update of one 32-column chunk.  FAST: the fast digit of the row's
-// window (fast_digit); else the row's next digit among keys
-// matching its prefix, with keys from float_key (PLAIN) or fast_key.  FULL skips
-// the causal bound check.
-template <bool FAST, bool PLAIN, bool FULL, bool PACKED, int MODE = 0>
-__device__ __forceinline__ void hist_chunk(const float (&v)[32], uint32_t *hcol, int jb,
-                                           int nvalid, const RowSel &s) {
-    // u >> shift as a high multiply (no variable-amount shift in the loop)
-    const int w = min(8, s.top);
-    const int shift = s.top - w;
-    const uint32_t mul = shift ? (1u << (32 - shift)) : 0u;
-    const uint32_t dmask = (1u << w) - 1u;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const bool ok = FULL || jb + i < nvalid;
-        uint32_t d;
-        bool in;
-        if (FAST) {
-            d = fast_digit_m<MODE>(v[i], s.pb);
-            in = ok;
-        } else {
-            const uint32_t u = PLAIN ? float_key(v[i]) : fast_key(v[i]);
-            d = (shift ? __umulhi(u, mul) : u) & dmask;
-            in = ok && (u & s.mask) == s.prefix;
-        }
-        if (PACKED) red_shared_if(hcol + (d >> 1) * kRows, (d & 1u) * 0xffffu + 1u, in);
-        else red_shared_if(hcol + d * kRows, 1u, in);
+__device__ __forceinline__ void lin_after1(RowSel &s, const uint32_t *hist, int col, int K,
+                                           unsigned long long *stats, bool count) {
+    int c, cum, cnt;
+    lin_choose(hist, col, s.need, c, cum, cnt);
+    s.need -= cum;
+    s.c1 = c;
+    s.cnt = cnt;
+    const float a0 = s.a0, b0 = s.b0, a1 = s.a1, b1 = s.b1;
+    const int c0 = s.c0;
+    // (bin0, bin1) is lexicographically monotone in the score
+    auto at_least = [&](int cc) {
+        return [=](float x) {
+            const int d0 = (int)lin_bin(x, a0, b0);
+            return d0 > c0 || (d0 == c0 && (int)lin_bin(x, a1, b1) >= cc);
+        };
+    };
+    const uint32_t klo = min_key_near(at_least(c), lin_edge_guess(c, a1, b1));
+    if (cnt == s.need) {
+        s.prefix = klo;
+        s.mask = 0xffffffffu;
+        s.top = 0;
+        s.done = s.exact = true;
+        return;
     }
+    if (cnt <= kCap) {
+        const uint32_t khi =
+            c < kLinTop ? min_key_near(at_least(c + 1), lin_edge_guess(c + 1, a1, b1))
+                        : min_key_near([=](float x) { return (int)lin_bin(x, a0, b0) > c0; },
+                                       lin_edge_guess(c0 + 1, a0, b0));
+        to_cand(s, klo, khi - 1u);
+        return;
+    }
+    to_plain(s, K);
+    if (count) atomicAdd(&stats[1], 1ull);
 }
 
 // Collect of one 32-column chunk: selected column indices go, branch-free,
 // into this row's 32-slot ring in shared memory (ring[slot * kRows + row]),
 // which the caller then flushes in order to the output row.
-template <bool PLAIN, bool FULL>
+template <bool FULL>
 __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ring, int jb,
                                               int nvalid, const RowSel &s, int &pos,
                                               int &taken, int &lastj) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const uint32_t m = (PLAIN ? float_key(v[i]) : fast_key(v[i])) & s.mask;
+        const uint32_t m = float_key(v[i]) & s.mask;
         const bool ok = FULL || jb + i < nvalid;
         const bool eq = ok && m == s.prefix && taken < s.need;
         const bool sel = eq || (ok && m > s.prefix);
@@ -476,13 +595,30 @@ __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ri
     }
 }
 
-template <int DI, bool PACKED>
-__global__ void __launch_bounds__(TcCfg<DI, PACKED>::kThreads, (TcCfg<DI, PACKED>::kMinBlocks))
+template <int DI>
+struct TcCfg {
+    static constexpr int kKB = DI / 64;                // 128-byte K blocks
+    // 64-key tiles: the tensor-core attention recomputes these scores with the
+    // same instruction shapes, which keeps them bit-identical
+    static constexpr int kN = 64;                      // keys per tile
+    static constexpr int kStages = 3;
+    static constexpr int kQBytes = 128 * DI * 2;
+    static constexpr int kKBytes = kN * DI * 2;
+    static constexpr int kHistBytes = kBins * kRows * 4;
+    static constexpr int kAcc = 4;                     // TMEM accumulator buffers
+    static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
+    static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
+    static constexpr int kTmemCols = kAcc * kN;
+    static constexpr int kThreads = 64 + kEpiThreads;
+};
+
+template <int DI>
+__global__ void __launch_bounds__(TcCfg<DI>::kThreads, 2)
 indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx,
                        uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt,
                        const int32_t *__restrict__ q_tiles, float *__restrict__ dbg_scores) {
-    using C = TcCfg<DI, PACKED>;
+    using C = TcCfg<DI>;
     using namespace sm100;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -494,8 +630,6 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
              *tempty = tfull + C::kAcc, *qbar = tempty + C::kAcc;
     __shared__ uint32_t s_tmem;
     __shared__ uint32_t s_xch[2][2][kRows];
-    __shared__ uint32_t s_amax;  // largest |score| bits of the first key tile's sample
-    constexpr int kCap = Cand<PACKED>::kCap;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int BH = B * H;
@@ -514,10 +648,10 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
     const bool has_row = epi && t < T;
+    const bool stat_thread = has_row && half == 0;
     int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
     uint4 *thr_row = (has_row && thr) ? thr + (size_t)bh * T + t : nullptr;
-    RowSel s{0u, 0u, K, 32, true, false, true, 0, false, false, 0, fast_base(0, kDefaultEtop),
-             kDefaultEtop};
+    RowSel s{0u, 0u, K, 32, true, false, true, false, 0, 0, 0.f, 0.f, 0.f, 0.f, 0, 0};
     if (epi && nvalid > K) {
         s.done = false;
         s.exact = false;
@@ -530,7 +664,6 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     if (q_last + 1 <= K) return;  // every row of the tile keeps all its columns
 
     if (warp == 0 && lane == 0) {
-        s_amax = 0u;
         for (int i = 0; i < C::kStages; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -550,13 +683,11 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    // fast digit, the other-sign retry, 4 plain digits after a fallback, spare
-    constexpr int kMaxDigitPasses = 7;
-    constexpr int kChunksPerHalf = C::kN / 64;
-    static_assert(kChunksPerHalf == 1, "the first-tile sample assumes one chunk per thread and tile");
     uint32_t it_p = 0, it_m = 0, it_e = 0;
     bool collecting = false;
     bool cand_pass = false;  // CTA-uniform: some row gathers candidates in this pass
+    uint32_t *hcol = hist + row;
+    const uint32_t cbase = (uint32_t)__cvta_generic_to_shared(hcol);
     for (int pass = 0;; ++pass) {
         if (warp == 0) {
             if (lane == 0) {
@@ -604,15 +735,17 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
         } else {
             const bool active = !s.done;
-            uint32_t *hcol = hist + row;
+            // what this row does in this pass
+            const bool do_cand = active && s.cand;
+            const bool do_hist = active && !s.cand;
             const bool collect = collecting && half == 0 && has_row && nvalid > K;
             if (!collecting) {
-                if (half == 0 && active && !s.cand)
-                    for (int w = 0; w < (PACKED ? 128 : 256); ++w) hcol[w * kRows] = 0u;
+                if (do_hist)
+                    for (int w = half * (kBins / 2); w < (half + 1) * (kBins / 2); ++w) hcol[w * kRows] = 0u;
                 epi_bar();
             }
             uint32_t *ring = hist + row;  // the histogram is idle during the collect pass
-            int pos = 0, taken = 0, flushed = 0, lastj = -1, ncand = 0;
+            int pos = 0, taken = 0, flushed = 0, lastj = -1;
             // candidate slots: half 0 from the front of the row's column, half 1 from the back
             uint32_t cslot = (uint32_t)__cvta_generic_to_shared(hcol + (half ? (kCap - 1) * kRows : 0));
             const int cstep = half ? -(int)(kRows * 4) : (int)(kRows * 4);
@@ -623,74 +756,64 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                 const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN;
                 const bool full_tile = (kt + 1) * C::kN <= nvalid;
                 if (!collecting) {
-#pragma unroll 1
-                    for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
-                        float v[32];
-                        tmem_ld32(taddr + c * 32, v);
-                        const int jb = kt * C::kN + c * 32;
-                        if (dbg_scores && pass == 0 && has_row) {
-                            // test support: the fp32 scores this pass selects from
-                            float *dr = dbg_scores + ((size_t)bh * T + t) * T;
+                    float v[32];
+                    tmem_ld32(taddr + half * 32, v);
+                    const int jb = kt * C::kN + half * 32;
+                    if (dbg_scores && pass == 0 && has_row) {
+                        // test support: the fp32 scores this pass selects from
+                        float *dr = dbg_scores + ((size_t)bh * T + t) * T;
 #pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                if (jb + i < nvalid) dr[jb + i] = v[i];
-                        }
-                        if (pass == 0 && kt == 0) {
-                            // sample of the first key tile: place every row's fast window
-                            uint32_t amax = 0u;
-                            int np = 0, nv = 0;
+                        for (int i = 0; i < 32; ++i)
+                            if (jb + i < nvalid) dr[jb + i] = v[i];
+                    }
+                    if (pass == 0 && kt == 0) {
+                        // sample of the first key tile: place every row's window
+                        uint32_t amax = 0u;
+                        int np = 0, nv = 0;
 #pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                const bool ok = active && jb + i < nvalid;
-                                amax = max(amax, ok ? (__float_as_uint(v[i]) & 0x7fffffffu) : 0u);
-                                np += ok && v[i] > 0.f;
-                                nv += ok;
-                            }
-                            amax = __reduce_max_sync(0xffffffffu, amax);
-                            if (lane == 0) atomicMax(&s_amax, amax);
-                            s_xch[0][half][row] = (uint32_t)np | ((uint32_t)nv << 16);
-                            epi_bar();
-                            const uint32_t o = s_xch[0][half ^ 1][row];
-                            const int npos = np + (int)(o & 0xffffu), nval = nv + (int)(o >> 16);
-                            const int etop = min(max((int)(s_amax >> 23) + 3, 17), 255);  // bottom above 0 and denormals
-                            s.etop = etop;
-                            // estimated positives p*(t+1) against need: clear margins pick a sign
-                            const float p = nval ? (float)npos / (float)nval : 0.5f;
-                            const float q = (float)s.need / (float)nvalid;
-                            const int m = p > q + 0.15f ? 0 : p < q - 0.15f ? 1 : 2;
-                            // one formula per warp: a sign only if every active row agrees
-                            const bool all0 = __all_sync(0xffffffffu, !active || m == 0);
-                            const bool all1 = __all_sync(0xffffffffu, !active || m == 1);
-                            s.mode = all0 ? 0 : all1 ? 1 : 2;
-                            s.pb = fast_base(s.mode, etop);
-                            s.fast = true;
+                        for (int i = 0; i < 32; ++i) {
+                            const bool ok = active && jb + i < nvalid;
+                            amax = max(amax, ok ? (__float_as_uint(v[i]) & 0x7fffffffu) : 0u);
+                            np += ok && v[i] > 0.f;
+                            nv += ok;
                         }
-                        if (!active || jb >= nvalid) continue;
-                        if (s.cand) {
-                            if (!s.plain) {
-                                if (full_tile) cand_chunk<false, true, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
-                                else cand_chunk<false, false, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
+                        s_xch[0][half][row] = (uint32_t)np | ((uint32_t)nv << 16);
+                        s_xch[1][half][row] = amax;
+                        epi_bar();
+                        const uint32_t o = s_xch[0][half ^ 1][row];
+                        amax = max(amax, s_xch[1][half ^ 1][row]);
+                        const int npos = np + (int)(o & 0xffffu), nval = nv + (int)(o >> 16);
+                        // window 2 max|s| wide; by the sample's share of positive scores
+                        // against the share to select: [0, W), [-W/2, W/2) or [-W, 0)
+                        float W = 2.0f * __uint_as_float(min(amax, 0x7f000000u));
+                        W = W > 1e-30f ? W : 1.0f;
+                        const float p = nval ? (float)npos / (float)nval : 0.5f;
+                        const float q = (float)s.need / (float)max(nvalid, 1);
+                        const float lo = p > q + 0.15f ? 0.f : p < q - 0.15f ? -W : -0.5f * W;
+                        s.a0 = 1.0f / W;
+                        s.b0 = -lo * s.a0;
+                    }
+                    if (active && jb < nvalid) {
+                        if (do_cand) {
+                            if (s.plain) {
+                                if (full_tile) plain_cand<true>(v, cslot, cstep, jb, nvalid, s);
+                                else plain_cand<false>(v, cslot, cstep, jb, nvalid, s);
+                            } else if (s.lvl == 0) {
+                                if (full_tile) lin_cand<true, false>(v, cslot, cstep, jb, nvalid, s);
+                                else lin_cand<false, false>(v, cslot, cstep, jb, nvalid, s);
                             } else {
-                                if (full_tile) cand_chunk<true, true, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
-                                else cand_chunk<true, false, kCap>(v, cslot, cstep, jb, nvalid, s, ncand);
+                                if (full_tile) lin_cand<true, true>(v, cslot, cstep, jb, nvalid, s);
+                                else lin_cand<false, true>(v, cslot, cstep, jb, nvalid, s);
                             }
-                        } else if (s.fast) {
-                            if (s.mode == 0) {
-                                if (full_tile) hist_chunk<true, false, true, PACKED, 0>(v, hcol, jb, nvalid, s);
-                                else hist_chunk<true, false, false, PACKED, 0>(v, hcol, jb, nvalid, s);
-                            } else if (s.mode == 1) {
-                                if (full_tile) hist_chunk<true, false, true, PACKED, 1>(v, hcol, jb, nvalid, s);
-                                else hist_chunk<true, false, false, PACKED, 1>(v, hcol, jb, nvalid, s);
-                            } else {
-                                if (full_tile) hist_chunk<true, false, true, PACKED, 2>(v, hcol, jb, nvalid, s);
-                                else hist_chunk<true, false, false, PACKED, 2>(v, hcol, jb, nvalid, s);
-                            }
-                        } else if (!s.plain) {
-                            if (full_tile) hist_chunk<false, false, true, PACKED>(v, hcol, jb, nvalid, s);
-                            else hist_chunk<false, false, false, PACKED>(v, hcol, jb, nvalid, s);
+                        } else if (s.plain) {
+                            if (full_tile) plain_hist<true>(v, hcol, jb, nvalid, s);
+                            else plain_hist<false>(v, hcol, jb, nvalid, s);
+                        } else if (s.lvl == 0) {
+                            if (full_tile) lin_hist0<true>(v, cbase, jb, nvalid, s.a0, s.b0);
+                            else lin_hist0<false>(v, cbase, jb, nvalid, s.a0, s.b0);
                         } else {
-                            if (full_tile) hist_chunk<false, true, true, PACKED>(v, hcol, jb, nvalid, s);
-                            else hist_chunk<false, true, false, PACKED>(v, hcol, jb, nvalid, s);
+                            if (full_tile) lin_hist1<true>(v, cbase, jb, nvalid, s);
+                            else lin_hist1<false>(v, cbase, jb, nvalid, s);
                         }
                     }
                 } else if (half == 0) {
@@ -700,13 +823,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         tmem_ld32(taddr + c * 32, v);
                         const int jb = kt * C::kN + c * 32;
                         if (!collect || jb >= nvalid) continue;
-                        if (!s.plain) {
-                            if (full_tile) collect_chunk<false, true>(v, ring, jb, nvalid, s, pos, taken, lastj);
-                            else collect_chunk<false, false>(v, ring, jb, nvalid, s, pos, taken, lastj);
-                        } else {
-                            if (full_tile) collect_chunk<true, true>(v, ring, jb, nvalid, s, pos, taken, lastj);
-                            else collect_chunk<true, false>(v, ring, jb, nvalid, s, pos, taken, lastj);
-                        }
+                        if (full_tile) collect_chunk<true>(v, ring, jb, nvalid, s, pos, taken, lastj);
+                        else collect_chunk<false>(v, ring, jb, nvalid, s, pos, taken, lastj);
                         if (out_row) {
                             for (; flushed < pos; ++flushed)
                                 if (flushed < K) out_row[flushed] = (int32_t)ring[(flushed & 31) * kRows];
@@ -719,15 +837,24 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             }
             if (!collecting) {
                 epi_bar();  // every reduction / candidate of the pass has landed
-                if (cand_pass) cand_resolve<kCap>(s, active && s.cand, hcol, ncand, half, s_xch, row);
-                if (active && !s.cand) {
-                    if (s.fast) row_choose<PACKED, true>(s, hist, row, K);
-                    else row_choose<PACKED, false>(s, hist, row, K);
+                if (cand_pass) {
+                    const uint32_t c0 = (uint32_t)__cvta_generic_to_shared(hcol + (half ? (kCap - 1) * kRows : 0));
+                    const int ncand = (int)((half ? c0 - cslot : cslot - c0) / (kRows * 4));
+                    cand_resolve(s, do_cand, hcol, ncand, half, s_xch, row);
                 }
-                // candidate mode only for whole warps: a warp mixing the two kinds of
-                // pass would run both code paths
-                const bool fits = __all_sync(0xffffffffu, s.done || s.cnt <= kCap);
-                if (!s.done && fits) s.cand = true;
+                if (do_hist) {
+                    if (s.plain) {
+                        row_choose_plain(s, hist, row);
+                        if (!s.done && s.cnt <= kCap) {
+                            s.cand = true;
+                            if (stat_thread) atomicAdd(&g_index_stats[2], 1ull);
+                        }
+                    } else if (s.lvl == 0) {
+                        lin_after0(s, hist, row, K, g_index_stats, stat_thread);
+                    } else {
+                        lin_after1(s, hist, row, K, g_index_stats, stat_thread);
+                    }
+                }
             } else if (collect) {
                 if (out_row)
                     for (int i = min(pos, K); i < K; ++i) out_row[i] = -1;
@@ -738,11 +865,17 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int more = __syncthreads_or(epi && !s.done);
         cand_pass = __syncthreads_or(epi && !s.done && s.cand);
         if (collecting) break;
-        if (!more || pass + 1 >= kMaxDigitPasses) {
+        if (more && pass + 1 >= kMaxPasses) {
+            // cannot happen (the plain radix ends after 4 digits); flag it rather than spin
+            if (threadIdx.x == 0) atomicOr(wd, 0x40u);
+        }
+        if (!more || pass + 1 >= kMaxPasses) {
             // Without index rows to write, the collect pass only finds the tie cut of
             // rows whose k-th key is an exact tie; if there is none, it is skipped.
+            const bool tie_row = epi && half == 0 && has_row && nvalid > K && !s.exact;
+            if (tie_row) atomicAdd(&g_index_stats[3], 1ull);
             if (!idx) {
-                const bool ties = __syncthreads_or(epi && half == 0 && has_row && nvalid > K && !s.exact);
+                const bool ties = __syncthreads_or(tie_row);
                 if (!ties) {
                     if (epi && half == 0 && thr_row && nvalid > K)
                         *thr_row = make_uint4(s.prefix, s.mask, 0x7fffffffu, 1u);
@@ -758,16 +891,16 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     if (warp == 1) tmem_dealloc(tmem, C::kTmemCols);
 }
 
-template <int DI, bool PACKED>
+template <int DI>
 cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T, int H,
                    int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st,
                    float *dbg_scores = nullptr) {
-    using C = TcCfg<DI, PACKED>;
+    using C = TcCfg<DI>;
     CUtensorMap mq, mk;
     if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
         !make_tmap_rows_bf16(&mk, ik, B, T, H, DI, C::kN))
         return cudaErrorInvalidValue;
-    auto kern = indexer_topk_tc_kernel<DI, PACKED>;
+    auto kern = indexer_topk_tc_kernel<DI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)C::kSmem);
     if (e != cudaSuccess) return e;
@@ -782,9 +915,7 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int
 template <int DI>
 cudaError_t run_tc_t(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T,
                      int H, int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st) {
-    // 16-bit counters hold any count below 65536, the longest row they can see.
-    if (T < 65536) return run_tc<DI, true>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st);
-    return run_tc<DI, false>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st);
+    return run_tc<DI>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st);
 }
 
 template <typename Tin, int DI>
@@ -866,9 +997,19 @@ cudaError_t launch_indexer_topk_debug(const void *iq, const void *ik, int32_t *i
                                      float *scores, int B, int T, int H, int DI, int K,
                                      cudaStream_t st) {
     if (T >= 65536) return cudaErrorInvalidValue;
-    if (DI == 64) return run_tc<64, true>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st, scores);
-    if (DI == 128) return run_tc<128, true>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st, scores);
+    if (DI == 64) return run_tc<64>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st, scores);
+    if (DI == 128) return run_tc<128>(iq, ik, idx, nullptr, B, T, H, K, nullptr, 0, st, scores);
     return cudaErrorInvalidValue;
+}
+
+int read_index_stats(unsigned long long *out, bool reset) {
+    if (cudaMemcpyFromSymbol(out, g_index_stats, 4 * sizeof(unsigned long long)) != cudaSuccess)
+        return -1;
+    if (reset) {
+        const unsigned long long z[4] = {0, 0, 0, 0};
+        if (cudaMemcpyToSymbol(g_index_stats, z, sizeof(z)) != cudaSuccess) return -1;
+    }
+    return 0;
 }
 
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,

@@ -1,11 +1,13 @@
-// Order-preserving keys and the indexer's first-pass digit.  Plain C++ apart from
-// the __host__ __device__ qualifiers, so that a host program can check the
+// Order-preserving keys and the indexer's linear-window bins.  Plain C++ apart
+// from the __host__ __device__ qualifiers, so that a host program can check the
 // invariants the exact selection relies on (tests/select_keys_check.cpp).
 #pragma once
 
 #include <stdint.h>
 #ifndef __CUDACC__
 #include <string.h>
+
+#include <cmath>
 #endif
 
 #ifdef __CUDACC__
@@ -34,54 +36,112 @@ SGSA_HD uint32_t float_key(float f) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Key of a score for a row whose k-th score is a positive float: the raw bits
-// with the sign flipped order every positive score correctly and put every
-// negative one (and -0.0) below any positive prefix, which is all the
-// comparisons against such a prefix need.
-SGSA_HD uint32_t fast_key(float f) { return float_bits(f) ^ 0x80000000u; }
-
-SGSA_HD int imin_(int a, int b) { return a < b ? a : b; }
-SGSA_HD int imax_(int a, int b) { return a > b ? a : b; }
-
-// First-pass (fast) digit, placed per CTA and row from a sample of the first key
-// tile (the window's top is 4-8x the sample's largest |score|: exponent field etop):
-//   mode 0 (rows whose sample says the k-th score is positive): 1/32-octave bins of
-//          the positive scores in the 8 octaves below the top: bin = code(v) - pb with
-//          code = raw bits >> 18 (14 bits: sign, exponent, 5 mantissa bits) and
-//          pb = (etop - 8) << 5 the code of the window's bottom;
-//   mode 1 (k-th negative): the same bins of -v, in reverse order;
-//   mode 2 (sign unclear): 1/8-octave bins over 16 octaves of each sign (pb =
-//          (etop - 16) << 3): negative scores in bins 0..127, positive ones in
-//          128..255, the small |v| of both signs meet in 127.
-// The kernel picks the mode per warp (fast_digit_m<MODE>), so a warp never mixes
-// the formulas.  Bins 0 and 255 (and 127 in mode 2) are the clamp bins: a k-th score
-// there makes the row retry in mode 2 (mode 0/1, towards zero) or fall back to plain
-// radix.  etop >= 17 keeps zero and the denormals below every window.
-constexpr int kDefaultEtop = 127 + 8;  // top 2^8 without a sample
-
-SGSA_HD int fast_base(int mode, int etop) { return mode == 2 ? (etop - 16) << 3 : (etop - 8) << 5; }
-SGSA_HD uint32_t fast_mask(int mode) { return mode == 2 ? 0xfff00000u : 0xfffc0000u; }
-SGSA_HD int fast_top(int mode) { return mode == 2 ? 20 : 18; }
-
-template <int MODE>
-SGSA_HD uint32_t fast_digit_m(float f, int pb) {
-    const uint32_t u = float_bits(f);
-    if (MODE == 0) return (uint32_t)imin_(imax_((int)u >> 18, pb) - pb, 255);  // (int)u < 0: bin 0
-    if (MODE == 1) return (uint32_t)imin_(imax_((int)(u ^ 0x80000000u) >> 18, pb) - pb, 255) ^ 255u;
-    const int sg = (int)u >> 31;                               // 0 or -1
-    const int c = (int)((u & 0x7fffffffu) >> 20) - pb;         // 1/8-octave code above bottom
-    return (uint32_t)(128 + imin_(imax_(c, -1 - sg), 127)) ^ (uint32_t)(sg & 255);
+// ---- Linear window bins (the tensor-core indexer's first pass) ---------------
+//
+// A row's window is [lo, lo + W), given as a = 1/W, b = -lo/W.  The bin of a score is
+//   lin_bin(v) = round(kLinTop * sat(v * a + b))  in 0 .. kLinTop = 127,
+// computed with two fused multiply-adds (the second adds 2^23, so the rounded
+// integer is the low byte of the result's bits).  Every step is monotone
+// non-decreasing in v (correctly rounded fma, saturation to [0, 1]), so the bin is a
+// monotone function of the score: a bin is an interval of scores, and "bin >= c" is
+// "key(v) >= min_key_where(bin >= c)".  Bins 0 and kLinTop also hold the scores below
+// and above the window.  NaN scores land in bin 0.
+constexpr int kLinTop = 127;
+SGSA_HD float sat01(float x) {
+#ifdef __CUDA_ARCH__
+    return __saturatef(x);
+#else
+    return x > 0.f ? (x < 1.f ? x : 1.f) : 0.f;  // NaN -> 0, as the device saturation
+#endif
 }
 
-SGSA_HD uint32_t fast_digit(float f, int mode, int pb) {
-    return mode == 0 ? fast_digit_m<0>(f, pb) : mode == 1 ? fast_digit_m<1>(f, pb) : fast_digit_m<2>(f, pb);
+SGSA_HD float fma_rn(float a, float b, float c) {
+#ifdef __CUDA_ARCH__
+    return __fmaf_rn(a, b, c);
+#else
+    return std::fma(a, b, c);
+#endif
 }
 
-// Key prefix (under fast_mask(mode)) of fast bin d, which is interior.
-SGSA_HD uint32_t fast_prefix(int d, int mode, int pb) {
-    if (mode == 0) return (uint32_t)(0x2000 + pb + d) << 18;
-    if (mode == 1) return (uint32_t)(0x1f00 - pb + d) << 18;
-    return d >= 128 ? (uint32_t)(0x800 + pb + d - 128) << 20 : (uint32_t)(0x7ff - pb - 127 + d) << 20;
+SGSA_HD uint32_t lin_bin(float v, float a, float b) {
+    const float y = sat01(fma_rn(v, a, b));
+    return float_bits(fma_rn(y, (float)kLinTop, 8388608.f)) - 0x4B000000u;
+}
+
+// The float whose order-preserving key is k (the inverse of float_key, -0.0 as +0.0).
+SGSA_HD float key_float(uint32_t k) {
+    const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f;
+    memcpy(&f, &u, sizeof(f));
+    return f;
+#endif
+}
+
+constexpr uint32_t kKeyNegInf = 0x007fffffu;  // float_key(-inf)
+constexpr uint32_t kKeyPosInf = 0xff800000u;  // float_key(+inf)
+
+// Smallest key k in (key(-inf), key(+inf)] with pred(key_float(k)) true, for a
+// predicate that is monotone in the key, false at -inf and true at +inf (the keys
+// between hold no NaN).  32 bisection steps.
+template <typename Pred>
+SGSA_HD uint32_t min_key_where(Pred pred) {
+    uint32_t lo = kKeyNegInf, hi = kKeyPosInf;  // pred(lo) false, pred(hi) true
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        if (pred(key_float(mid))) hi = mid;
+        else lo = mid;
+    }
+    return hi;
+}
+
+// min_key_where(pred), searched from a guess key0: gallop away from key0 until the
+// edge is bracketed, then bisect.  A good guess (a few ulps off) takes a few steps.
+template <typename Pred>
+SGSA_HD uint32_t min_key_near(Pred pred, uint32_t key0) {
+    key0 = key0 <= kKeyNegInf ? kKeyNegInf + 1u : key0 > kKeyPosInf ? kKeyPosInf : key0;
+    uint32_t lo, hi;  // pred(lo) false, pred(hi) true
+    uint32_t step = 1u;
+    if (pred(key_float(key0))) {
+        hi = key0;
+        for (;;) {
+            const uint32_t c = hi - kKeyNegInf > step ? hi - step : kKeyNegInf;
+            if (c == kKeyNegInf || !pred(key_float(c))) { lo = c; break; }
+            hi = c;
+            step <<= 1;
+        }
+    } else {
+        lo = key0;
+        for (;;) {
+            const uint32_t c = kKeyPosInf - lo > step ? lo + step : kKeyPosInf;
+            if (c == kKeyPosInf || pred(key_float(c))) { hi = c; break; }
+            lo = c;
+            step <<= 1;
+        }
+    }
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + ((hi - lo) >> 1);
+        if (pred(key_float(mid))) hi = mid;
+        else lo = mid;
+    }
+    return hi;
+}
+
+// Guess of the lower edge of bin c of the window (a, b): the score where
+// c_real * (v a + b) crosses c - 1/2.
+SGSA_HD uint32_t lin_edge_guess(int c, float a, float b) {
+    return float_key(((c - 0.5f) / (float)kLinTop - b) / a);
+}
+
+// (prefix, top) of the keys in [lo, hi]: they all agree on the bits above `top`.
+SGSA_HD void key_range_prefix(uint32_t lo, uint32_t hi, uint32_t &prefix, int &top) {
+    const uint32_t d = lo ^ hi;
+    int t = 0;
+    while (t < 32 && (d >> t)) ++t;
+    top = t;
+    prefix = t >= 32 ? 0u : (lo & ~((1u << t) - 1u));
 }
 
 }  // namespace sgsa

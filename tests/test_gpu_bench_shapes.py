@@ -16,6 +16,8 @@ Index sets against the float64 oracle are exact except for near ties of the k-th
 score (|s - s_k| <= 1e-5 |s_k|), where bf16-input fp32 MMA scores and float64
 scores may order two keys differently.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -146,11 +148,8 @@ def test_decode_configs4_full_size():
     assert min(hits) == 1.0  # every planted key retrieved on every step
 
 
-@pytest.mark.parametrize("T,DI,K,kind", [(1024, 64, 128, "normal"), (2048, 64, 512, "normal"),
-                                         (1536, 128, 256, "shifted"), (1024, 64, 100, "ties"),
-                                         (777, 64, 64, "wide"), (4096, 64, 512, "normal")])
-def test_tc_selector_bit_exact_on_its_own_scores(T, DI, K, kind):
-    g = torch.Generator().manual_seed(T + K)
+def _selector_inputs(T, DI, kind, seed):
+    g = torch.Generator().manual_seed(seed)
     B, H = 1, 2
     iq = torch.randn(B, T, H, DI, generator=g)
     ik = torch.randn(B, T, H, DI, generator=g)
@@ -161,7 +160,21 @@ def test_tc_selector_bit_exact_on_its_own_scores(T, DI, K, kind):
         ik = torch.randint(-2, 3, ik.shape, generator=g).float()
     elif kind == "wide":  # rows whose score scale varies by 2^10
         iq = iq * torch.exp2(torch.randint(-5, 6, (B, T, H, 1), generator=g).float())
-    iq, ik = iq.bfloat16().cuda(), ik.bfloat16().cuda()
+    elif kind == "late_keys":  # keys after the sampled first tile 2^10 larger: window misses
+        ik[:, 64:] *= 1024.0
+    elif kind == "cluster":  # every score close to 64: a few window bins of ~700 keys
+        iq = torch.ones(B, T, H, DI) + 0.02 * iq
+        ik = torch.ones(B, T, H, DI) + 0.02 * ik
+    return iq.bfloat16().cuda(), ik.bfloat16().cuda()
+
+
+@pytest.mark.parametrize("T,DI,K,kind", [(1024, 64, 128, "normal"), (2048, 64, 512, "normal"),
+                                         (1536, 128, 256, "shifted"), (1024, 64, 100, "ties"),
+                                         (777, 64, 64, "wide"), (4096, 64, 512, "normal"),
+                                         (1024, 64, 128, "late_keys"), (2048, 64, 300, "cluster")])
+def test_tc_selector_bit_exact_on_its_own_scores(T, DI, K, kind):
+    B, H = 1, 2
+    iq, ik = _selector_inputs(T, DI, kind, T + K)
     idx = torch.empty(B, H, T, K, dtype=torch.int32, device="cuda")
     sc = torch.zeros(B, H, T, T, dtype=torch.float32, device="cuda")
     lib = _lib.load()
@@ -181,3 +194,20 @@ def test_tc_selector_bit_exact_on_its_own_scores(T, DI, K, kind):
     short = got[~long_rows]
     expect = np.where(np.arange(K)[None, :] < valid[~long_rows][:, None], np.arange(K)[None, :], -1)
     np.testing.assert_array_equal(short, expect)
+
+
+def test_tc_selector_paths_are_exercised():
+    """The refine pass, the plain restart and exact ties all occur on these inputs
+    (counted by the kernel) -- so the bit-exact test above covers them."""
+    lib = _lib.load()
+    counts = (ctypes.c_ulonglong * 4)()
+    seen = {}
+    for kind, T, K in (("cluster", 2048, 300), ("late_keys", 1024, 128), ("ties", 1024, 100)):
+        iq, ik = _selector_inputs(T, 64, kind, 5)
+        _lib.check(lib.sgsa_indexer_stats(counts, 1), "stats")
+        ops.indexer_topk(iq, ik, K)
+        _lib.check(lib.sgsa_indexer_stats(counts, 1), "stats")
+        seen[kind] = list(counts)
+    assert seen["cluster"][0] > 0, seen      # refine pass
+    assert seen["late_keys"][1] > 0, seen    # plain restart
+    assert seen["ties"][3] > 0, seen         # exact ties at the k-th score

@@ -1,4 +1,4 @@
-"""The indexer's key and first-pass digit functions (sgsa_b200/csrc/select_keys.cuh),
+"""The indexer's key and linear-window bin functions (sgsa_b200/csrc/select_keys.cuh),
 compiled for the host and checked for the invariants the exact selection relies on."""
 import os
 import shutil
@@ -9,7 +9,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def test_fast_digit_invariants(tmp_path):
+def test_linear_bin_invariants(tmp_path):
     cxx = shutil.which("g++") or shutil.which("c++")
     if cxx is None:
         pytest.skip("no host C++ compiler")
