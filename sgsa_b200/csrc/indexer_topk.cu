@@ -192,10 +192,10 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 // ---- tcgen05 indexer: bf16 scores on the tensor cores, fp32 in TMEM. --------
 //
 // Warp roles of the 320-thread CTA (one CTA per 128-query tile of one (b, h)):
-//   warp 0  TMA producer: the query tile once, then key tiles into a ring of
-//           shared-memory stages;
+//   warp 0  TMA producer: key tiles into a ring of shared-memory stages;
 //   warp 1  TMEM owner and MMA issuer: S_tile = Q K^T, M=128 (queries) x
-//           N=kN (keys) x K=DI, into one of four TMEM accumulators;
+//           N=kN (keys) x K=DI with the query tile Q in tensor memory (written
+//           once by the epilogue threads), into one of three TMEM accumulators;
 //   warps 2-9  two threads per query row (warps w and w+4 read the same TMEM
 //           lane quarter and split the tile's columns): tcgen05.ld of their
 //           part of the row and the selection work of the pass; the first
@@ -601,20 +601,23 @@ struct TcCfg {
     // 64-key tiles: the tensor-core attention recomputes these scores with the
     // same instruction shapes, which keeps them bit-identical
     static constexpr int kN = 64;                      // keys per tile
-    static constexpr int kStages = 3;
-    static constexpr int kQBytes = 128 * DI * 2;
     static constexpr int kKBytes = kN * DI * 2;
+    static constexpr int kStages = DI == 64 ? 5 : 3;
     static constexpr int kHistBytes = kBins * kRows * 4;
-    static constexpr int kAcc = 4;                     // TMEM accumulator buffers
-    static constexpr int kBars = 2 * kStages + 2 * kAcc + 1;
-    static constexpr size_t kSmem = 1024 + kQBytes + kStages * kKBytes + kHistBytes + kBars * 8;
-    static constexpr int kTmemCols = kAcc * kN;
+    static constexpr int kAcc = 3;                     // TMEM accumulator buffers
+    static constexpr int kBars = 2 * kStages + 2 * kAcc;
+    static constexpr size_t kSmem = 1024 + kStages * kKBytes + kHistBytes + kBars * 8;
+    // TMEM: the accumulators, then the query tile (the MMA's A operand: row = lane,
+    // two bf16 per 32-bit column)
+    static constexpr int kTIQ = kAcc * kN;
+    static constexpr int kTmemCols = 256;
+    static_assert(kTIQ + DI / 2 <= kTmemCols, "tensor memory");
     static constexpr int kThreads = 64 + kEpiThreads;
 };
 
 template <int DI>
 __global__ void __launch_bounds__(TcCfg<DI>::kThreads, 2)
-indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                        const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx,
                        uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt,
                        const int32_t *__restrict__ q_tiles, float *__restrict__ dbg_scores) {
@@ -622,12 +625,11 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     using namespace sm100;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    unsigned char *sQ = base;
-    unsigned char *sK = sQ + C::kQBytes;
+    unsigned char *sK = base;
     uint32_t *hist = (uint32_t *)(sK + C::kStages * C::kKBytes);
     uint64_t *bars = (uint64_t *)((unsigned char *)hist + C::kHistBytes);
     uint64_t *full = bars, *empty = bars + C::kStages, *tfull = bars + 2 * C::kStages,
-             *tempty = tfull + C::kAcc, *qbar = tempty + C::kAcc;
+             *tempty = tfull + C::kAcc;
     __shared__ uint32_t s_tmem;
     __shared__ uint32_t s_xch[2][2][kRows];
 
@@ -672,9 +674,7 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], kEpiThreads / 32);
         }
-        mbar_init(qbar, 1);
         fence_barrier_init();
-        prefetch_tmap(&tm_q);
         prefetch_tmap(&tm_k);
     }
     if (warp == 1) tmem_alloc(&s_tmem, C::kTmemCols);
@@ -682,6 +682,29 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    if (epi) {
+        // the query tile into tensor memory: this thread's half of its row, DI/4 values
+        // (rows past T as zeros), as bf16 pairs in DI/4 columns
+        constexpr int kW = DI / 4;  // 32-bit columns per thread
+        uint32_t w[kW];
+        const uint4 *src = reinterpret_cast<const uint4 *>(iq + (((size_t)b * T + t) * H + h) * DI + half * (DI / 2));
+#pragma unroll
+        for (int i = 0; i < kW / 4; ++i) {
+            const uint4 u = has_row ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+            w[4 * i] = u.x; w[4 * i + 1] = u.y; w[4 * i + 2] = u.z; w[4 * i + 3] = u.w;
+        }
+        const uint32_t ta = tmem + ((uint32_t)(quad * 32) << 16) + C::kTIQ + half * kW;
+#pragma unroll
+        for (int c = 0; c < kW / 8; ++c) {
+            uint32_t w8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w8[i] = w[8 * c + i];
+            tmem_st8u(ta + 8 * c, w8);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
     uint32_t it_p = 0, it_m = 0, it_e = 0;
     bool collecting = false;
@@ -691,11 +714,6 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     for (int pass = 0;; ++pass) {
         if (warp == 0) {
             if (lane == 0) {
-                if (pass == 0) {
-                    mbar_arrive_expect_tx(qbar, C::kQBytes);
-                    for (int kb = 0; kb < C::kKB; ++kb)
-                        tma_load_3d(sQ + kb * (128 * 128), &tm_q, qbar, kb * 64, h, b * T + q0);
-                }
                 for (int kt = 0; kt < nkt; ++kt, ++it_p) {
                     const uint32_t st = it_p % C::kStages, ph = (it_p / C::kStages) & 1;
                     mbar_wait(&empty[st], ph ^ 1, wd, 1u);
@@ -709,9 +727,8 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             __syncwarp();
         } else if (warp == 1) {
             if (lane == 0) {
-                if (pass == 0) mbar_wait(qbar, 0, wd, 2u);
                 constexpr uint32_t idesc = idesc_bf16_f32(128, C::kN);
-                const uint32_t qa = smem_u32(sQ);
+                const uint32_t tq = tmem + C::kTIQ;  // A operand in tensor memory
                 for (int kt = 0; kt < nkt; ++kt, ++it_m) {
                     const uint32_t st = it_m % C::kStages, ph = (it_m / C::kStages) & 1;
                     const uint32_t buf = it_m % C::kAcc, bph = (it_m / C::kAcc) & 1;
@@ -723,9 +740,9 @@ indexer_topk_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     for (int kb = 0; kb < C::kKB; ++kb) {
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
-                            const uint64_t ad = sdesc_kmajor_sw128(qa + kb * (128 * 128) + kk * 32);
                             const uint64_t bd = sdesc_kmajor_sw128(ka + kb * (C::kN * 128) + kk * 32);
-                            mma_bf16(tmem + buf * C::kN, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+                            mma_bf16_ts(tmem + buf * C::kN, tq + kb * 32 + kk * 8, bd, idesc,
+                                        (kb | kk) ? 1u : 0u);
                         }
                     }
                     mma_commit(&empty[st]);
@@ -896,10 +913,8 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int
                    int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st,
                    float *dbg_scores = nullptr) {
     using C = TcCfg<DI>;
-    CUtensorMap mq, mk;
-    if (!make_tmap_rows_bf16(&mq, iq, B, T, H, DI, 128) ||
-        !make_tmap_rows_bf16(&mk, ik, B, T, H, DI, C::kN))
-        return cudaErrorInvalidValue;
+    CUtensorMap mk;
+    if (!make_tmap_rows_bf16(&mk, ik, B, T, H, DI, C::kN)) return cudaErrorInvalidValue;
     auto kern = indexer_topk_tc_kernel<DI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)C::kSmem);
@@ -907,8 +922,8 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int
     const int nqt = ceil_div(T, kRows);
     const int ntiles = q_tiles ? n_tiles : nqt;
     if (ntiles <= 0) return cudaSuccess;
-    kern<<<ntiles * B * H, C::kThreads, C::kSmem, st>>>(mq, mk, idx, thr, B, T, H, K, nqt, q_tiles,
-                                                      dbg_scores);
+    kern<<<ntiles * B * H, C::kThreads, C::kSmem, st>>>((const __nv_bfloat16 *)iq, mk, idx, thr, B,
+                                                      T, H, K, nqt, q_tiles, dbg_scores);
     return launched();
 }
 

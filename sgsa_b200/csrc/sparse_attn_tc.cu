@@ -4,23 +4,28 @@
 // scores (written by the tensor-core indexer): column j <= t is selected iff
 // (key(s_tj) & mask) > prefix, or == prefix and j <= cut.  This kernel
 // recomputes the indexer scores with the very same tcgen05 instruction
-// sequence the indexer used (M=128 query rows, N=64 keys, K=64 in four K=16
-// steps, tiles at the same offsets), so the scores -- and the selection -- are
-// bit-identical, and evaluates
+// sequence the indexer used (M=128 query rows from tensor memory, N=64 keys,
+// K=64 in four K=16 steps, tiles at the same offsets), so the scores -- and the
+// selection -- are bit-identical, and evaluates
 //     o_s,t = sum_{j selected} softmax_j(q_t . k_j * scale) v_j
 //     out_t = mix_t * o_s,t + (1 - mix_t) * o_delta,t
 // (modelings/hybrid_dense_delta_topk.py:343-356 and :389-390) over 64-key
 // tiles of the causal prefix: S = Q K^T and O += P V on the tensor cores, the
-// softmax in fp32 with an online maximum.  Work grows with the causal prefix
-// instead of the number of selected rows, but runs at tensor-core rate and
-// reads each K/V tile once per 128 queries instead of once per query.
+// softmax in fp32.  Work grows with the causal prefix instead of the number of
+// selected rows, but runs at tensor-core rate and reads each K/V tile once per
+// 128 queries instead of once per query.
 //
-// P is fed to the PV MMA as bf16 hi + lo parts (p = hi + lo to ~2^-16), so the
-// result keeps fp32-level accuracy with V in bf16; the parts are written with
-// tcgen05.st over the index-score columns the thread has just read and enter the
-// MMA as a tensor-memory A operand.  The softmax reference is a fixed bound
-// (max|q| max|k| scale, from a norm pre-pass) when that keeps p within 2^-120;
-// otherwise the running maximum is updated lazily: O and the row sum are
+// Operands: the query tiles (q and the indexer's iq) sit in tensor memory as the
+// A operand of the score MMAs, so those MMAs read only the key tile from shared
+// memory; P is fed to the PV MMA from shared memory as bf16 hi + lo parts
+// (p = hi + lo to ~2^-16), so the result keeps fp32-level accuracy with V in
+// bf16.  Each softmax group has its own P tiles (K-major, 128-byte swizzle), so
+// the scores of a group's next tile are computed while its PV is pending.
+//
+// The softmax reference is a fixed bound (max|q| max|k| scale, from a norm
+// pre-pass) when that keeps p within 2^-120: then both groups accumulate into one
+// O in tensor memory.  Otherwise (no norm pass, or large norms) group 0 alone
+// takes every key tile with a lazy running maximum: O and the row sum are
 // rescaled only when a tile's maximum exceeds the one in use by more than 2^8,
 // which keeps p <= 256 and is exact.
 //
@@ -29,13 +34,12 @@
 // indexer head 0's vectors and thresholds.
 //
 // Warp roles (96 + 128 kParts kGroups threads, one CTA per (b, h, 128-query tile)):
-// warp 0 TMA, warp 1 TMEM owner + MMA issuer, warp 2 TMA of the values, warps 3..
-// softmax: two groups that take alternate key tiles (each with its own score
-// buffers and its own O accumulator in TMEM, an online softmax each, merged at the
-// end), so that one group's softmax overlaps the other's and the MMAs; kParts
-// threads per query row in each group.  The MMA warp issues event-driven: the
-// scores of a tile once its keys have landed, its buffer is free and the PV two
-// tiles back (whose P shares those TMEM columns) has been issued; PV in order.
+// warp 0 TMA of the (indexer key, key) ring, warp 1 TMEM owner + MMA issuer, warp 2
+// TMA of the value ring, warps 3.. softmax: two groups that take alternate key tiles
+// (each with its own score buffers in TMEM and its own P tiles), kParts threads per
+// query row in each group.  The MMA warp issues event-driven: the scores of a tile
+// once its keys have landed and its buffer has been read, PV in order once P and V
+// are there.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -47,34 +51,38 @@ static __device__ unsigned int g_attn_watchdog;
 
 constexpr int kRowsA = 128;
 constexpr int kNk = 64;                // keys per tile
-constexpr int kGroups = 2;             // softmax groups: alternate key tiles, one O each
+constexpr int kGroups = 2;             // softmax groups: alternate key tiles
 constexpr int kParts = 2;              // threads per query row within a group
 constexpr int kCP = kNk / kParts;      // key columns per thread
 constexpr int kAttnThreads = 96 + 128 * kParts * kGroups;
-constexpr int kKS = 3;                 // stages of the (indexer key, key) ring
-constexpr int kVS = 2;                 // stages of the value ring
+constexpr int kKS = 4;                 // stages of the (indexer key, key) ring
+constexpr int kVS = 3;                 // stages of the value ring
 namespace L {
-constexpr int kQ = 0;                    // Q tile, 2 x 16 KB (K-major, 64-col blocks)
-constexpr int kIQ = kQ + 32768;          // IQ tile 16 KB
-constexpr int kKStage = kIQ + 16384;     // kKS stages x 24 KB: IK 8 KB | K 2 x 8 KB
+constexpr int kKStage = 0;                        // kKS stages x 24 KB: IK 8 KB | K 2 x 8 KB
 constexpr int kKBytes = 24576;
 constexpr int kVStage = kKStage + kKS * kKBytes;  // kVS stages x 16 KB: V 2 x 8 KB
 constexpr int kVBytes = 16384;
-constexpr int kBar = kVStage + kVS * kVBytes;
-constexpr int kXmax = kBar + 256;                            // [group][slot][part][row] floats
-constexpr int kMrow = kXmax + kGroups * 2 * kParts * 128 * 4;  // [group][row]
+constexpr int kP = kVStage + kVS * kVBytes;       // per group: P hi 16 KB | P lo 16 KB
+constexpr int kPBytes = 32768;
+constexpr int kBar = kP + kGroups * kPBytes;
+constexpr int kXmax = kBar + 256;                            // [slot][part][row] floats
+constexpr int kMrow = kXmax + 2 * kParts * 128 * 4;          // [group][row]
 constexpr int kLrow = kMrow + kGroups * 128 * 4;             // [group][part][row]
 constexpr int kBytes = kLrow + kGroups * kParts * 128 * 4;
 constexpr size_t kSmem = 1024 + kBytes;
 }  // namespace L
 static_assert(L::kSmem <= 232448, "shared memory");
 
+// TMEM columns (512): O, the query tiles (bf16 pairs), then per group the indexer
+// scores and the scores of its current tile.
+constexpr uint32_t kTO = 0, kTQ = 128, kTIQ = 192, kTSidx = 256, kTS = 384;
+
 template <typename Tmix, typename Tout>
 __global__ void __launch_bounds__(kAttnThreads, 1)
-sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
                       const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
-                      const __grid_constant__ CUtensorMap tm_iq,
+                      const __nv_bfloat16 *__restrict__ iq,
                       const __grid_constant__ CUtensorMap tm_ik, const uint4 *__restrict__ thr,
                       const float *__restrict__ od, const Tmix *__restrict__ mix,
                       Tout *__restrict__ out, int B, int T, int H, float scale_log2,
@@ -85,9 +93,9 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(sm + L::kBar);
-    uint64_t *qfull = bars, *kfull = bars + 1, *kempty = bars + 4, *vfull = bars + 7,
-             *vempty = bars + 9, *sfull = bars + 11, *sfree = bars + 13, *pfull = bars + 15,
-             *pfree = bars + 17;
+    uint64_t *kfull = bars, *kempty = bars + kKS, *vfull = bars + 2 * kKS,
+             *vempty = vfull + kVS, *sfull = vempty + kVS, *sfree = sfull + 2, *pfull = sfree + 2,
+             *pfree = pfull + 2;
     __shared__ uint32_t s_tmem;
     unsigned int *wd = &g_attn_watchdog;
 
@@ -100,8 +108,22 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int q_last = min(T - 1, q0 + kRowsA - 1);
     const int nkt = q_last / kNk + 1;
 
+    // Fixed reference maximum: with |s| <= max|q| max|k| (Cauchy-Schwarz, per head),
+    // bound = max|q| max|k| * scale * log2(e) is >= every x, and when it is <= 60,
+    // p = 2^(x - bound) stays in [2^-120, ~1]: no running maximum, no rescaling of O,
+    // and both groups can share one O.  CTA-uniform.
+    bool use_bound = false;
+    float bound = 0.f;
+    if (qkmax) {
+        const float qm2 = __uint_as_float(qkmax[2 * bh]), km2 = __uint_as_float(qkmax[2 * bh + 1]);
+        bound = sqrtf(qm2) * sqrtf(km2) * scale_log2;
+        use_bound = bound <= 60.f;
+    }
+    // the softmax group of key tile j, and its index among that group's tiles
+    auto group_of = [&](int j) { return use_bound ? (j & 1) : 0; };
+    auto seq_of = [&](int j) { return use_bound ? (j >> 1) : j; };
+
     if (threadIdx.x == 0) {
-        mbar_init(qfull, 1);
         for (int i = 0; i < kKS; ++i) {
             mbar_init(&kfull[i], 1);
             mbar_init(&kempty[i], 1);
@@ -110,7 +132,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             mbar_init(&vfull[i], 1);
             mbar_init(&vempty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {  // per group (= per S / P buffer)
+        for (int i = 0; i < 2; ++i) {  // per score buffer (sfull/sfree) and per group (pfull/pfree)
             mbar_init(&sfull[i], 1);
             mbar_init(&sfree[i], 4 * kParts);
             mbar_init(&pfull[i], 4 * kParts);
@@ -123,15 +145,35 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    // TMEM columns: Sidx[g] at 0/64, S[g] at 128/192, O[g] at 256/384
-    const uint32_t tSidx = tmem, tS = tmem + 128, tO = tmem + 256;
+    if (warp >= 3) {
+        // The query tiles into tensor memory (A operand: row = lane, bf16 pairs in 32-bit
+        // columns): the four warps of a lane quarter take a quarter of each row each.
+        const int w4 = (warp - 3) >> 2, quad = warp & 3;
+        const int t = q0 + quad * 32 + lane;
+        const bool ok = t < T;
+        const uint32_t lq = (uint32_t)(quad * 32) << 16;
+        const uint4 *sq = reinterpret_cast<const uint4 *>(q + (((size_t)b * T + t) * H + h) * D + 32 * w4);
+        const uint4 *si = reinterpret_cast<const uint4 *>(iq + (((size_t)b * T + t) * HI + hi) * 64 + 16 * w4);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            const uint4 u0 = ok ? sq[2 * c] : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 u1 = ok ? sq[2 * c + 1] : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+            tmem_st8u(tmem + lq + kTQ + 16 * w4 + 8 * c, w8);
+        }
+        {
+            const uint4 u0 = ok ? si[0] : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 u1 = ok ? si[1] : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+            tmem_st8u(tmem + lq + kTIQ + 8 * w4, w8);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
 
-    if (warp == 0) {  // producer of the query tiles and the (indexer key, key) ring
+    if (warp == 0) {  // producer of the (indexer key, key) ring
         if (lane == 0) {
-            mbar_arrive_expect_tx(qfull, 32768 + 16384);
-            tma_load_3d(sm + L::kQ, &tm_q, qfull, 0, h, b * T + q0);
-            tma_load_3d(sm + L::kQ + 16384, &tm_q, qfull, 64, h, b * T + q0);
-            tma_load_3d(sm + L::kIQ, &tm_iq, qfull, 0, hi, b * T + q0);
             for (int j = 0; j < nkt; ++j) {
                 const int st = j % kKS;
                 mbar_wait(&kempty[st], ((j / kKS) & 1) ^ 1, wd, 1u);
@@ -161,18 +203,15 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (lane == 0) {
             constexpr uint32_t id_s = idesc_bf16_f32(128, kNk);
             constexpr uint32_t id_pv = idesc_bf16_f32_bmn(128, D);
-            const uint32_t aq = smem_u32(sm + L::kQ), aiq = smem_u32(sm + L::kIQ);
-            mbar_wait(qfull, 0, wd, 2u);
-            // Event-driven issue: S(js) as soon as its key tile has landed and its group has
-            // read S(js - 2); PV(jp), in order, as soon as P(jp) and V(jp) are there.  S can
-            // so run ahead of a group's softmax instead of waiting behind the other's PV.
+            const uint32_t tq = tmem + kTQ, tiq = tmem + kTIQ;
+            // Event-driven issue: S(js) as soon as its key tile has landed and its score
+            // buffer (js & 1) has been read; PV(jp), in order, as soon as P(jp) and V(jp)
+            // are there.
             int js = 0, jp = 0;
             uint32_t idle = 0;
             while (jp < nkt) {
                 bool progress = false;
-                // S(js) overwrites the TMEM columns that hold P(js - 2): only after PV(js - 2)
-                // has been issued (the tensor pipe runs its MMAs in order)
-                if (js < nkt && js < jp + 2) {
+                if (js < nkt) {
                     const int st = js % kKS, buf = js & 1;
                     if (mbar_test_wait(&kfull[st], (js / kKS) & 1) &&
                         mbar_test_wait(&sfree[buf], ((js >> 1) & 1) ^ 1)) {
@@ -180,35 +219,36 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const uint32_t stg = smem_u32(sm + L::kKStage + st * L::kKBytes);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)  // indexer scores: same sequence as the indexer
-                            mma_bf16(tSidx + buf * kNk, sdesc_kmajor_sw128(aiq + kk * 32),
-                                     sdesc_kmajor_sw128(stg + kk * 32), id_s, kk ? 1u : 0u);
+                            mma_bf16_ts(tmem + kTSidx + buf * kNk, tiq + kk * 8,
+                                        sdesc_kmajor_sw128(stg + kk * 32), id_s, kk ? 1u : 0u);
 #pragma unroll
                         for (int kb = 0; kb < 2; ++kb)
 #pragma unroll
                             for (int kk = 0; kk < 4; ++kk)
-                                mma_bf16(tS + buf * kNk, sdesc_kmajor_sw128(aq + kb * 16384 + kk * 32),
-                                         sdesc_kmajor_sw128(stg + 8192 + kb * 8192 + kk * 32), id_s,
-                                         (kb | kk) ? 1u : 0u);
+                                mma_bf16_ts(tmem + kTS + buf * kNk, tq + kb * 32 + kk * 8,
+                                            sdesc_kmajor_sw128(stg + 8192 + kb * 8192 + kk * 32), id_s,
+                                            (kb | kk) ? 1u : 0u);
                         mma_commit(&sfull[buf]);
                         mma_commit(&kempty[st]);
                         ++js;
                         progress = true;
                     }
                 }
-                if (jp < js) {  // PV of tile jp into the O of its group (jp & 1)
-                    const int g = jp & 1, vs = jp % kVS;
+                if (jp < js) {  // PV of tile jp into O
+                    const int g = group_of(jp), vs = jp % kVS;
                     if (mbar_test_wait(&vfull[vs], (jp / kVS) & 1) &&
-                        mbar_test_wait(&pfull[g], (jp >> 1) & 1)) {
+                        mbar_test_wait(&pfull[g], seq_of(jp) & 1)) {
                         tc_fence_after();
                         const uint32_t vq = smem_u32(sm + L::kVStage + vs * L::kVBytes);
-                        // P from TMEM (the group's index-score columns): keys [32 p, 32 p + 32)
-                        // as 16 columns of bf16 pairs, hi at +0, lo at +16 of column 32 p
+                        // P of the group from shared memory (K-major, 128-byte swizzle): the hi
+                        // parts at +0, the lo parts at +16 KB
+                        const uint32_t pq = smem_u32(sm + L::kP + g * L::kPBytes);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
-                            const uint32_t a_hi = tSidx + g * kNk + (kk >> 1) * 32 + (kk & 1) * 8;
                             const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
-                            mma_bf16_ts(tO + g * 128, a_hi, bd, id_pv, ((jp >> 1) | kk) ? 1u : 0u);
-                            mma_bf16_ts(tO + g * 128, a_hi + 16, bd, id_pv, 1u);
+                            mma_bf16(tmem + kTO, sdesc_kmajor_sw128(pq + kk * 32), bd, id_pv,
+                                     (jp | kk) ? 1u : 0u);
+                            mma_bf16(tmem + kTO, sdesc_kmajor_sw128(pq + 16384 + kk * 32), bd, id_pv, 1u);
                         }
                         mma_commit(&pfree[g]);
                         mma_commit(&vempty[vs]);
@@ -229,7 +269,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         __syncwarp();
     } else {
         // Two groups of kParts threads per query row: group g takes key tiles j = g, g+2, ...
-        // into its own S/P buffers and its own O (an online softmax each, merged at the end).
+        // (every tile for group 0 without the fixed bound).
         // Warps 3 + 8 g + 4 p + i: TMEM lane quarter (warp & 3), part p of the tile's columns.
         const int sw = warp - 3, g = sw >> 3, part = (sw >> 2) & 1;
         const int quad = warp & 3, r = quad * 32 + lane;
@@ -250,26 +290,13 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int cut = (int)th.z;
         const float a_thr = mask == 0u ? -INFINITY
                                        : __uint_as_float((prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix);
-        float m_used = -INFINITY, l = 0.f;
-        // Fixed reference maximum: with |s| <= max|q| max|k| (Cauchy-Schwarz, per head),
-        // bound = max|q| max|k| * scale * log2(e) is >= every x, and when it is <= 60,
-        // p = 2^(x - bound) stays in [2^-120, ~1]: no running maximum, no exchange
-        // between the row's threads, no rescaling of O.
-        bool use_bound = false;
-        if (qkmax) {
-            const float qm2 = __uint_as_float(qkmax[2 * bh]), km2 = __uint_as_float(qkmax[2 * bh + 1]);
-            const float bound = sqrtf(qm2) * sqrtf(km2) * scale_log2;
-            if (bound <= 60.f) {
-                use_bound = true;
-                m_used = bound;
-            }
-        }
+        float m_used = use_bound ? bound : -INFINITY, l = 0.f;
         // no row of this warp has a tie cut (the common case): selection is s >= a
         const bool tie_free = __all_sync(0xffffffffu, cut == 0x7fffffff);
-        int n_mine = 0;  // tiles of this group
-        for (int j = g; j < nkt; j += 2, ++n_mine) {
-            const int slot = (j >> 1) & 1;
-            mbar_wait(&sfull[g], (j >> 1) & 1, wd, 32u);
+        const int j0 = use_bound ? g : (g == 0 ? 0 : nkt), jstep = use_bound ? 2 : 1;
+        for (int j = j0; j < nkt; j += jstep) {
+            const int buf = j & 1, n = seq_of(j);
+            mbar_wait(&sfull[buf], (j >> 1) & 1, wd, 32u);
             tc_fence_after();
             float x[kCP];
             float mt = -INFINITY;
@@ -278,20 +305,24 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             // x = the raw score where selected, -inf elsewhere (scaled inside the exponent);
             // off the diagonal and without tie cuts in the warp the test is one compare
             const bool simple = full && tie_free;
-#pragma unroll
-            for (int hf = 0; hf < kCP / 16; ++hf) {
-                float si[16], sv[16];
-                tmem_ld16(tSidx + lrow + g * kNk + part * kCP + hf * 16, si);
-                tmem_ld16(tS + lrow + g * kNk + part * kCP + hf * 16, sv);
+            {
+                // both 32-column loads in flight before one wait
+                uint32_t rsi[32], rsv[32];
+                tmem_ld32_issue(tmem + kTSidx + lrow + buf * kNk + part * kCP, rsi);
+                tmem_ld32_issue(tmem + kTS + lrow + buf * kNk + part * kCP, rsv);
+                tmem_ld_wait(rsi);
+                tmem_ld_wait(rsv);
                 if (simple) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) x[hf * 16 + i] = si[i] >= a_thr ? sv[i] : -INFINITY;
+                    for (int i = 0; i < kCP; ++i)
+                        x[i] = __uint_as_float(rsi[i]) >= a_thr ? __uint_as_float(rsv[i]) : -INFINITY;
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int jj = jb0 + hf * 16 + i;
-                        const bool sel = (full || jj <= t) && (si[i] > a_thr || (si[i] == a_thr && jj <= cut));
-                        x[hf * 16 + i] = sel ? sv[i] : -INFINITY;
+                    for (int i = 0; i < kCP; ++i) {
+                        const int jj = jb0 + i;
+                        const float si = __uint_as_float(rsi[i]);
+                        const bool sel = (full || jj <= t) && (si > a_thr || (si == a_thr && jj <= cut));
+                        x[i] = sel ? __uint_as_float(rsv[i]) : -INFINITY;
                     }
                 }
             }
@@ -302,27 +333,28 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sfree[g]);
-            if (!use_bound) {
-                xmax[((g * 2 + slot) * kParts + part) * 128 + r] = mt;
+            if (lane == 0) mbar_arrive(&sfree[buf]);
+            if (!use_bound) {  // group 0 alone, every tile: lazy running maximum
+                const int slot = j & 1;
+                xmax[(slot * kParts + part) * 128 + r] = mt;
                 asm volatile("bar.sync %0, %1;" ::"r"(gbar), "r"(kParts * 128) : "memory");
 #pragma unroll
                 for (int p2 = 0; p2 < kParts; ++p2)
-                    mt = fmaxf(mt, xmax[((g * 2 + slot) * kParts + p2) * 128 + r]);
+                    mt = fmaxf(mt, xmax[(slot * kParts + p2) * 128 + r]);
                 // lazy maximum: rescale only when this tile's maximum is > m_used + 8
                 const bool grow = mt > m_used + 8.f || (m_used == -INFINITY && mt != -INFINITY);
                 if (__any_sync(0xffffffffu, grow)) {
                     const float m_new = grow ? mt : m_used;
                     const float f = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
                     l *= (grow ? f : 1.f);
-                    if (n_mine > 0) {  // this group's O holds its earlier tiles
-                        mbar_wait(&pfree[g], ((j >> 1) - 1) & 1, wd, 64u);
+                    if (n > 0) {  // O holds the earlier tiles
+                        mbar_wait(&pfree[g], (n - 1) & 1, wd, 64u);
                         tc_fence_after();
                         const float gsc = grow ? f : 1.f;
 #pragma unroll 1
                         for (int c = 0; c < 4; ++c) {
                             float o[16];
-                            const uint32_t oa = tO + g * 128 + lrow + part * 64 + c * 16;
+                            const uint32_t oa = tmem + kTO + lrow + part * 64 + c * 16;
                             tmem_ld16(oa, o);
 #pragma unroll
                             for (int i = 0; i < 16; ++i) o[i] *= gsc;
@@ -333,8 +365,8 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     if (grow) m_used = m_new;
                 }
             }
-            // P = exp2(x - m_used) as bf16 hi + lo pairs into this thread's own index-score
-            // columns (read above): the A operand of PV, straight from TMEM
+            // P = exp2(x - m_used) as bf16 hi + lo parts into the group's P tiles in shared
+            // memory (K-major, 128-byte swizzle): the A operand of PV
             const float mref = (m_used == -INFINITY) ? 0.f : m_used;  // x = -inf -> p = 0
             {
                 uint32_t hw[16], lw[16];
@@ -349,48 +381,46 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                     hw[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lw[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                float pw[32];
+                // the group's previous PV must have read the P tiles before they are rewritten
+                if (n > 0) mbar_wait(&pfree[g], (n - 1) & 1, wd, 128u);
+                unsigned char *ph = sm + L::kP + g * L::kPBytes;
+                const uint32_t rbase = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    pw[u] = __uint_as_float(hw[u]);
-                    pw[16 + u] = __uint_as_float(lw[u]);
+                for (int c4 = 0; c4 < 4; ++c4) {  // 16-byte chunk c holds keys 8c .. 8c + 7
+                    const uint32_t off = rbase + ((uint32_t)((part * 4 + c4) ^ (r & 7)) << 4);
+                    *reinterpret_cast<uint4 *>(ph + off) =
+                        make_uint4(hw[4 * c4], hw[4 * c4 + 1], hw[4 * c4 + 2], hw[4 * c4 + 3]);
+                    *reinterpret_cast<uint4 *>(ph + 16384 + off) =
+                        make_uint4(lw[4 * c4], lw[4 * c4 + 1], lw[4 * c4 + 2], lw[4 * c4 + 3]);
                 }
-                tmem_st32(tSidx + lrow + g * kNk + part * kCP, pw);
+                fence_proxy_async();  // the generic-proxy stores, before the tensor core reads them
             }
-            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&pfull[g]);
         }
-        // merge the groups: out = mix * (sum_g 2^(m_g - m) O_g) / (sum_g 2^(m_g - m) l_g)
-        //                        + (1 - mix) * o_delta
+        // out = mix * O / sum_g (2^(m_g - m) l_g) + (1 - mix) * o_delta: with the fixed bound
+        // both groups share O and m; without it group 1 has no tiles (l = 0)
         lrow_s[(g * kParts + part) * 128 + r] = l;
         if (part == 0) mrow[g * 128 + r] = m_used;
         // (named barriers: 1 and 2 are the groups' per-tile exchanges, 3 this merge)
         asm volatile("bar.sync 3, %0;" ::"r"(kGroups * kParts * 128) : "memory");
-        float mg[kGroups], lg[kGroups];
         float m_all = -INFINITY;
+        float mg[kGroups], lg[kGroups];
 #pragma unroll
         for (int g2 = 0; g2 < kGroups; ++g2) {
             mg[g2] = mrow[g2 * 128 + r];
             lg[g2] = 0.f;
 #pragma unroll
             for (int p2 = 0; p2 < kParts; ++p2) lg[g2] += lrow_s[(g2 * kParts + p2) * 128 + r];
-            m_all = fmaxf(m_all, mg[g2]);
+            if (lg[g2] > 0.f) m_all = fmaxf(m_all, mg[g2]);
         }
-        float wgt[kGroups], lsum = 0.f;
+        float lsum = 0.f;
 #pragma unroll
-        for (int g2 = 0; g2 < kGroups; ++g2) {
-            // a group without tiles (nkt == 1) or without selected keys has l = 0
-            wgt[g2] = (lg[g2] > 0.f) ? exp2f(mg[g2] - m_all) : 0.f;
-            lsum += wgt[g2] * lg[g2];
-        }
+        for (int g2 = 0; g2 < kGroups; ++g2)
+            lsum += (lg[g2] > 0.f) ? exp2f(mg[g2] - m_all) * lg[g2] : 0.f;
         const float inv = (lsum > 0.f) ? 1.f / lsum : 0.f;
-        // wait for the last PV of each group
-#pragma unroll
-        for (int g2 = 0; g2 < kGroups; ++g2) {
-            const int last = (nkt - 1 - g2) >= 0 ? ((nkt - 1 - g2) / 2) * 2 + g2 : -1;
-            if (last >= 0) mbar_wait(&pfree[g2], (last >> 1) & 1, wd, 256u);
-        }
+        // wait for the last PV (the tensor pipe completes them in order)
+        mbar_wait(&pfree[group_of(nkt - 1)], seq_of(nkt - 1) & 1, wd, 256u);
         tc_fence_after();
         const size_t rowq = ((size_t)b * T + t) * H + h;
         const int c0 = (g * kParts + part) * 32;  // this thread's 32 output columns
@@ -398,17 +428,7 @@ sparse_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int hc = 0; hc < 2; ++hc) {
             const int cc = c0 + hc * 16;
             float o[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = 0.f;
-#pragma unroll
-            for (int g2 = 0; g2 < kGroups; ++g2) {
-                if (g2 < nkt) {  // the group's O was written
-                    float og[16];
-                    tmem_ld16(tO + g2 * 128 + lrow + cc, og);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) o[i] = fmaf(wgt[g2], og[i], o[i]);
-                }
-            }
+            tmem_ld16(tmem + kTO + lrow + cc, o);
             if (valid_row) {
                 Tout *dst = out + rowq * D + cc;
 #pragma unroll
@@ -490,11 +510,9 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
                                   int HI, uint32_t *qkmax, cudaStream_t st) {
-    CUtensorMap mq, mk, mv, miq, mik;
-    if (!make_tmap_rows_bf16(&mq, q, B, T, H, 128, 128) ||
-        !make_tmap_rows_bf16(&mk, k, B, T, H, 128, kNk) ||
+    CUtensorMap mk, mv, mik;
+    if (!make_tmap_rows_bf16(&mk, k, B, T, H, 128, kNk) ||
         !make_tmap_rows_bf16(&mv, v, B, T, H, 128, kNk) ||
-        !make_tmap_rows_bf16(&miq, iq, B, T, HI, 64, 128) ||
         !make_tmap_rows_bf16(&mik, ik, B, T, HI, 64, kNk))
         return cudaErrorInvalidValue;
     const int nqt = ceil_div(T, kRowsA);
@@ -516,16 +534,17 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                              (int)L::kSmem);
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
-            mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
-            (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
+            (const __nv_bfloat16 *)q, mk, mv, (const __nv_bfloat16 *)iq, mik, (const uint4 *)thr, od,
+            (const __nv_bfloat16 *)mix, (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
     } else {
         auto kern = sparse_attn_tc_kernel<__nv_bfloat16, __nv_bfloat16>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)L::kSmem);
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
-            mq, mk, mv, miq, mik, (const uint4 *)thr, od, (const __nv_bfloat16 *)mix,
-            (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
+            (const __nv_bfloat16 *)q, mk, mv, (const __nv_bfloat16 *)iq, mik, (const uint4 *)thr, od,
+            (const __nv_bfloat16 *)mix, (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI,
+            qkmax);
     }
     return launched();
 }
