@@ -211,6 +211,18 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
                                 void *norm_scratch, void *stream);
 
 /*
+ * Test support for the tensor-core attention (bf16, D 128, DI 64, T <= 4096,
+ * per-head indexer): runs sgsa_sparse_attn_thresholds (out float32, no gate, the
+ * running-maximum softmax) and also writes the indexer scores it recomputed for
+ * its selection, scores[B,H,T,T] (row t: columns j <= t).  They must equal, bit
+ * for bit, the scores sgsa_indexer_topk_scores reports for the same iq, ik -- the
+ * attention's selection is then exactly the indexer's.  No reference counterpart.
+ */
+int sgsa_sparse_attn_index_scores(const void *q, const void *k, const void *v, const void *iq,
+                                  const void *ik, const uint32_t *thresholds, float *out,
+                                  float *scores, int B, int T, int H, void *stream);
+
+/*
  * Retrieval of the sparse-write SGSA block: k_hat, v_hat [B,T,H,D] (dtype) are
  * the softmax(q_t . k_j * scale)-weighted sums of the selected k and v rows.
  * Replaces the aggregation of SparseRetriever._token_only

@@ -39,6 +39,7 @@ SIGNATURES = {
     "sgsa_indexer_thresholds": (_i, [_vp] * 5 + [_i] * 6 + [_vp]),
     "sgsa_sparse_attn_thresholds": (_i, [_vp] * 7 + [_i] + [_vp] * 3 + [_i] * 6 +
                                     [ctypes.c_float, _i, _i, _vp, _vp]),
+    "sgsa_sparse_attn_index_scores": (_i, [_vp] * 8 + [_i] * 3 + [_vp]),
     "sgsa_sparse_retrieve": (_i, [_vp] * 6 + [_i] * 6 + [ctypes.c_float, _i, _vp]),
     "sgsa_rmsnorm": (_i, [_vp] * 3 + [ctypes.c_longlong, _i, ctypes.c_float, _i, _vp]),
     "sgsa_swiglu": (_i, [_vp] * 2 + [ctypes.c_longlong, _i, _i, _vp]),

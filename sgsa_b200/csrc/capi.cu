@@ -248,6 +248,20 @@ int sgsa_sparse_attn_thresholds(const void *q, const void *k, const void *v, con
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_sparse_attn_index_scores(const void *q, const void *k, const void *v, const void *iq,
+                                  const void *ik, const uint32_t *thresholds, float *out,
+                                  float *scores, int B, int T, int H, void *stream) {
+    if (B < 0 || T < 0 || H < 0 || T > 4096) return SGSA_ERR_SHAPE;
+    if (!sgsa::sparse_attn_tc_eligible(T, 128, 64, SGSA_DTYPE_BF16)) return SGSA_ERR_UNSUPPORTED;
+    if ((size_t)B * T * H == 0) return SGSA_OK;
+    if (!q || !k || !v || !iq || !ik || !thresholds || !out || !scores) return SGSA_ERR_NULL;
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thresholds, nullptr, nullptr, out,
+                                                B, T, H, 1.0f / sqrtf(128.0f), 0, nullptr, 0, true,
+                                                H, nullptr, (cudaStream_t)stream, scores);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
 int sgsa_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *indices,
                          void *k_hat, void *v_hat, int B, int T, int H, int D, int top_k,
                          int idx_heads, float scale, int dtype, void *stream) {

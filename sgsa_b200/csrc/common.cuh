@@ -64,7 +64,8 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  int HI, uint32_t *qkmax, cudaStream_t st);
+                                  int HI, uint32_t *qkmax, cudaStream_t st,
+                                  float *dbg_scores = nullptr);
 cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
                                    void *khat, void *vhat, int B, int T, int H, int D, int K,
                                    float scale, int HI, int dtype, cudaStream_t st);

@@ -195,12 +195,12 @@ __global__ void __launch_bounds__(kRows) topk_select_kernel(const float *__restr
 //   warp 0  TMA producer: key tiles into a ring of shared-memory stages;
 //   warp 1  TMEM owner and MMA issuer: S_tile = Q K^T, M=128 (queries) x
 //           N=kN (keys) x K=DI with the query tile Q in tensor memory (written
-//           once by the epilogue threads), into one of three TMEM accumulators;
+//           once by the epilogue threads), into the TMEM accumulator;
 //   warps 2-9  two threads per query row (warps w and w+4 read the same TMEM
-//           lane quarter and split the tile's columns): tcgen05.ld of their
-//           part of the row and the selection work of the pass; the first
-//           thread of each row also runs the collect pass, which must walk the
-//           row in order.
+//           lane quarter and take alternate 32-column chunks of the tile):
+//           tcgen05.ld of their part of the row and the selection work of the
+//           pass; the first thread of each row also runs the collect pass, which
+//           must walk the row in order.
 // The key stream is replayed once per pass; the tensor cores recompute the
 // identical fp32 scores each time.
 //
@@ -598,13 +598,14 @@ __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ri
 template <int DI>
 struct TcCfg {
     static constexpr int kKB = DI / 64;                // 128-byte K blocks
-    // 64-key tiles: the tensor-core attention recomputes these scores with the
-    // same instruction shapes, which keeps them bit-identical
-    static constexpr int kN = 64;                      // keys per tile
+    // 128-key tiles: the tensor-core attention recomputes these scores with the
+    // same instruction shapes (M=128, N=128, K=16 steps), which keeps them
+    // bit-identical
+    static constexpr int kN = 128;                     // keys per tile
     static constexpr int kKBytes = kN * DI * 2;
-    static constexpr int kStages = DI == 64 ? 5 : 3;
+    static constexpr int kStages = 2;
     static constexpr int kHistBytes = kBins * kRows * 4;
-    static constexpr int kAcc = 3;                     // TMEM accumulator buffers
+    static constexpr int kAcc = 1;                     // TMEM accumulator buffers
     static constexpr int kBars = 2 * kStages + 2 * kAcc;
     static constexpr size_t kSmem = 1024 + kStages * kKBytes + kHistBytes + kBars * 8;
     // TMEM: the accumulators, then the query tile (the MMA's A operand: row = lane,
@@ -771,11 +772,14 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                 mbar_wait(&tfull[buf], bph, wd, 16u);
                 tc_fence_after();
                 const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN;
-                const bool full_tile = (kt + 1) * C::kN <= nvalid;
                 if (!collecting) {
+#pragma unroll 1
+                  for (int ci = 0; ci < C::kN / 64; ++ci) {  // chunks half, half + 2 of the tile
+                    const int c = half + 2 * ci;
                     float v[32];
-                    tmem_ld32(taddr + half * 32, v);
-                    const int jb = kt * C::kN + half * 32;
+                    tmem_ld32(taddr + c * 32, v);
+                    const int jb = kt * C::kN + c * 32;
+                    const bool full_tile = jb + 32 <= nvalid;
                     if (dbg_scores && pass == 0 && has_row) {
                         // test support: the fp32 scores this pass selects from
                         float *dr = dbg_scores + ((size_t)bh * T + t) * T;
@@ -783,7 +787,7 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                         for (int i = 0; i < 32; ++i)
                             if (jb + i < nvalid) dr[jb + i] = v[i];
                     }
-                    if (pass == 0 && kt == 0) {
+                    if (pass == 0 && kt == 0 && ci == 0) {
                         // sample of the first key tile: place every row's window
                         uint32_t amax = 0u;
                         int np = 0, nv = 0;
@@ -833,6 +837,7 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                             else lin_hist1<false>(v, cbase, jb, nvalid, s);
                         }
                     }
+                  }
                 } else if (half == 0) {
 #pragma unroll 1
                     for (int c = 0; c < C::kN / 32; ++c) {
@@ -840,6 +845,7 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                         tmem_ld32(taddr + c * 32, v);
                         const int jb = kt * C::kN + c * 32;
                         if (!collect || jb >= nvalid) continue;
+                        const bool full_tile = jb + 32 <= nvalid;
                         if (full_tile) collect_chunk<true>(v, ring, jb, nvalid, s, pos, taken, lastj);
                         else collect_chunk<false>(v, ring, jb, nvalid, s, pos, taken, lastj);
                         if (out_row) {

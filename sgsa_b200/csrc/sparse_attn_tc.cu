@@ -4,12 +4,12 @@
 // scores (written by the tensor-core indexer): column j <= t is selected iff
 // (key(s_tj) & mask) > prefix, or == prefix and j <= cut.  This kernel
 // recomputes the indexer scores with the very same tcgen05 instruction
-// sequence the indexer used (M=128 query rows from tensor memory, N=64 keys,
+// sequence the indexer used (M=128 query rows from tensor memory, N=128 keys,
 // K=64 in four K=16 steps, tiles at the same offsets), so the scores -- and the
 // selection -- are bit-identical, and evaluates
 //     o_s,t = sum_{j selected} softmax_j(q_t . k_j * scale) v_j
 //     out_t = mix_t * o_s,t + (1 - mix_t) * o_delta,t
-// (modelings/hybrid_dense_delta_topk.py:343-356 and :389-390) over 64-key
+// (modelings/hybrid_dense_delta_topk.py:343-356 and :389-390) over 128-key
 // tiles of the causal prefix: S = Q K^T and O += P V on the tensor cores, the
 // softmax in fp32.  Work grows with the causal prefix instead of the number of
 // selected rows, but runs at tensor-core rate and reads each K/V tile once per
@@ -19,27 +19,27 @@
 // A operand of the score MMAs, so those MMAs read only the key tile from shared
 // memory; P is fed to the PV MMA from shared memory as bf16 hi + lo parts
 // (p = hi + lo to ~2^-16), so the result keeps fp32-level accuracy with V in
-// bf16.  Each softmax group has its own P tiles (K-major, 128-byte swizzle), so
-// the scores of a group's next tile are computed while its PV is pending.
+// bf16.  The score MMAs use N = 128 (two 64-key TMA stages): with N = 64 an MMA
+// instruction took about as long as one with N = 128.  The scores of the next
+// tile are computed as soon as the softmax has read the current ones; P has its
+// own shared-memory tiles.
 //
 // The softmax reference is a fixed bound (max|q| max|k| scale, from a norm
-// pre-pass) when that keeps p within 2^-120: then both groups accumulate into one
-// O in tensor memory.  Otherwise (no norm pass, or large norms) group 0 alone
-// takes every key tile with a lazy running maximum: O and the row sum are
-// rescaled only when a tile's maximum exceeds the one in use by more than 2^8,
-// which keeps p <= 256 and is exact.
+// pre-pass) when that keeps p within 2^-120.  Otherwise (no norm pass, or large
+// norms) a lazy running maximum is kept per row (the row's threads exchange
+// their tile maxima): O and the row sum are rescaled only when a tile's maximum
+// exceeds the one in use by more than 2^8, which keeps p <= 256 and is exact.
 //
 // With HI == 1 (a shared-across-heads indexer, one index set per token as in
 // the DeepSeek indexer of modelings/deepseek_v3_2.py:435-487) every head reads
 // indexer head 0's vectors and thresholds.
 //
-// Warp roles (96 + 128 kParts kGroups threads, one CTA per (b, h, 128-query tile)):
-// warp 0 TMA of the (indexer key, key) ring, warp 1 TMEM owner + MMA issuer, warp 2
-// TMA of the value ring, warps 3.. softmax: two groups that take alternate key tiles
-// (each with its own score buffers in TMEM and its own P tiles), kParts threads per
-// query row in each group.  The MMA warp issues event-driven: the scores of a tile
-// once its keys have landed and its buffer has been read, PV in order once P and V
-// are there.
+// Warp roles (96 + 128 kParts threads, one CTA per (b, h, 128-query tile)): warp 0
+// TMA of the indexer-key and key rings, warp 1 TMEM owner + MMA issuer, warp 2 TMA
+// of the value ring, warps 3.. softmax: kParts threads per query row, 32 keys of
+// each tile each.  The MMA warp issues event-driven: the scores of a tile once its
+// keys have landed and the previous scores have been read, PV in order once P and
+// V are there.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -50,31 +50,36 @@ namespace {
 static __device__ unsigned int g_attn_watchdog;
 
 constexpr int kRowsA = 128;
-constexpr int kNk = 64;                // keys per tile
-constexpr int kGroups = 2;             // softmax groups: alternate key tiles
-constexpr int kParts = 2;              // threads per query row within a group
+constexpr int kNk = 128;               // keys per tile (the N of the score MMAs)
+constexpr int kBlk = 64;               // keys per TMA stage (two stages form a tile)
+constexpr int kParts = 4;              // threads per query row
 constexpr int kCP = kNk / kParts;      // key columns per thread
-constexpr int kAttnThreads = 96 + 128 * kParts * kGroups;
-constexpr int kKS = 4;                 // stages of the (indexer key, key) ring
-constexpr int kVS = 3;                 // stages of the value ring
+constexpr int kSoftThreads = 128 * kParts;
+constexpr int kAttnThreads = 96 + kSoftThreads;
+constexpr int kKS = 4;                 // 64-key stages of the indexer-key and key rings (even)
+constexpr int kVS = 3;                 // 64-key stages of the value ring
 namespace L {
-constexpr int kKStage = 0;                        // kKS stages x 24 KB: IK 8 KB | K 2 x 8 KB
-constexpr int kKBytes = 24576;
-constexpr int kVStage = kKStage + kKS * kKBytes;  // kVS stages x 16 KB: V 2 x 8 KB
+// Three rings of 64-key stages: IK (8 KB), K columns 0-63 (8 KB), K columns 64-127
+// (8 KB); stages 2i and 2i+1 are adjacent, so a 128-key tile is one K-major operand
+// (128 rows, 128-byte swizzle) in each ring.
+constexpr int kIK = 0;
+constexpr int kK0 = kIK + kKS * 8192;
+constexpr int kK1 = kK0 + kKS * 8192;
+constexpr int kVStage = kK1 + kKS * 8192;         // kVS stages x 16 KB: V columns 0-63 | 64-127
 constexpr int kVBytes = 16384;
-constexpr int kP = kVStage + kVS * kVBytes;       // per group: P hi 16 KB | P lo 16 KB
-constexpr int kPBytes = 32768;
-constexpr int kBar = kP + kGroups * kPBytes;
-constexpr int kXmax = kBar + 256;                            // [slot][part][row] floats
-constexpr int kMrow = kXmax + 2 * kParts * 128 * 4;          // [group][row]
-constexpr int kLrow = kMrow + kGroups * 128 * 4;             // [group][part][row]
-constexpr int kBytes = kLrow + kGroups * kParts * 128 * 4;
+constexpr int kP = kVStage + kVS * kVBytes;       // P hi 2 x 16 KB | P lo 2 x 16 KB (64-key blocks)
+constexpr int kPBytes = 65536;
+constexpr int kBar = kP + kPBytes;
+constexpr int kXmax = kBar + 256;                 // [slot][part][row] floats
+constexpr int kLrow = kXmax + 2 * kParts * 128 * 4;  // [part][row]
+constexpr int kBytes = kLrow + kParts * 128 * 4;
 constexpr size_t kSmem = 1024 + kBytes;
 }  // namespace L
 static_assert(L::kSmem <= 232448, "shared memory");
+static_assert(kKS % 2 == 0, "a tile takes two adjacent key stages");
 
-// TMEM columns (512): O, the query tiles (bf16 pairs), then per group the indexer
-// scores and the scores of its current tile.
+// TMEM columns (512): O, the query tiles (bf16 pairs), the indexer scores and the
+// scores of the current tile.
 constexpr uint32_t kTO = 0, kTQ = 128, kTIQ = 192, kTSidx = 256, kTS = 384;
 
 template <typename Tmix, typename Tout>
@@ -87,15 +92,15 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
                       const float *__restrict__ od, const Tmix *__restrict__ mix,
                       Tout *__restrict__ out, int B, int T, int H, float scale_log2,
                       int mix_pc, int nqt, const int32_t *__restrict__ q_tiles, int HI,
-                      const uint32_t *__restrict__ qkmax) {
+                      const uint32_t *__restrict__ qkmax, float *__restrict__ dbg_scores) {
     using namespace sm100;
     constexpr int D = 128;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(sm + L::kBar);
     uint64_t *kfull = bars, *kempty = bars + kKS, *vfull = bars + 2 * kKS,
-             *vempty = vfull + kVS, *sfull = vempty + kVS, *sfree = sfull + 2, *pfull = sfree + 2,
-             *pfree = pfull + 2;
+             *vempty = vfull + kVS, *sfull = vempty + kVS, *sfree = sfull + 1, *pfull = sfree + 1,
+             *pfree = pfull + 1;
     __shared__ uint32_t s_tmem;
     unsigned int *wd = &g_attn_watchdog;
 
@@ -106,22 +111,8 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
     const int hi = (HI == 1) ? 0 : h;  // indexer head: shared by all heads when HI == 1
     const int q0 = qt * kRowsA;
     const int q_last = min(T - 1, q0 + kRowsA - 1);
-    const int nkt = q_last / kNk + 1;
-
-    // Fixed reference maximum: with |s| <= max|q| max|k| (Cauchy-Schwarz, per head),
-    // bound = max|q| max|k| * scale * log2(e) is >= every x, and when it is <= 60,
-    // p = 2^(x - bound) stays in [2^-120, ~1]: no running maximum, no rescaling of O,
-    // and both groups can share one O.  CTA-uniform.
-    bool use_bound = false;
-    float bound = 0.f;
-    if (qkmax) {
-        const float qm2 = __uint_as_float(qkmax[2 * bh]), km2 = __uint_as_float(qkmax[2 * bh + 1]);
-        bound = sqrtf(qm2) * sqrtf(km2) * scale_log2;
-        use_bound = bound <= 60.f;
-    }
-    // the softmax group of key tile j, and its index among that group's tiles
-    auto group_of = [&](int j) { return use_bound ? (j & 1) : 0; };
-    auto seq_of = [&](int j) { return use_bound ? (j >> 1) : j; };
+    const int nkt = q_last / kNk + 1;  // 128-key tiles
+    const int nblk = 2 * nkt;          // 64-key stages
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kKS; ++i) {
@@ -132,12 +123,10 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
             mbar_init(&vfull[i], 1);
             mbar_init(&vempty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {  // per score buffer (sfull/sfree) and per group (pfull/pfree)
-            mbar_init(&sfull[i], 1);
-            mbar_init(&sfree[i], 4 * kParts);
-            mbar_init(&pfull[i], 4 * kParts);
-            mbar_init(&pfree[i], 1);
-        }
+        mbar_init(sfull, 1);
+        mbar_init(sfree, kSoftThreads / 32);
+        mbar_init(pfull, kSoftThreads / 32);
+        mbar_init(pfree, 1);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(&s_tmem, 512);
@@ -172,28 +161,27 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
     __syncthreads();
     tc_fence_after();
 
-    if (warp == 0) {  // producer of the (indexer key, key) ring
+    if (warp == 0) {  // producer of the indexer-key and key rings, 64 keys per stage
         if (lane == 0) {
-            for (int j = 0; j < nkt; ++j) {
+            for (int j = 0; j < nblk; ++j) {
                 const int st = j % kKS;
                 mbar_wait(&kempty[st], ((j / kKS) & 1) ^ 1, wd, 1u);
-                unsigned char *stg = sm + L::kKStage + st * L::kKBytes;
-                mbar_arrive_expect_tx(&kfull[st], L::kKBytes);
-                const int row = b * T + j * kNk;
-                tma_load_3d(stg, &tm_ik, &kfull[st], 0, hi, row);
-                tma_load_3d(stg + 8192, &tm_k, &kfull[st], 0, h, row);
-                tma_load_3d(stg + 16384, &tm_k, &kfull[st], 64, h, row);
+                mbar_arrive_expect_tx(&kfull[st], 3 * 8192);
+                const int row = b * T + j * kBlk;
+                tma_load_3d(sm + L::kIK + st * 8192, &tm_ik, &kfull[st], 0, hi, row);
+                tma_load_3d(sm + L::kK0 + st * 8192, &tm_k, &kfull[st], 0, h, row);
+                tma_load_3d(sm + L::kK1 + st * 8192, &tm_k, &kfull[st], 64, h, row);
             }
         }
         __syncwarp();
     } else if (warp == 2) {  // producer of the value ring
         if (lane == 0) {
-            for (int j = 0; j < nkt; ++j) {
+            for (int j = 0; j < nblk; ++j) {
                 const int st = j % kVS;
                 mbar_wait(&vempty[st], ((j / kVS) & 1) ^ 1, wd, 1u);
                 unsigned char *stg = sm + L::kVStage + st * L::kVBytes;
                 mbar_arrive_expect_tx(&vfull[st], L::kVBytes);
-                const int row = b * T + j * kNk;
+                const int row = b * T + j * kBlk;
                 tma_load_3d(stg, &tm_v, &vfull[st], 0, h, row);
                 tma_load_3d(stg + 8192, &tm_v, &vfull[st], 64, h, row);
             }
@@ -204,54 +192,65 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
             constexpr uint32_t id_s = idesc_bf16_f32(128, kNk);
             constexpr uint32_t id_pv = idesc_bf16_f32_bmn(128, D);
             const uint32_t tq = tmem + kTQ, tiq = tmem + kTIQ;
-            // Event-driven issue: S(js) as soon as its key tile has landed and its score
-            // buffer (js & 1) has been read; PV(jp), in order, as soon as P(jp) and V(jp)
-            // are there.
+            // Event-driven issue: S(js) once its two key stages have landed and the scores
+            // of tile js - 1 have been read; PV(jp), in order, once P(jp) and its two value
+            // stages are there.
             int js = 0, jp = 0;
             uint32_t idle = 0;
             while (jp < nkt) {
                 bool progress = false;
                 if (js < nkt) {
-                    const int st = js % kKS, buf = js & 1;
-                    if (mbar_test_wait(&kfull[st], (js / kKS) & 1) &&
-                        mbar_test_wait(&sfree[buf], ((js >> 1) & 1) ^ 1)) {
+                    const int st = (2 * js) % kKS;  // and st + 1
+                    const uint32_t kph = ((2 * js) / kKS) & 1;
+                    if (mbar_test_wait(&kfull[st], kph) && mbar_test_wait(&kfull[st + 1], kph) &&
+                        mbar_test_wait(sfree, (js & 1) ^ 1)) {
                         tc_fence_after();
-                        const uint32_t stg = smem_u32(sm + L::kKStage + st * L::kKBytes);
+                        const uint32_t aik = smem_u32(sm + L::kIK + st * 8192);
+                        const uint32_t ak0 = smem_u32(sm + L::kK0 + st * 8192);
+                        const uint32_t ak1 = smem_u32(sm + L::kK1 + st * 8192);
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk)  // indexer scores: same sequence as the indexer
-                            mma_bf16_ts(tmem + kTSidx + buf * kNk, tiq + kk * 8,
-                                        sdesc_kmajor_sw128(stg + kk * 32), id_s, kk ? 1u : 0u);
+                            mma_bf16_ts(tmem + kTSidx, tiq + kk * 8, sdesc_kmajor_sw128(aik + kk * 32),
+                                        id_s, kk ? 1u : 0u);
 #pragma unroll
-                        for (int kb = 0; kb < 2; ++kb)
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_bf16_ts(tmem + kTS, tq + kk * 8, sdesc_kmajor_sw128(ak0 + kk * 32), id_s,
+                                        kk ? 1u : 0u);
 #pragma unroll
-                            for (int kk = 0; kk < 4; ++kk)
-                                mma_bf16_ts(tmem + kTS + buf * kNk, tq + kb * 32 + kk * 8,
-                                            sdesc_kmajor_sw128(stg + 8192 + kb * 8192 + kk * 32), id_s,
-                                            (kb | kk) ? 1u : 0u);
-                        mma_commit(&sfull[buf]);
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_bf16_ts(tmem + kTS, tq + 32 + kk * 8, sdesc_kmajor_sw128(ak1 + kk * 32),
+                                        id_s, 1u);
+                        mma_commit(sfull);
                         mma_commit(&kempty[st]);
+                        mma_commit(&kempty[st + 1]);
                         ++js;
                         progress = true;
                     }
                 }
                 if (jp < js) {  // PV of tile jp into O
-                    const int g = group_of(jp), vs = jp % kVS;
-                    if (mbar_test_wait(&vfull[vs], (jp / kVS) & 1) &&
-                        mbar_test_wait(&pfull[g], seq_of(jp) & 1)) {
+                    const int v0 = (2 * jp) % kVS, v1 = (2 * jp + 1) % kVS;
+                    if (mbar_test_wait(&vfull[v0], ((2 * jp) / kVS) & 1) &&
+                        mbar_test_wait(&vfull[v1], ((2 * jp + 1) / kVS) & 1) &&
+                        mbar_test_wait(pfull, jp & 1)) {
                         tc_fence_after();
-                        const uint32_t vq = smem_u32(sm + L::kVStage + vs * L::kVBytes);
-                        // P of the group from shared memory (K-major, 128-byte swizzle): the hi
-                        // parts at +0, the lo parts at +16 KB
-                        const uint32_t pq = smem_u32(sm + L::kP + g * L::kPBytes);
+                        // P from shared memory (K-major, 128-byte swizzle, 64-key blocks): the hi
+                        // parts at +0, the lo parts at +32 KB
+                        const uint32_t pq = smem_u32(sm + L::kP);
 #pragma unroll
-                        for (int kk = 0; kk < 4; ++kk) {
-                            const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
-                            mma_bf16(tmem + kTO, sdesc_kmajor_sw128(pq + kk * 32), bd, id_pv,
-                                     (jp | kk) ? 1u : 0u);
-                            mma_bf16(tmem + kTO, sdesc_kmajor_sw128(pq + 16384 + kk * 32), bd, id_pv, 1u);
+                        for (int blk = 0; blk < 2; ++blk) {
+                            const uint32_t vq = smem_u32(sm + L::kVStage + (blk ? v1 : v0) * L::kVBytes);
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const uint64_t bd = sdesc_mnmajor_sw128(vq + kk * 2048, 8192, 1024);
+                                mma_bf16(tmem + kTO, sdesc_kmajor_sw128(pq + blk * 16384 + kk * 32), bd,
+                                         id_pv, (jp | blk | kk) ? 1u : 0u);
+                                mma_bf16(tmem + kTO, sdesc_kmajor_sw128(pq + 32768 + blk * 16384 + kk * 32),
+                                         bd, id_pv, 1u);
+                            }
                         }
-                        mma_commit(&pfree[g]);
-                        mma_commit(&vempty[vs]);
+                        mma_commit(pfree);
+                        mma_commit(&vempty[v0]);
+                        mma_commit(&vempty[v1]);
                         ++jp;
                         progress = true;
                     }
@@ -268,18 +267,15 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
         }
         __syncwarp();
     } else {
-        // Two groups of kParts threads per query row: group g takes key tiles j = g, g+2, ...
-        // (every tile for group 0 without the fixed bound).
-        // Warps 3 + 8 g + 4 p + i: TMEM lane quarter (warp & 3), part p of the tile's columns.
-        const int sw = warp - 3, g = sw >> 3, part = (sw >> 2) & 1;
+        // kParts threads per query row, every key tile: warps 3 + 4 p + i take TMEM lane
+        // quarter (warp & 3) and keys [32 p, 32 p + 32) of the tile.
+        const int sw = warp - 3, part = sw >> 2;
         const int quad = warp & 3, r = quad * 32 + lane;
         const int t = q0 + r;
         const bool valid_row = t < T;
         const uint32_t lrow = (uint32_t)(quad * 32) << 16;
         float *xmax = (float *)(sm + L::kXmax);
-        float *mrow = (float *)(sm + L::kMrow);
         float *lrow_s = (float *)(sm + L::kLrow);
-        const uint32_t gbar = 1 + g;  // named barrier of the group (kParts * 128 threads)
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
         if (valid_row) th = thr[((size_t)b * HI + hi) * T + t];
         // The threshold as a float: key(s) & mask > prefix, or == prefix and j <= cut, is
@@ -290,13 +286,24 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
         const int cut = (int)th.z;
         const float a_thr = mask == 0u ? -INFINITY
                                        : __uint_as_float((prefix & 0x80000000u) ? (prefix & 0x7fffffffu) : ~prefix);
-        float m_used = use_bound ? bound : -INFINITY, l = 0.f;
+        // Fixed reference maximum: with |s| <= max|q| max|k| (Cauchy-Schwarz, per head),
+        // bound = max|q| max|k| * scale * log2(e) is >= every x, and when it is <= 60,
+        // p = 2^(x - bound) stays in [2^-120, ~1]: no running maximum, no exchange
+        // between the row's threads, no rescaling of O.
+        bool use_bound = false;
+        float m_used = -INFINITY, l = 0.f;
+        if (qkmax) {
+            const float qm2 = __uint_as_float(qkmax[2 * bh]), km2 = __uint_as_float(qkmax[2 * bh + 1]);
+            const float bound = sqrtf(qm2) * sqrtf(km2) * scale_log2;
+            if (bound <= 60.f) {
+                use_bound = true;
+                m_used = bound;
+            }
+        }
         // no row of this warp has a tie cut (the common case): selection is s >= a
         const bool tie_free = __all_sync(0xffffffffu, cut == 0x7fffffff);
-        const int j0 = use_bound ? g : (g == 0 ? 0 : nkt), jstep = use_bound ? 2 : 1;
-        for (int j = j0; j < nkt; j += jstep) {
-            const int buf = j & 1, n = seq_of(j);
-            mbar_wait(&sfull[buf], (j >> 1) & 1, wd, 32u);
+        for (int j = 0; j < nkt; ++j) {
+            mbar_wait(sfull, j & 1, wd, 32u);
             tc_fence_after();
             float x[kCP];
             float mt = -INFINITY;
@@ -308,10 +315,16 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
             {
                 // both 32-column loads in flight before one wait
                 uint32_t rsi[32], rsv[32];
-                tmem_ld32_issue(tmem + kTSidx + lrow + buf * kNk + part * kCP, rsi);
-                tmem_ld32_issue(tmem + kTS + lrow + buf * kNk + part * kCP, rsv);
+                tmem_ld32_issue(tmem + kTSidx + lrow + part * kCP, rsi);
+                tmem_ld32_issue(tmem + kTS + lrow + part * kCP, rsv);
                 tmem_ld_wait(rsi);
                 tmem_ld_wait(rsv);
+                if (dbg_scores && valid_row) {  // test support: the recomputed indexer scores
+                    float *dr = dbg_scores + ((size_t)bh * T + t) * T;
+#pragma unroll
+                    for (int i = 0; i < kCP; ++i)
+                        if (jb0 + i <= t) dr[jb0 + i] = __uint_as_float(rsi[i]);
+                }
                 if (simple) {
 #pragma unroll
                     for (int i = 0; i < kCP; ++i)
@@ -333,11 +346,11 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sfree[buf]);
-            if (!use_bound) {  // group 0 alone, every tile: lazy running maximum
+            if (lane == 0) mbar_arrive(sfree);
+            if (!use_bound) {  // lazy running maximum, shared by the row's threads
                 const int slot = j & 1;
                 xmax[(slot * kParts + part) * 128 + r] = mt;
-                asm volatile("bar.sync %0, %1;" ::"r"(gbar), "r"(kParts * 128) : "memory");
+                asm volatile("bar.sync 1, %0;" ::"r"(kSoftThreads) : "memory");
 #pragma unroll
                 for (int p2 = 0; p2 < kParts; ++p2)
                     mt = fmaxf(mt, xmax[(slot * kParts + p2) * 128 + r]);
@@ -347,14 +360,14 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
                     const float m_new = grow ? mt : m_used;
                     const float f = (m_used == -INFINITY) ? 0.f : exp2f(m_used - m_new);
                     l *= (grow ? f : 1.f);
-                    if (n > 0) {  // O holds the earlier tiles
-                        mbar_wait(&pfree[g], (n - 1) & 1, wd, 64u);
+                    if (j > 0) {  // O holds the earlier tiles
+                        mbar_wait(pfree, (j - 1) & 1, wd, 64u);
                         tc_fence_after();
                         const float gsc = grow ? f : 1.f;
 #pragma unroll 1
-                        for (int c = 0; c < 4; ++c) {
+                        for (int c = 0; c < 2; ++c) {
                             float o[16];
-                            const uint32_t oa = tmem + kTO + lrow + part * 64 + c * 16;
+                            const uint32_t oa = tmem + kTO + lrow + part * 32 + c * 16;
                             tmem_ld16(oa, o);
 #pragma unroll
                             for (int i = 0; i < 16; ++i) o[i] *= gsc;
@@ -365,8 +378,8 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
                     if (grow) m_used = m_new;
                 }
             }
-            // P = exp2(x - m_used) as bf16 hi + lo parts into the group's P tiles in shared
-            // memory (K-major, 128-byte swizzle): the A operand of PV
+            // P = exp2(x - m_used) as bf16 hi + lo parts into the P tiles in shared memory
+            // (K-major, 128-byte swizzle, 64-key blocks): the A operand of PV
             const float mref = (m_used == -INFINITY) ? 0.f : m_used;  // x = -inf -> p = 0
             {
                 uint32_t hw[16], lw[16];
@@ -381,49 +394,35 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
                     hw[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lw[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                // the group's previous PV must have read the P tiles before they are rewritten
-                if (n > 0) mbar_wait(&pfree[g], (n - 1) & 1, wd, 128u);
-                unsigned char *ph = sm + L::kP + g * L::kPBytes;
+                // the previous PV must have read the P tiles before they are rewritten
+                if (j > 0) mbar_wait(pfree, (j - 1) & 1, wd, 128u);
+                unsigned char *ph = sm + L::kP + (part >> 1) * 16384;
                 const uint32_t rbase = (uint32_t)((r >> 3) * 1024 + (r & 7) * 128);
 #pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {  // 16-byte chunk c holds keys 8c .. 8c + 7
-                    const uint32_t off = rbase + ((uint32_t)((part * 4 + c4) ^ (r & 7)) << 4);
+                for (int c4 = 0; c4 < 4; ++c4) {  // 16-byte chunk c holds keys 8c .. 8c + 7 of the block
+                    const uint32_t off = rbase + ((uint32_t)(((part & 1) * 4 + c4) ^ (r & 7)) << 4);
                     *reinterpret_cast<uint4 *>(ph + off) =
                         make_uint4(hw[4 * c4], hw[4 * c4 + 1], hw[4 * c4 + 2], hw[4 * c4 + 3]);
-                    *reinterpret_cast<uint4 *>(ph + 16384 + off) =
+                    *reinterpret_cast<uint4 *>(ph + 32768 + off) =
                         make_uint4(lw[4 * c4], lw[4 * c4 + 1], lw[4 * c4 + 2], lw[4 * c4 + 3]);
                 }
                 fence_proxy_async();  // the generic-proxy stores, before the tensor core reads them
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&pfull[g]);
+            if (lane == 0) mbar_arrive(pfull);
         }
-        // out = mix * O / sum_g (2^(m_g - m) l_g) + (1 - mix) * o_delta: with the fixed bound
-        // both groups share O and m; without it group 1 has no tiles (l = 0)
-        lrow_s[(g * kParts + part) * 128 + r] = l;
-        if (part == 0) mrow[g * 128 + r] = m_used;
-        // (named barriers: 1 and 2 are the groups' per-tile exchanges, 3 this merge)
-        asm volatile("bar.sync 3, %0;" ::"r"(kGroups * kParts * 128) : "memory");
-        float m_all = -INFINITY;
-        float mg[kGroups], lg[kGroups];
-#pragma unroll
-        for (int g2 = 0; g2 < kGroups; ++g2) {
-            mg[g2] = mrow[g2 * 128 + r];
-            lg[g2] = 0.f;
-#pragma unroll
-            for (int p2 = 0; p2 < kParts; ++p2) lg[g2] += lrow_s[(g2 * kParts + p2) * 128 + r];
-            if (lg[g2] > 0.f) m_all = fmaxf(m_all, mg[g2]);
-        }
+        // out = mix * O / l + (1 - mix) * o_delta
+        lrow_s[part * 128 + r] = l;
+        asm volatile("bar.sync 1, %0;" ::"r"(kSoftThreads) : "memory");
         float lsum = 0.f;
 #pragma unroll
-        for (int g2 = 0; g2 < kGroups; ++g2)
-            lsum += (lg[g2] > 0.f) ? exp2f(mg[g2] - m_all) * lg[g2] : 0.f;
+        for (int p2 = 0; p2 < kParts; ++p2) lsum += lrow_s[p2 * 128 + r];
         const float inv = (lsum > 0.f) ? 1.f / lsum : 0.f;
         // wait for the last PV (the tensor pipe completes them in order)
-        mbar_wait(&pfree[group_of(nkt - 1)], seq_of(nkt - 1) & 1, wd, 256u);
+        mbar_wait(pfree, (nkt - 1) & 1, wd, 256u);
         tc_fence_after();
         const size_t rowq = ((size_t)b * T + t) * H + h;
-        const int c0 = (g * kParts + part) * 32;  // this thread's 32 output columns
+        const int c0 = part * 32;  // this thread's 32 output columns
 #pragma unroll 1
         for (int hc = 0; hc < 2; ++hc) {
             const int cc = c0 + hc * 16;
@@ -509,11 +508,11 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  int HI, uint32_t *qkmax, cudaStream_t st) {
+                                  int HI, uint32_t *qkmax, cudaStream_t st, float *dbg_scores) {
     CUtensorMap mk, mv, mik;
-    if (!make_tmap_rows_bf16(&mk, k, B, T, H, 128, kNk) ||
-        !make_tmap_rows_bf16(&mv, v, B, T, H, 128, kNk) ||
-        !make_tmap_rows_bf16(&mik, ik, B, T, HI, 64, kNk))
+    if (!make_tmap_rows_bf16(&mk, k, B, T, H, 128, kBlk) ||
+        !make_tmap_rows_bf16(&mv, v, B, T, H, 128, kBlk) ||
+        !make_tmap_rows_bf16(&mik, ik, B, T, HI, 64, kBlk))
         return cudaErrorInvalidValue;
     const int nqt = ceil_div(T, kRowsA);
     const int ntiles = q_tiles ? n_tiles : nqt;
@@ -535,7 +534,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         if (e != cudaSuccess) return e;
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
             (const __nv_bfloat16 *)q, mk, mv, (const __nv_bfloat16 *)iq, mik, (const uint4 *)thr, od,
-            (const __nv_bfloat16 *)mix, (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax);
+            (const __nv_bfloat16 *)mix, (float *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI, qkmax, dbg_scores);
     } else {
         auto kern = sparse_attn_tc_kernel<__nv_bfloat16, __nv_bfloat16>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -544,7 +543,7 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
         kern<<<ntiles * B * H, kAttnThreads, L::kSmem, st>>>(
             (const __nv_bfloat16 *)q, mk, mv, (const __nv_bfloat16 *)iq, mik, (const uint4 *)thr, od,
             (const __nv_bfloat16 *)mix, (__nv_bfloat16 *)out, B, T, H, sl, mix_pc, nqt, q_tiles, HI,
-            qkmax);
+            qkmax, dbg_scores);
     }
     return launched();
 }

@@ -211,3 +211,32 @@ def test_tc_selector_paths_are_exercised():
     assert seen["cluster"][0] > 0, seen      # refine pass
     assert seen["late_keys"][1] > 0, seen    # plain restart
     assert seen["ties"][3] > 0, seen         # exact ties at the k-th score
+
+
+@pytest.mark.parametrize("T,K,kind", [(1024, 128, "normal"), (2000, 300, "ties"), (777, 64, "wide")])
+def test_attention_recomputes_the_indexer_scores_bit_for_bit(T, K, kind):
+    """The fused attention selects with the indexer's thresholds on scores it
+    recomputes; both kernels use the same MMA sequence, so the scores must be
+    bit-identical (else a near-threshold key could be selected differently)."""
+    iq, ik = _selector_inputs(T, 64, kind, 7)
+    B, H = iq.shape[0], iq.shape[2]
+    g = torch.Generator().manual_seed(8)
+    qkv = [torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g), dim=-1)
+           .bfloat16().cuda() for _ in range(3)]
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    idx = torch.empty(B, H, T, K, dtype=torch.int32, device="cuda")
+    s_idx = torch.full((B, H, T, T), float("nan"), device="cuda")
+    _lib.check(lib.sgsa_indexer_topk_scores(iq.data_ptr(), ik.data_ptr(), idx.data_ptr(),
+                                            s_idx.data_ptr(), B, T, H, 64, K, st), "indexer")
+    thr = ops.indexer_thresholds(iq, ik, K)
+    out = torch.empty(B, T, H, 128, device="cuda")
+    s_att = torch.full((B, H, T, T), float("nan"), device="cuda")
+    _lib.check(lib.sgsa_sparse_attn_index_scores(qkv[0].data_ptr(), qkv[1].data_ptr(),
+                                                 qkv[2].data_ptr(), iq.data_ptr(), ik.data_ptr(),
+                                                 thr.data_ptr(), out.data_ptr(), s_att.data_ptr(),
+                                                 B, T, H, st), "attention")
+    torch.cuda.synchronize()
+    written = ~torch.isnan(s_idx)  # rows the indexer had to select in (t + 1 > K)
+    assert written.sum() > 0
+    assert torch.equal(s_idx[written].view(torch.int32), s_att[written].view(torch.int32))
