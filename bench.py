@@ -430,7 +430,7 @@ def run_decode(args):
     torch.cuda.set_device(0)
     B, H, D, DI, Tc, K, reuse, nplant = 64, 16, 128, 64, 32768, 1024, 4, 256
     steps = args.steps
-    n0 = Tc - (args.warmup + steps + 1)
+    n0 = Tc - (args.warmup + steps + 8 + 1)
     g = torch.Generator(device="cuda").manual_seed(0)
     bf = torch.bfloat16
     kc = torch.nn.functional.normalize(torch.randn(B, Tc, H, D, device="cuda", generator=g), dim=-1).to(bf)
@@ -456,7 +456,6 @@ def run_decode(args):
                 torch.sigmoid(r(B, H, D)).to(bf))
 
     toks = [token(i) for i in range(args.warmup + steps)]
-    hits = []
     for i in range(args.warmup):
         cache.step(*toks[i])
     torch.cuda.synchronize()
@@ -469,12 +468,58 @@ def run_decode(args):
     ms = e0.elapsed_time(e1) / steps
     sel = cache.indices  # [B, H, K]
     hit = (sel == targets[:, None, None].int()).any(-1).float().mean().item()
+
+    # Agreement with the reference on sampled batch rows over `check` more steps: the
+    # reference re-scores the whole cache at every step (modelings/hybrid_dense_delta_topk.py
+    # :343-349), this cache refreshes every `reuse` steps.  Exact index agreement on the
+    # refresh steps, planted-key hits of both on every step, and the CPU time of the
+    # reference's decode path on those rows.
+    from oracle import oracle
+    rows = [0, B // 2 + 5]
+    check = 2 * reuse
+    kc_o, vc_o, ikc_o = kc[rows].cpu(), vc[rows].cpu(), ikc[rows].cpu()
+    st_o = cache.state[rows].cpu().numpy()
+    n_cur = cache.n
+    agree, ref_hits, our_hits = [], [], []
+    cpu_s, cpu_rows = 0.0, 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    for i in range(check):
+        tk = token(steps + args.warmup + i)
+        cache.step(*tk)
+        sub = lambda t: t[rows].cpu()
+        q, k, v, beta, gamma, iq, ik, mix = (sub(t) for t in tk)
+        kc_o[:, n_cur], vc_o[:, n_cur], ikc_o[:, n_cur] = k, v, ik
+        n_cur += 1
+        t0 = time.perf_counter()
+        od, st_o = oracle.sgsa_recurrent(q[:, None], k[:, None], v[:, None], beta[:, None],
+                                         gamma[:, None], initial_state=st_o)
+        ref_idx = oracle.decode_topk(iq, ikc_o, n_cur, K)
+        oracle.decode_attn_mix(q, kc_o, vc_o, ref_idx, od[:, 0], mix)
+        cpu_s += time.perf_counter() - t0
+        cpu_rows += len(rows)
+        ours = cache.indices[rows].cpu().numpy()
+        tg = targets[rows].cpu().numpy()
+        if (cache.steps - 1) % reuse == 0:  # a refresh step: the sets must agree
+            agree.append(float((ours == ref_idx).all(-1).mean()))
+        ref_hits.append(float((ref_idx == tg[:, None, None]).any(-1).mean()))
+        our_hits.append(float((ours == tg[:, None, None]).any(-1).mean()))
     print(json.dumps({
         "metric": "SGSA decode tokens/s", "workload": "decode_topk_reuse (configs[4])",
         "value": B / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
         "warmup": args.warmup, "config": {"batch": B, "cache": Tc, "H": H, "d": D, "d_idx": DI,
                                           "top_k": K, "reuse": reuse, "planted": nplant},
-        "retrieval_hit_rate": hit, "dtype": "bf16", "data": "synthetic planted retrieval"}))
+        "retrieval_hit_rate": hit,
+        "agreement": {"rows": rows, "steps": check,
+                      "refresh_index_sets_equal": statistics.mean(agree) if agree else None,
+                      "hit_rate_ours": statistics.mean(our_hits),
+                      "hit_rate_reference": statistics.mean(ref_hits),
+                      "reference": "oracle decode step: recurrence, full re-score top-k every "
+                                   "step, attention + gate (float64)"},
+        "cpu_baseline": {"value": cpu_rows / cpu_s, "unit": "tokens/s",
+                         "cores": os.cpu_count() or 1, "kind": "port",
+                         "sample": f"{len(rows)} batch rows x {check} decode steps of the "
+                                   "float64 restatement (full re-score each step)"},
+        "dtype": "bf16", "data": "synthetic planted retrieval"}))
 
 
 HYBRID_B, HYBRID_T = 8, 4096
