@@ -252,12 +252,15 @@ int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void 
  * iq, ik are [B,T,idx_heads,DI] with idx_heads == H (per-head selection) or 1
  * (one selection per token shared by all heads).
  * The workspace depends on the path the call takes: bf16 with D == 128 and
- * DI in {64, 128} runs the tensor-core indexer and attention and keeps 16-byte
+ * DI == 64 runs the tensor-core indexer and attention and keeps 16-byte
  * selection records per row; every other case keeps B*idx_heads*T*top_k int32
- * index rows.  The delta stage runs on a non-blocking side stream with a fork
- * and a join event, created on the first call of each host thread on each
- * device and reused by that thread's later calls; the call joins it back into
- * `stream` before the gate, so the call is stream-ordered as a whole.
+ * index rows.  The delta stage's per-chunk operands are capped at 1.25 GiB:
+ * beyond that the stage runs in groups of (batch, head) pairs that reuse them.
+ * The delta stage runs on a non-blocking side stream with a fork and a join
+ * event, created on the first call of each host thread on each device and
+ * reused by that thread's later calls; the call joins it back into `stream`
+ * before the attention (which applies the gate), so the call is stream-ordered
+ * as a whole.
  */
 size_t sgsa_layer_fwd_workspace_size(int B, int T, int H, int D, int DI, int idx_heads,
                                      int top_k, int dtype);

@@ -293,12 +293,26 @@ int sgsa_gate_mix(const float *o_s, const float *o_delta, const void *mix, void 
 
 namespace {
 
-// Workspace carving of sgsa_layer_fwd.  The fused path (tensor-core indexer and
-// attention) keeps 16-byte threshold records per row and never an index buffer;
-// the gather path keeps the B*idx_heads*T*K int32 index rows.
+// Workspace carving of sgsa_layer_fwd.  The delta stage's per-chunk operands are
+// bounded by kLayerDeltaCap: larger problems run the delta stage in groups of
+// (batch, head) pairs that reuse one region.  The fused path (tensor-core indexer
+// and attention) keeps 16-byte threshold records per row and never an index
+// buffer; the gather path keeps the B*idx_heads*T*K int32 index rows.
+constexpr size_t kLayerDeltaCap = (size_t)5 << 28;  // 1.25 GiB
+
+// SGSA_LAYER_DELTA_CAP=<bytes> lowers the cap (tests exercise the grouping on small problems).
+size_t layer_delta_cap() {
+    const char *e = getenv("SGSA_LAYER_DELTA_CAP");
+    if (e && e[0]) {
+        const unsigned long long v = strtoull(e, nullptr, 10);
+        if (v > 0 && v < kLayerDeltaCap) return (size_t)v;
+    }
+    return kLayerDeltaCap;
+}
+
 struct LayerPlan {
     bool fused;
-    size_t chunk, od, idx, thr, qkmax, os, total;
+    size_t chunk, od, idx, thr, qkmax, total;
 };
 
 bool layer_fused(int T, int D, int DI, int dtype) {
@@ -310,13 +324,13 @@ LayerPlan layer_plan(int B, int T, int H, int D, int DI, int idx_heads, int top_
     LayerPlan p{};
     p.fused = layer_fused(T, D, DI, dtype);
     const size_t bthd = (size_t)B * T * H * D;
-    p.chunk = align256(sgsa::chunk_delta_ws_bytes(B, T, H, D, 0));
+    const int pairs = sgsa::chunk_delta_group_pairs(B, T, H, D, 0, layer_delta_cap());
+    p.chunk = align256(sgsa::chunk_delta_ws_bytes_pairs(pairs, T, D, 0));
     p.od = align256(bthd * sizeof(float));
     p.idx = p.fused ? 0 : align256((size_t)B * idx_heads * T * top_k * sizeof(int32_t));
     p.thr = p.fused ? align256((size_t)B * idx_heads * T * 16) : 0;
     p.qkmax = p.fused ? align256((size_t)B * H * 2 * sizeof(uint32_t)) : 0;
-    p.os = p.fused ? align256(bthd * sizeof(float)) : 0;
-    p.total = p.chunk + p.od + p.idx + p.thr + p.qkmax + p.os;
+    p.total = p.chunk + p.od + p.idx + p.thr + p.qkmax;
     return p;
 }
 
@@ -353,16 +367,15 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
     int32_t *ix = (int32_t *)(w + p.chunk + p.od);
     uint32_t *thr = (uint32_t *)((char *)ix + p.idx);
     uint32_t *qkmax = (uint32_t *)((char *)thr + p.thr);
-    float *os_ws = (float *)((char *)qkmax + p.qkmax);
     if (indices) ix = indices;
     int flags = SGSA_FLAG_OUT_F32 | (initial_state ? SGSA_FLAG_HAS_INIT : 0) |
                 (final_state ? SGSA_FLAG_STORE_FINAL : 0);
     const float scale = 1.0f / sqrtf((float)D);
     cudaError_t e;
     if (p.fused) {
-        // The delta stage runs on a side stream beside the indexer and the attention
-        // (neither reads its output); the attention writes o_s in fp32 and the gate,
-        // which needs the delta output, joins the two streams.
+        // The delta stage runs on a side stream beside the indexer (which does not read its
+        // output); the streams join before the attention, whose epilogue applies the gate
+        // with the delta output.
         SideStream *ss = side_stream();
         cudaStream_t side = ss ? ss->stream : st;  // without one: in order on the caller's stream
         if (side != st) {
@@ -371,26 +384,23 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
         }
         e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
                                      initial_state, od, final_state, B, T, H, D, dtype, flags, w,
-                                     side);
+                                     side, layer_delta_cap());
         cudaError_t ej = cudaSuccess;
         if (side != st) ej = cudaEventRecord(ss->join, side);
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
             e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, idx_heads, DI, top_k,
                                               nullptr, 0, st);
-        if (e == cudaSuccess)
-            e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, nullptr, nullptr, os_ws, B, T, H,
-                                            scale, mix_per_channel, nullptr, 0, true, idx_heads,
-                                            qkmax, st);
         // always join, so that the caller's stream never runs ahead of the side stream
         if (side != st && ej == cudaSuccess) ej = cudaStreamWaitEvent(st, ss->join, 0);
         if (e != cudaSuccess) return fail_cuda(e);
         if (ej != cudaSuccess) return fail_cuda(ej);
-        e = sgsa::launch_gate_mix(os_ws, od, mix, out, (long long)B * T * H, D, mix_per_channel,
-                                  dtype, st);
+        e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
+                                        mix_per_channel, nullptr, 0, dtype == SGSA_DTYPE_F32,
+                                        idx_heads, qkmax, st);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
     e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr, initial_state,
-                                 od, final_state, B, T, H, D, dtype, flags, w, st);
+                                 od, final_state, B, T, H, D, dtype, flags, w, st, layer_delta_cap());
     if (e != cudaSuccess) return fail_cuda(e);
     e = sgsa::launch_indexer_topk(iq, ik, ix, B, T, idx_heads, DI, top_k, dtype, st);
     if (e != cudaSuccess) return fail_cuda(e);

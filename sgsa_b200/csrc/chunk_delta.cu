@@ -24,6 +24,8 @@
 // memory in fp32.
 #include <stdlib.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
@@ -41,6 +43,7 @@ struct ChunkArgs {
     void *o;
     float *sT;
     int B, T, H, NC;
+    int bh0, nbh;  // this launch's (batch, head) pairs: flattened b*H + h in [bh0, bh0 + nbh)
     float *W, *U, *Aqk, *G;
     float *Qt, *KtT;  // tensor-core scan only: exp(G_t) q_t [C x D] and Kap~^T [D x C]
     int transition;   // tensor-core scan only: v taken as zero, o not written
@@ -67,7 +70,7 @@ __global__ void __launch_bounds__(kThreads) chunk_prep_kernel(ChunkArgs a) {
     __shared__ float sLam[M];
 
     const int c = blockIdx.x, bh = blockIdx.y;
-    const int b = bh / a.H, h = bh % a.H;
+    const int b = (a.bh0 + bh) / a.H, h = (a.bh0 + bh) % a.H;
     const int t0 = c * kC;
     const int L = min(kC, a.T - t0);
     const int tid = threadIdx.x;
@@ -230,13 +233,13 @@ __global__ void __launch_bounds__(kThreads) chunk_scan_kernel(ChunkArgs a) {
     __shared__ float sTail[M];     // exp(G_last - G_tau_m)
 
     const int v0 = blockIdx.x * kBV, bh = blockIdx.y;
-    const int b = bh / a.H, h = bh % a.H;
+    const int gbh = a.bh0 + bh, b = gbh / a.H, h = gbh % a.H;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const Tin *q = (const Tin *)a.q, *k = (const Tin *)a.k, *sk = (const Tin *)a.sk;
 
     for (int e = tid; e < D * kBV; e += kThreads) {
         const int d = e / kBV, vv = e % kBV;
-        S[e] = a.s0 ? a.s0[((size_t)bh * D + d) * D + v0 + vv] : 0.f;
+        S[e] = a.s0 ? a.s0[((size_t)gbh * D + d) * D + v0 + vv] : 0.f;
     }
     for (int c = 0; c < a.NC; ++c) {
         const int t0 = c * kC;
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(kThreads) chunk_scan_kernel(ChunkArgs a) {
     if (a.sT) {
         for (int e = tid; e < D * kBV; e += kThreads) {
             const int d = e / kBV, vv = e % kBV;
-            a.sT[((size_t)bh * D + d) * D + v0 + vv] = S[e];
+            a.sT[((size_t)gbh * D + d) * D + v0 + vv] = S[e];
         }
     }
 }
@@ -312,10 +315,10 @@ cudaError_t run(const ChunkArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Dm::scan_smem);
     if (e != cudaSuccess) return e;
-    prep<<<dim3(a.NC, a.B * a.H), kThreads, Dm::prep_smem, st>>>(a);
+    prep<<<dim3(a.NC, a.nbh), kThreads, Dm::prep_smem, st>>>(a);
     e = launched();
     if (e != cudaSuccess) return e;
-    scan<<<dim3(D / kBV, a.B * a.H), kThreads, Dm::scan_smem, st>>>(a);
+    scan<<<dim3(D / kBV, a.nbh), kThreads, Dm::scan_smem, st>>>(a);
     return launched();
 }
 
@@ -370,7 +373,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
     unsigned int *wd = &g_scan_watchdog;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+    const int bh = blockIdx.x, gbh = a.bh0 + bh, b = gbh / a.H, h = gbh % a.H;
     const int NC = a.NC;
 
     if (threadIdx.x == 0) {
@@ -448,7 +451,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
         for (int k4 = 0; k4 < tc::kD; k4 += 4) {
             float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
             if (a.s0) {
-                const float *s0 = a.s0 + (size_t)bh * tc::kD * tc::kD + v;
+                const float *s0 = a.s0 + (size_t)gbh * tc::kD * tc::kD + v;
                 x = make_float4(s0[(k4 + 0) * tc::kD], s0[(k4 + 1) * tc::kD],
                                 s0[(k4 + 2) * tc::kD], s0[(k4 + 3) * tc::kD]);
             }
@@ -534,7 +537,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
             __syncwarp();
         }
         if (a.sT) {
-            float *sT = a.sT + (size_t)bh * tc::kD * tc::kD + v;
+            float *sT = a.sT + (size_t)gbh * tc::kD * tc::kD + v;
             for (int k = 0; k < tc::kD; ++k)
                 sT[(size_t)k * tc::kD] = *(float *)((unsigned char *)ST + sw128_f32(128, v, k));
         }
@@ -588,7 +591,7 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
     unsigned int *wd = &g_scan_watchdog;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int c0 = blockIdx.x * 2, bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+    const int c0 = blockIdx.x * 2, bh = blockIdx.y, b = (a.bh0 + bh) / a.H, h = (a.bh0 + bh) % a.H;
     const int NC = a.NC, T = a.T;
     const int t0 = c0 * kC;
     const __nv_bfloat16 *beta = (const __nv_bfloat16 *)a.beta,
@@ -859,7 +862,7 @@ static bool scan_use_tc() {
 
 template <typename Tout>
 cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
-    const long long nch = (long long)a.B * a.H * a.NC;
+    const long long nch = (long long)a.nbh * a.NC;
     CUtensorMap mw, mq, ma, mk, mkin, mqin, mvin;
     if (!make_tmap_2d_f32(&mw, a.W, 128, nch * 64, 64) ||
         !make_tmap_2d_f32(&mq, a.Qt, 128, nch * 64, 64) ||
@@ -877,11 +880,11 @@ cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
     e = cudaFuncSetAttribute(scan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmem);
     if (e != cudaSuccess) return e;
     if (!reuse_prep) {
-        prep<<<dim3((a.NC + 1) / 2, a.B * a.H), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
+        prep<<<dim3((a.NC + 1) / 2, a.nbh), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
         e = launched();
         if (e != cudaSuccess) return e;
     }
-    scan<<<a.B * a.H, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
+    scan<<<a.nbh, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
     return launched();
 }
 
@@ -910,7 +913,7 @@ unsigned int read_scan_watchdog(cudaStream_t st) {
     return v;
 }
 
-size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags) {
+size_t chunk_delta_ws_bytes_pairs(long long pairs, int T, int D, int flags) {
     const int M = (flags & SGSA_FLAG_HAS_SPARSE) ? 2 * kC : kC;
     const size_t NC = (size_t)ceil_div(T, kC);
     size_t per = (size_t)2 * M * D + (size_t)kC * M + kC;
@@ -919,16 +922,28 @@ size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags) {
         per += (size_t)2 * kC * D;
         extra = 256;
     }
-    return (size_t)B * H * NC * per * sizeof(float) + extra;
+    return (size_t)pairs * NC * per * sizeof(float) + extra;
+}
+
+size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags) {
+    return chunk_delta_ws_bytes_pairs((long long)B * H, T, D, flags);
+}
+
+int chunk_delta_group_pairs(int B, int T, int H, int D, int flags, size_t cap) {
+    const long long pairs = (long long)B * H;
+    if (cap == 0 || chunk_delta_ws_bytes_pairs(pairs, T, D, flags) <= cap) return (int)pairs;
+    const size_t one = chunk_delta_ws_bytes_pairs(1, T, D, flags);
+    return (int)std::max<long long>(1, std::min<long long>(pairs, (long long)(cap / one)));
 }
 
 cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, const void *beta,
                                const void *gamma, const void *sk, const void *sv,
                                const void *alpha, const float *s0, void *o, float *sT, int B,
                                int T, int H, int D, int dtype, int flags, void *ws,
-                               cudaStream_t st) {
+                               cudaStream_t st, size_t ws_cap) {
     const bool sparse = flags & SGSA_FLAG_HAS_SPARSE;
     const int M = sparse ? 2 * kC : kC;
+    const int group = chunk_delta_group_pairs(B, T, H, D, flags, ws_cap);
     ChunkArgs a;
     a.q = q; a.k = k; a.v = v; a.beta = beta; a.gamma = gamma;
     a.sk = sk; a.sv = sv; a.alpha = alpha;
@@ -936,37 +951,43 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
     a.o = o;
     a.sT = (flags & SGSA_FLAG_STORE_FINAL) ? sT : nullptr;
     a.B = B; a.T = T; a.H = H; a.NC = ceil_div(T, kC);
-    const size_t nchunk = (size_t)B * H * a.NC;
-    a.W = (float *)ws;
-    a.U = a.W + nchunk * M * D;
-    a.Aqk = a.U + nchunk * M * D;
-    a.G = a.Aqk + nchunk * kC * M;
-    a.Qt = nullptr;
-    a.KtT = nullptr;
-    if (D == 128 && !sparse) {
-        float *tail = a.G + nchunk * kC;
-        // keep the fp32 operand arrays 16-byte aligned for TMA
-        tail = (float *)(((uintptr_t)tail + 255) & ~(uintptr_t)255);
-        a.Qt = tail;
-        a.KtT = a.Qt + nchunk * kC * D;
-    }
     a.transition = (flags & SGSA_FLAG_TRANSITION) ? 1 : 0;
-    if (chunk_tc_eligible(D, dtype, flags)) {
-        const bool of32b = (flags & SGSA_FLAG_OUT_F32);
-        const bool reuse = (flags & SGSA_FLAG_REUSE_PREP);
-        return of32b ? run_tc_scan<float>(a, reuse, st) : run_tc_scan<__nv_bfloat16>(a, reuse, st);
-    }
-    a.Qt = nullptr;
-    a.KtT = nullptr;
+    const bool tc = chunk_tc_eligible(D, dtype, flags);
     const bool of32 = (flags & SGSA_FLAG_OUT_F32) || dtype == SGSA_DTYPE_F32;
-    if (dtype == SGSA_DTYPE_F32) {
-        return sparse ? run_d<float, float, true>(D, a, st) : run_d<float, float, false>(D, a, st);
+    // The (batch, head) pairs in groups whose per-chunk operands fit the workspace cap; the
+    // groups run one after the other on `st` and reuse the same workspace.
+    for (int g0 = 0; g0 < B * H; g0 += group) {
+        a.bh0 = g0;
+        a.nbh = std::min(group, B * H - g0);
+        const size_t nchunk = (size_t)a.nbh * a.NC;
+        a.W = (float *)ws;
+        a.U = a.W + nchunk * M * D;
+        a.Aqk = a.U + nchunk * M * D;
+        a.G = a.Aqk + nchunk * kC * M;
+        a.Qt = nullptr;
+        a.KtT = nullptr;
+        cudaError_t e;
+        if (tc) {
+            float *tail = a.G + nchunk * kC;
+            // keep the fp32 operand arrays 16-byte aligned for TMA
+            tail = (float *)(((uintptr_t)tail + 255) & ~(uintptr_t)255);
+            a.Qt = tail;
+            a.KtT = a.Qt + nchunk * kC * D;
+            const bool reuse = (flags & SGSA_FLAG_REUSE_PREP);
+            e = (flags & SGSA_FLAG_OUT_F32) ? run_tc_scan<float>(a, reuse, st)
+                                            : run_tc_scan<__nv_bfloat16>(a, reuse, st);
+        } else if (dtype == SGSA_DTYPE_F32) {
+            e = sparse ? run_d<float, float, true>(D, a, st) : run_d<float, float, false>(D, a, st);
+        } else if (of32) {
+            e = sparse ? run_d<__nv_bfloat16, float, true>(D, a, st)
+                       : run_d<__nv_bfloat16, float, false>(D, a, st);
+        } else {
+            e = sparse ? run_d<__nv_bfloat16, __nv_bfloat16, true>(D, a, st)
+                       : run_d<__nv_bfloat16, __nv_bfloat16, false>(D, a, st);
+        }
+        if (e != cudaSuccess) return e;
     }
-    if (of32)
-        return sparse ? run_d<__nv_bfloat16, float, true>(D, a, st)
-                      : run_d<__nv_bfloat16, float, false>(D, a, st);
-    return sparse ? run_d<__nv_bfloat16, __nv_bfloat16, true>(D, a, st)
-                  : run_d<__nv_bfloat16, __nv_bfloat16, false>(D, a, st);
+    return cudaSuccess;
 }
 
 }  // namespace sgsa

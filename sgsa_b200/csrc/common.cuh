@@ -30,12 +30,16 @@ __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / 
 cudaError_t launched();
 
 // Launch wrappers implemented in the .cu files (all return cudaError_t of the launch).
+// ws_cap > 0: run the (batch, head) pairs in groups whose per-chunk operands fit
+// ws_cap bytes (chunk_delta_group_pairs), one after the other in the same workspace.
 cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, const void *beta,
                                const void *gamma, const void *sk, const void *sv,
                                const void *alpha, const float *s0, void *o, float *sT, int B,
                                int T, int H, int D, int dtype, int flags, void *ws,
-                               cudaStream_t st);
+                               cudaStream_t st, size_t ws_cap = 0);
 size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags);
+size_t chunk_delta_ws_bytes_pairs(long long pairs, int T, int D, int flags);
+int chunk_delta_group_pairs(int B, int T, int H, int D, int flags, size_t cap);
 bool chunk_tc_eligible(int D, int dtype, int flags);
 
 cudaError_t launch_indexer_topk(const void *iq, const void *ik, int32_t *idx, int B, int T,

@@ -423,28 +423,58 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
         tc_fence_after();
         const size_t rowq = ((size_t)b * T + t) * H + h;
         const int c0 = part * 32;  // this thread's 32 output columns
+        // the row's mix when it is one value per row
+        const float mrow_v = (od && mix && !mix_pc && valid_row) ? to_f32(mix[rowq]) : 1.f;
 #pragma unroll 1
         for (int hc = 0; hc < 2; ++hc) {
             const int cc = c0 + hc * 16;
             float o[16];
             tmem_ld16(tmem + kTO + lrow + cc, o);
             if (valid_row) {
-                Tout *dst = out + rowq * D + cc;
+                const size_t e = rowq * D + cc;  // 16 consecutive columns: 16-byte vectors
 #pragma unroll
-                for (int i = 0; i < 16; i += 2) {
-                    float r0 = o[i] * inv, r1 = o[i + 1] * inv;
-                    if (od) {
-                        const size_t e = rowq * D + cc + i;
-                        const float m0 = mix ? to_f32(mix_pc ? mix[e] : mix[rowq]) : 1.f;
-                        const float m1 = mix ? to_f32(mix_pc ? mix[e + 1] : mix[rowq]) : 1.f;
-                        r0 = m0 * r0 + (1.f - m0) * od[e];
-                        r1 = m1 * r1 + (1.f - m1) * od[e + 1];
+                for (int i = 0; i < 16; ++i) o[i] *= inv;
+                if (od) {
+                    float dv[16], mv[16];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 f = reinterpret_cast<const float4 *>(od + e)[i];
+                        dv[4 * i] = f.x; dv[4 * i + 1] = f.y; dv[4 * i + 2] = f.z; dv[4 * i + 3] = f.w;
                     }
-                    if constexpr (sizeof(Tout) == 2) {
-                        *reinterpret_cast<__nv_bfloat162 *>(dst + i) = __floats2bfloat162_rn(r0, r1);
+                    if (mix && mix_pc) {
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const uint4 u = reinterpret_cast<const uint4 *>(mix + e)[i];
+                            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[j]));
+                                mv[8 * i + 2 * j] = f.x;
+                                mv[8 * i + 2 * j + 1] = f.y;
+                            }
+                        }
                     } else {
-                        *reinterpret_cast<float2 *>(dst + i) = make_float2(r0, r1);
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) mv[i] = mrow_v;
                     }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) o[i] = mv[i] * o[i] + (1.f - mv[i]) * dv[i];
+                }
+                if constexpr (sizeof(Tout) == 2) {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const __nv_bfloat162 h2 = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+                        w[i] = *reinterpret_cast<const uint32_t *>(&h2);
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(out + e);
+                    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+                } else {
+                    float4 *dst = reinterpret_cast<float4 *>(out + e);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
                 }
             }
         }

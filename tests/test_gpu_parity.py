@@ -386,3 +386,24 @@ def test_sparse_write_block_matches_oracle(dtype):
                                    vh_dev.cpu(), x["alpha"], x["initial_state"])
     assert oracle.rel_l2(o.float().cpu().numpy(), ro) < TOL[dtype]
     assert oracle.rel_l2(st.float().cpu().numpy(), rs) < TOL[dtype]
+
+
+@pytest.mark.parametrize("dtype,cfgname", [(torch.bfloat16, "bf16"), (torch.float32, "fp32")])
+def test_layer_delta_stage_in_pair_groups_is_identical(dtype, cfgname, monkeypatch):
+    """A workspace cap that splits the delta stage into groups of (batch, head) pairs
+    changes nothing: the same kernels run on each pair."""
+    cfg = CONFIGS["b200_bf16"].scaled(name="groups", B=2, T=1024, H=3, top_k=128, dtype=dtype)
+    if dtype == torch.float32:
+        cfg = cfg.scaled(D=64, d_idx=32)
+    x = make_inputs(cfg, seed=14)
+    d = dev(x)
+    args = (d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["iq"], d["ik"], d["mix"], cfg.top_k)
+    out, st = ops.sgsa_layer_fwd(*args, output_final_state=True)
+    from sgsa_b200 import _lib
+    lib = _lib.load()
+    per_pair = lib.sgsa_chunk_fwd_workspace_size(1, cfg.T, 1, cfg.D, 0)
+    monkeypatch.setenv("SGSA_LAYER_DELTA_CAP", str(2 * per_pair + 256))  # groups of 2 pairs
+    ops.release_workspaces()
+    out2, st2 = ops.sgsa_layer_fwd(*args, output_final_state=True)
+    assert torch.equal(out, out2)
+    assert torch.equal(st, st2)
