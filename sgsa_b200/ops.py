@@ -338,20 +338,26 @@ def sgsa_layer_fwd_from_host(q, k, v, beta, gamma, iq, ik, mix, top_k, device=No
                              out: Optional[Tensor] = None):
     """``sgsa_layer_fwd`` for inputs in host memory: returns the output in host memory.
 
-    The host->device copies run on a side stream in the order the stages consume
+    The host->device copies run on a copy stream in the order the stages consume
     them (indexer vectors, then q/k/v/beta/gamma, then the mix), so they overlap the
-    indexer and the delta stage; the output is copied back on the same stream as the
-    last kernel.  Host tensors should be pinned for the copies to be asynchronous.
+    indexer and the delta stage.  They are ordered after the previous call's copies,
+    not after earlier work of the current stream, so that back-to-back calls overlap
+    one call's copies with the previous call's kernels; a host input written by an
+    asynchronous device->host copy must be synchronised before the call.  The output
+    returns batch by batch on a second copy stream (the link is full duplex), and the
+    current stream waits for it before the call returns, so a synchronisation of the
+    current stream makes ``out`` valid.  Host tensors should be pinned for the copies
+    to be asynchronous.
     """
     dev = torch.device(device) if device is not None else torch.device("cuda",
                                                                         torch.cuda.current_device())
     comp = torch.cuda.current_stream(dev)
-    cs = _copy_streams.get(dev.index)
-    if cs is None:
-        cs = _copy_streams[dev.index] = torch.cuda.Stream(dev)
+    streams = _copy_streams.get(dev.index)
+    if streams is None:
+        streams = _copy_streams[dev.index] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    cs, os_ = streams
     host = dict(iq=iq, ik=ik, q=q, k=k, v=v, beta=beta, gamma=gamma, mix=mix)
     d, ev = {}, {}
-    cs.wait_stream(comp)
     with torch.cuda.stream(cs):
         for n in ("iq", "ik", "q", "k", "v", "beta", "gamma", "mix"):
             d[n] = host[n].to(dev, non_blocking=True)
@@ -370,6 +376,7 @@ def sgsa_layer_fwd_from_host(q, k, v, beta, gamma, iq, ik, mix, top_k, device=No
                              d["mix"], top_k)
         out.copy_(res, non_blocking=True)
         return out
+    os_.wait_stream(comp)  # the previous user of `out` has finished with it
     comp.wait_event(ev["ik"])
     thr = indexer_thresholds(d["iq"], d["ik"], top_k)
     comp.wait_event(ev["gamma"])
@@ -383,11 +390,11 @@ def sgsa_layer_fwd_from_host(q, k, v, beta, gamma, iq, ik, mix, top_k, device=No
                                          d["ik"][sl], thr[sl], od[sl], d["mix"][sl])
         done = torch.cuda.Event()
         done.record(comp)
-        cs.wait_event(done)
-        with torch.cuda.stream(cs):
+        os_.wait_event(done)
+        with torch.cuda.stream(os_):
             out[sl].copy_(res[sl], non_blocking=True)
-    res.record_stream(cs)
-    comp.wait_stream(cs)
+    res.record_stream(os_)
+    comp.wait_stream(os_)
     return out
 
 

@@ -218,9 +218,23 @@ def sp_layer_fwd(q, k, v, beta, gamma, iq, ik, mix, top_k, group=None,
     p, work_rows, own_rows, work_tiles = plan
     ev = (lambda name, st: _mark(timings, name, st)) if timings is not None else (lambda *a: None)
 
+    # All collectives of a process group run in issue order on one NCCL stream, so the
+    # key all-gather and the query all-to-all are issued before the delta stage's state
+    # all-gather, which waits for the first delta pass: issued after it, they would
+    # wait for that pass as well.
+    start = torch.cuda.Event()
+    start.record(comp)
+    # keys of the whole sequence; queries only of this rank's zigzag tiles
+    ev("key_allgather", comp)
+    fk, fv, fik = [_gather_seq(t, world, group) for t in (k, v, ik)]
+    ev("query_alltoall", comp)
+    fq = torch.zeros(B, T, H, D, device=dev, dtype=q.dtype)  # zero rows keep max|q| exact
+    fiq = torch.empty(B, T, iq.shape[2], iq.shape[3], device=dev, dtype=iq.dtype)
+    _all_to_all_rows(q, own_rows, p.own_count, work_rows, p.work_count, fq, group)
+    _all_to_all_rows(iq, own_rows, p.own_count, work_rows, p.work_count, fiq, group)
     # the delta stage runs on its own stream, beside the exchanges, the indexer and
     # the attention; it only joins at the gate
-    dstream.wait_stream(comp)
+    dstream.wait_event(start)
     with torch.cuda.stream(dstream):
         ev("delta_pass1", dstream)
         delta = _Delta(q, k, v, beta, gamma)
@@ -234,14 +248,6 @@ def sp_layer_fwd(q, k, v, beta, gamma, iq, ik, mix, top_k, group=None,
         ev("delta_pass2", dstream)
         o_delta, s_last = delta.pass2(s_in[rank])
         ev("delta_end", dstream)
-    # keys of the whole sequence; queries only of this rank's zigzag tiles
-    ev("key_allgather", comp)
-    fk, fv, fik = [_gather_seq(t, world, group) for t in (k, v, ik)]
-    ev("query_alltoall", comp)
-    fq = torch.zeros(B, T, H, D, device=dev, dtype=q.dtype)  # zero rows keep max|q| exact
-    fiq = torch.empty(B, T, iq.shape[2], iq.shape[3], device=dev, dtype=iq.dtype)
-    _all_to_all_rows(q, own_rows, p.own_count, work_rows, p.work_count, fq, group)
-    _all_to_all_rows(iq, own_rows, p.own_count, work_rows, p.work_count, fiq, group)
     ev("indexer", comp)
     thr = torch.empty(B, iq.shape[2], T, 4, device=dev, dtype=torch.int32)
     ops.indexer_thresholds(fiq, fik, top_k, q_tiles=work_tiles.flip(0), out=thr)
