@@ -383,17 +383,20 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
             const float mref = (m_used == -INFINITY) ? 0.f : m_used;  // x = -inf -> p = 0
             {
                 uint32_t hw[16], lw[16];
+                const float2 sc2 = make_float2(scale_log2, scale_log2), nm2 = make_float2(-mref, -mref);
+                float2 l2s = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
-                    const float p0 = ex2_approx(fmaf(x[2 * u], scale_log2, -mref));
-                    const float p1 = ex2_approx(fmaf(x[2 * u + 1], scale_log2, -mref));
-                    l += p0 + p1;
-                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-                    const float2 hf = __bfloat1622float2(h2);
-                    const __nv_bfloat162 l2 = __floats2bfloat162_rn(p0 - hf.x, p1 - hf.y);
+                    const float2 e2 = fma2(make_float2(x[2 * u], x[2 * u + 1]), sc2, nm2);
+                    const float2 p2 = make_float2(ex2_approx(e2.x), ex2_approx(e2.y));
+                    l2s = add2(l2s, p2);
+                    const __nv_bfloat162 h2 = __floats2bfloat162_rn(p2.x, p2.y);
+                    const float2 lo = sub2(p2, __bfloat1622float2(h2));
+                    const __nv_bfloat162 l2 = __floats2bfloat162_rn(lo.x, lo.y);
                     hw[u] = *reinterpret_cast<const uint32_t *>(&h2);
                     lw[u] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
+                l += l2s.x + l2s.y;
                 // the previous PV must have read the P tiles before they are rewritten
                 if (j > 0) mbar_wait(pfree, (j - 1) & 1, wd, 128u);
                 unsigned char *ph = sm + L::kP + (part >> 1) * 16384;
