@@ -85,6 +85,21 @@ int sgsa_watchdog_status(void *stream);
 int sgsa_watchdog_selftest(unsigned int spin_limit, void *stream);
 
 /*
+ * Bounds-checked debug build (libsgsa_b200_check.so, the same sources compiled
+ * with -DSGSA_CHECK): kernels test the invariants of their index arithmetic --
+ * caller-supplied gather and decode indices within [-1, T), the indexer's
+ * candidate lists within their capacity, exactly top_k collected indices, each
+ * inside its row, a threshold record for every attended row -- record a violated
+ * one as a bit (0x1 gather index, 0x2 decode index, 0x10 candidate capacity,
+ * 0x20 collect count, 0x40 collected index, 0x100 threshold record) and skip the
+ * access it guards.  Synchronises the device and stores the OR of the bits in
+ * *word (cleared when reset != 0).  The release build returns
+ * SGSA_ERR_UNSUPPORTED.  No reference counterpart (a stand-in for running the
+ * kernels under a memory checker).
+ */
+int sgsa_check_status(unsigned int *word, int reset);
+
+/*
  * Chunked SGSA / gated-delta-rule forward.
  * Replaces chunk_sgsa (modelings/sgsa_ops/chunk.py:104-148) and its forward
  * chunk_sgsa_fwd (modelings/sgsa_ops/chunk_fwd.py:12-131), with the semantics of

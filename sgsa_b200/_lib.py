@@ -9,7 +9,9 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libsgsa_b200.so")
+# SGSA_CHECK=1 selects the bounds-checked debug build (same C ABI; see sgsa_check_status)
+CHECK_BUILD = os.environ.get("SGSA_CHECK", "0") == "1"
+LIB_PATH = os.path.join(_HERE, "_lib", "libsgsa_b200_check.so" if CHECK_BUILD else "libsgsa_b200.so")
 
 SGSA_OK = 0
 DTYPE_F32, DTYPE_BF16 = 0, 1
@@ -28,6 +30,7 @@ SIGNATURES = {
     "sgsa_kernel_launches": (ctypes.c_ulonglong, []),
     "sgsa_watchdog_status": (_i, [_vp]),
     "sgsa_watchdog_selftest": (_i, [ctypes.c_uint, _vp]),
+    "sgsa_check_status": (_i, [_vp, _i]),
     "sgsa_chunk_fwd_workspace_size": (_sz, [_i, _i, _i, _i, _i]),
     "sgsa_chunk_fwd": (_i, [_vp] * 11 + [_i] * 7 + [_vp, _sz, _vp]),
     "sgsa_chunk_fwd_noalloc": (_i, [_vp] * 11 + [_i] * 7 + [_vp]),
@@ -67,8 +70,8 @@ def load():
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise ImportError(
-                f"{LIB_PATH} is missing: build it with `python -m sgsa_b200.build` "
-                "(there is no CPU or Python fallback)")
+                f"{LIB_PATH} is missing: build it with `python -m sgsa_b200.build"
+                + (" --check" if CHECK_BUILD else "") + "` (there is no CPU or Python fallback)")
         lib = ctypes.CDLL(LIB_PATH)
         for name, (res, args) in SIGNATURES.items():
             fn = getattr(lib, name)

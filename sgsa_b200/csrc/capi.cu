@@ -116,6 +116,22 @@ int sgsa_watchdog_selftest(unsigned int spin_limit, void *stream) {
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_check_status(unsigned int *word, int reset) {
+    if (!word) return SGSA_ERR_NULL;
+    *word = 0;
+    if (!sgsa::kCheckBuild) return SGSA_ERR_UNSUPPORTED;
+    if (int s = check_device()) return s;
+    const unsigned int w[4] = {sgsa::check_word_gather(reset != 0), sgsa::check_word_decode(reset != 0),
+                               sgsa::check_word_indexer(reset != 0), sgsa::check_word_attn(reset != 0)};
+    unsigned int all = 0;
+    for (unsigned int x : w) {
+        if (x == 0xffffffffu) return fail_cuda(cudaGetLastError());
+        all |= x;
+    }
+    *word = all;
+    return SGSA_OK;
+}
+
 size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags) {
     if (B <= 0 || T <= 0 || H <= 0 || !head_dim_ok(D)) return 0;
     return sgsa::chunk_delta_ws_bytes(B, T, H, D, flags);

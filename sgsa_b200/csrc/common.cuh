@@ -29,6 +29,28 @@ __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / 
 // cudaGetLastError(); every launch site calls it right after its <<<...>>>.
 cudaError_t launched();
 
+// Bounds-checked debug build (compiled with -DSGSA_CHECK into libsgsa_b200_check.so):
+// kernels test the invariants below, record a violated one as a bit of their source
+// file's check word and skip the access it guards; sgsa_check_status() reads the words.
+// In the release build the tests compile away.
+#ifdef SGSA_CHECK
+#define SGSA_CHECK_FAIL(word, code) atomicOr(&(word), (unsigned int)(code))
+constexpr bool kCheckBuild = true;
+#else
+#define SGSA_CHECK_FAIL(word, code) ((void)0)
+constexpr bool kCheckBuild = false;
+#endif
+constexpr unsigned int kChkGatherIndex = 0x1u;     // gather: index outside [-1, T) (or > t)
+constexpr unsigned int kChkDecodeIndex = 0x2u;     // decode: index outside [-1, cache length)
+constexpr unsigned int kChkCandCap = 0x10u;        // indexer: candidate list over capacity
+constexpr unsigned int kChkCollectCount = 0x20u;   // indexer: collect selected != top_k
+constexpr unsigned int kChkCollectIndex = 0x40u;   // indexer: collected index outside the row
+constexpr unsigned int kChkThresholdRecord = 0x100u;  // attention: no threshold record for a row
+unsigned int check_word_gather(bool reset);
+unsigned int check_word_decode(bool reset);
+unsigned int check_word_indexer(bool reset);
+unsigned int check_word_attn(bool reset);
+
 // Launch wrappers implemented in the .cu files (all return cudaError_t of the launch).
 // ws_cap > 0: run the (batch, head) pairs in groups whose per-chunk operands fit
 // ws_cap bytes (chunk_delta_group_pairs), one after the other in the same workspace.

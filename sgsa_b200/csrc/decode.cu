@@ -19,6 +19,8 @@
 namespace sgsa {
 namespace {
 
+static __device__ unsigned int g_check;  // bounds-checked build only
+
 // Load 8 consecutive elements (16 bytes of bf16, 32 of fp32) as floats.
 __device__ __forceinline__ void load8(const __nv_bfloat16 *p, float *x) {
     const uint4 r = __ldg(reinterpret_cast<const uint4 *>(p));
@@ -227,6 +229,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(
     for (int base = 2 * warp; base < K; base += 2 * kAttnWarps) {
         const int s = base + half;
         int j = (s < K) ? ix[s] : -1;
+        if (kCheckBuild && s < K && (j < -1 || j >= Tc)) SGSA_CHECK_FAIL(g_check, kChkDecodeIndex);
         if ((unsigned)j >= (unsigned)Tc) j = -1;  // out-of-range rows count as padding
         float d0 = 0.f;
         float kr[EPL], vr[EPL];
@@ -376,6 +379,14 @@ cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, co
         if (D == 128) return run_dattn<__nv_bfloat16, 128>(q, kc, vc, idx, od, mix, out, B, H, Tc, K, scale, mix_pc, st);
     }
     return cudaErrorInvalidValue;
+}
+
+unsigned int check_word_decode(bool reset) {
+    unsigned int v = 0, z = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_check, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (reset && v) cudaMemcpyToSymbol(g_check, &z, sizeof(z));
+    return v;
 }
 
 }  // namespace sgsa

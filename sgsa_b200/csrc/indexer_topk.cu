@@ -33,6 +33,8 @@ static bool indexer_use_tc() {
 
 namespace {
 
+static __device__ unsigned int g_check;  // bounds-checked build only
+
 constexpr int kRows = 128;       // query rows per CTA (one per thread)
 constexpr int kKeyTile = 64;     // keys per shared-memory tile
 
@@ -405,7 +407,12 @@ __device__ __forceinline__ void cand_resolve(RowSel &s, bool act_row, const uint
     s.done = true;
     s.cand = false;
     if (half == 1) return;
-    const int n1 = (int)xch[0][1][row];
+    int n1 = (int)xch[0][1][row];
+    if (kCheckBuild && (n < 0 || n1 < 0 || n + n1 > kCap)) {  // the two lists overlap
+        SGSA_CHECK_FAIL(g_check, kChkCandCap);
+        n = min(max(n, 0), kCap);
+        n1 = min(max(n1, 0), kCap - n);
+    }
     const uint32_t *back = col + (kCap - 1) * kRows;
     uint32_t x = s.prefix;
     const int need = s.need;
@@ -850,7 +857,12 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                         else collect_chunk<false>(v, ring, jb, nvalid, s, pos, taken, lastj);
                         if (out_row) {
                             for (; flushed < pos; ++flushed)
-                                if (flushed < K) out_row[flushed] = (int32_t)ring[(flushed & 31) * kRows];
+                                if (flushed < K) {
+                                    const uint32_t jv = ring[(flushed & 31) * kRows];
+                                    if (kCheckBuild && jv >= (uint32_t)nvalid)
+                                        SGSA_CHECK_FAIL(g_check, kChkCollectIndex);
+                                    out_row[flushed] = (int32_t)jv;
+                                }
                         }
                     }
                 }
@@ -879,6 +891,7 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                     }
                 }
             } else if (collect) {
+                if (kCheckBuild && pos != K) SGSA_CHECK_FAIL(g_check, kChkCollectCount);
                 if (out_row)
                     for (int i = min(pos, K); i < K; ++i) out_row[i] = -1;
                 // the exact selection as a threshold: key & mask > prefix, or equal and j <= cut
@@ -1041,6 +1054,14 @@ cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_
     if (e != cudaSuccess) return e;
     topk_select_kernel<<<ceil_div(R, kRows), kRows, smem, st>>>(scores, valid, idx, R, S, K);
     return launched();
+}
+
+unsigned int check_word_indexer(bool reset) {
+    unsigned int v = 0, z = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_check, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (reset && v) cudaMemcpyToSymbol(g_check, &z, sizeof(z));
+    return v;
 }
 
 }  // namespace sgsa

@@ -18,6 +18,8 @@
 namespace sgsa {
 namespace {
 
+static __device__ unsigned int g_check;  // bounds-checked build only
+
 constexpr int kWarps = 8;
 
 template <typename T, int N>
@@ -148,6 +150,8 @@ __global__ void __launch_bounds__(kWarps * 32) sparse_attn_mix_kernel(
                 const int slot = p + 2 * u + half;
                 jr[u] = __shfl_sync(0xffffffffu, my, slot & 31);
                 // out-of-range rows (caller-supplied indices) count as padding
+                if (kCheckBuild && slot < cnt && (jr[u] < -1 || jr[u] >= T_))
+                    SGSA_CHECK_FAIL(g_check, kChkGatherIndex);
                 if (slot >= cnt || (unsigned)jr[u] >= (unsigned)T_) jr[u] = -1;
                 if (jr[u] >= 0) {
                     kr[u].load(kb + (size_t)jr[u] * kvstride);
@@ -316,6 +320,14 @@ cudaError_t launch_gate_mix(const float *os, const float *od, const void *mix, v
         gate_mix_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(os, od, (const __nv_bfloat16 *)mix,
                                                              (__nv_bfloat16 *)out, n, D, mix_pc);
     return launched();
+}
+
+unsigned int check_word_gather(bool reset) {
+    unsigned int v = 0, z = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_check, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (reset && v) cudaMemcpyToSymbol(g_check, &z, sizeof(z));
+    return v;
 }
 
 }  // namespace sgsa

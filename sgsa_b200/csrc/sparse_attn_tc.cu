@@ -47,6 +47,8 @@
 namespace sgsa {
 namespace {
 
+static __device__ unsigned int g_check;  // bounds-checked build only
+
 static __device__ unsigned int g_attn_watchdog;
 
 constexpr int kRowsA = 128;
@@ -278,6 +280,7 @@ sparse_attn_tc_kernel(const __nv_bfloat16 *__restrict__ q,
         float *lrow_s = (float *)(sm + L::kLrow);
         uint4 th = make_uint4(0u, 0xffffffffu, 0u, 0u);  // selects nothing
         if (valid_row) th = thr[((size_t)b * HI + hi) * T + t];
+        if (kCheckBuild && valid_row && th.w != 1u) SGSA_CHECK_FAIL(g_check, kChkThresholdRecord);
         // The threshold as a float: key(s) & mask > prefix, or == prefix and j <= cut, is
         // s > a || (s == a && j <= cut) with a the float whose key is the prefix (its
         // unmasked bits are zero; a partial mask always comes with cut = max, which makes
@@ -586,6 +589,14 @@ unsigned int read_attn_watchdog(cudaStream_t st) {
     if (cudaStreamSynchronize(st) != cudaSuccess) return 0xffffffffu;
     if (cudaMemcpyFromSymbol(&v, g_attn_watchdog, sizeof(v)) != cudaSuccess) return 0xffffffffu;
     if (v) cudaMemcpyToSymbol(g_attn_watchdog, &z, sizeof(z));
+    return v;
+}
+
+unsigned int check_word_attn(bool reset) {
+    unsigned int v = 0, z = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyFromSymbol(&v, g_check, sizeof(v)) != cudaSuccess) return 0xffffffffu;
+    if (reset && v) cudaMemcpyToSymbol(g_check, &z, sizeof(z));
     return v;
 }
 

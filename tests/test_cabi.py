@@ -81,3 +81,17 @@ def test_layer_workspace_follows_the_path(lib):
     assert long_ctx < 1 * 65536 * 32 * 2048 * 4
     assert long_ctx < 3 * GB
     assert lib.sgsa_layer_fwd_workspace_size(1, 1024, 4, 64, 32, 3, 128, 0) == 0  # bad idx_heads
+
+
+def test_check_status_is_a_check_build_entry_point(lib):
+    w = ctypes.c_uint(123)
+    assert lib.sgsa_check_status(ctypes.byref(w), 0) == -6  # release build: unsupported
+    assert w.value == 0
+    assert lib.sgsa_check_status(None, 0) == -3
+
+
+def test_bounds_checked_build_exports_the_same_symbols():
+    path = build.build(check=True)
+    chk = ctypes.CDLL(path)
+    for n in header_functions():
+        assert hasattr(chk, n), f"{n} missing from {os.path.basename(path)}"
