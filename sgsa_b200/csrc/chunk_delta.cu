@@ -347,7 +347,8 @@ constexpr int kU = kK + 32768;               // U^T  [128 v][64 tok]   32 KB
 constexpr int kBar = kU + 32768;
 constexpr int kBytes = kBar + 64;
 constexpr size_t kSmem = 1024 + kBytes;
-constexpr uint32_t kOpBytes = 32768 * 3 + 16384;
+constexpr uint32_t kOpWQ = 32768 * 2;         // W and Qt: the first MMA group's operands
+constexpr uint32_t kOpAK = 16384 + 32768;      // Aqk and Kt^T: the second group's
 }  // namespace tc
 
 // Byte offset of fp32 element (r, k) in a K-major 128-byte-swizzled operand of
@@ -368,7 +369,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
     unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(sm + tc::kBar);
     uint64_t *opfull = bars + 0, *d1done = bars + 1, *utready = bars + 2, *d23done = bars + 3,
-             *stready = bars + 4;
+             *stready = bars + 4, *opfull2 = bars + 5;
     __shared__ uint32_t s_tmem;
     unsigned int *wd = &g_scan_watchdog;
 
@@ -382,6 +383,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
         mbar_init(utready, 4);
         mbar_init(d23done, 1);
         mbar_init(stready, 4);
+        mbar_init(opfull2, 1);
         fence_barrier_init();
     }
     if (warp == 1) tmem_alloc(&s_tmem, 256);
@@ -392,17 +394,23 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
 
     if (warp == 0) {
         if (lane == 0) {
+            // Each operand pair is refilled as soon as the MMAs that read it have completed:
+            // W and Qt of chunk c once the first group of chunk c - 1 is done (d1done), Aqk
+            // and Kt^T once its second group is done (d23done), so the loads overlap the
+            // rest of the chunk instead of its epilogue alone.
             for (int c = 0; c < NC; ++c) {
-                if (c > 0) mbar_wait(d23done, (c - 1) & 1, wd, 1u);
                 const int cix = bh * NC + c;
-                mbar_arrive_expect_tx(opfull, tc::kOpBytes);
+                if (c > 0) mbar_wait(d1done, (c - 1) & 1, wd, 1u);
+                mbar_arrive_expect_tx(opfull, tc::kOpWQ);
                 for (int kb = 0; kb < 4; ++kb) {
                     tma_load_2d(sm + tc::kW + kb * 8192, &tm_w, opfull, kb * 32, cix * 64);
                     tma_load_2d(sm + tc::kQ + kb * 8192, &tm_q, opfull, kb * 32, cix * 64);
                 }
+                if (c > 0) mbar_wait(d23done, (c - 1) & 1, wd, 1u);
+                mbar_arrive_expect_tx(opfull2, tc::kOpAK);
                 for (int kb = 0; kb < 2; ++kb) {
-                    tma_load_2d(sm + tc::kA + kb * 8192, &tm_a, opfull, kb * 32, cix * 64);
-                    tma_load_2d(sm + tc::kK + kb * 16384, &tm_k, opfull, kb * 32, cix * 128);
+                    tma_load_2d(sm + tc::kA + kb * 8192, &tm_a, opfull2, kb * 32, cix * 64);
+                    tma_load_2d(sm + tc::kK + kb * 16384, &tm_k, opfull2, kb * 32, cix * 128);
                 }
             }
         }
@@ -429,6 +437,7 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
                     }
                 mma_commit(d1done);
                 mbar_wait(utready, ph, wd, 8u);
+                mbar_wait(opfull2, ph, wd, 4u);
                 tc_fence_after();
                 // D2 += U^T Aqk^T, D3 = U^T Kt   (K = tok = 64: 2 blocks x 4 steps)
                 for (int kb = 0; kb < 2; ++kb)
