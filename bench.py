@@ -429,6 +429,8 @@ def run_decode(args):
 
     torch.cuda.set_device(0)
     B, H, D, DI, Tc, K, reuse, nplant = 64, 16, 128, 64, 32768, 1024, 4, 256
+    if args.B:  # a smaller batch (profiling captures); the metric's configuration is B = 64
+        B = args.B
     steps = args.steps
     n0 = Tc - (args.warmup + steps + 8 + 1)
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -475,7 +477,7 @@ def run_decode(args):
     # refresh steps, planted-key hits of both on every step, and the CPU time of the
     # reference's decode path on those rows.
     from oracle import oracle
-    rows = [0, B // 2 + 5]
+    rows = [0, min(B - 1, B // 2 + 5)]
     check = 2 * reuse
     kc_o, vc_o, ikc_o = kc[rows].cpu(), vc[rows].cpu(), ikc[rows].cpu()
     st_o = cache.state[rows].cpu().numpy()
