@@ -345,7 +345,7 @@ constexpr int kA = kQ + 32768;               // Aqk  [64 t][64 tok]    16 KB
 constexpr int kK = kA + 16384;               // Kt^T [128 dk][64 tok]  32 KB
 constexpr int kU = kK + 32768;               // U^T  [128 v][64 tok]   32 KB
 constexpr int kBar = kU + 32768;
-constexpr int kBytes = kBar + 64;
+constexpr int kBytes = kBar + 128;
 constexpr size_t kSmem = 1024 + kBytes;
 constexpr uint32_t kOpWQ = 32768 * 2;         // W and Qt: the first MMA group's operands
 constexpr uint32_t kOpAK = 16384 + 32768;      // Aqk and Kt^T: the second group's
@@ -359,7 +359,7 @@ __device__ __forceinline__ uint32_t sw128_f32(int rows, int r, int k) {
 }
 
 template <typename Tout>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
 chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
                      const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_a,
@@ -368,8 +368,19 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *sm = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(sm + tc::kBar);
-    uint64_t *opfull = bars + 0, *d1done = bars + 1, *utready = bars + 2, *d23done = bars + 3,
-             *stready = bars + 4, *opfull2 = bars + 5;
+    // opfull / opfull2: W, Qt / Aqk, Kt^T of the chunk landed; d1done: D1 = S^T W^T in TMEM;
+    // wqfree: the MMAs reading W and Qt completed; utready: U^T in shared memory (and this
+    // chunk's Uh read); d3done: D3 = U^T Kt in TMEM; d2done: o^T = D2 complete (and U^T, Aqk,
+    // Kt^T read); stready: the updated state in shared memory; uhready: the chunk's Uh^T in
+    // TMEM; ofree: the chunk's o^T read out of its TMEM buffer.
+    uint64_t *opfull = bars + 0, *d1done = bars + 1, *utready = bars + 2, *d3done = bars + 3,
+             *stready = bars + 4, *opfull2 = bars + 5, *wqfree = bars + 6, *d2done = bars + 7,
+             *uhready = bars + 8, *ofree = bars + 10, *uhfree = bars + 12, *d2out = bars + 14;
+    // uhready, ofree, uhfree, d2out: two each, by chunk parity.  A thread never waits on a
+    // barrier that may have completed two phases past the one it wants (the parity would
+    // read as pending), so the output warps, which may lag the chain by a chunk, wait on
+    // per-parity barriers: uhfree (E1 read Uh of that buffer) and d2out (o^T of that buffer
+    // complete).
     __shared__ uint32_t s_tmem;
     unsigned int *wd = &g_scan_watchdog;
 
@@ -381,32 +392,42 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
         mbar_init(opfull, 1);
         mbar_init(d1done, 1);
         mbar_init(utready, 4);
-        mbar_init(d23done, 1);
+        mbar_init(d3done, 1);
         mbar_init(stready, 4);
         mbar_init(opfull2, 1);
+        mbar_init(wqfree, 1);
+        mbar_init(d2done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&uhready[i], 4);
+            mbar_init(&ofree[i], 4);
+            mbar_init(&uhfree[i], 4);
+            mbar_init(&d2out[i], 1);
+        }
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(&s_tmem, 256);
+    if (warp == 1) tmem_alloc(&s_tmem, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    // TMEM columns: D1 [0, 64), D3 [128, 256), D2 (o^T) [256 + 64 p, 320 + 64 p) and
+    // Uh^T [384 + 64 p, 448 + 64 p) for chunk parity p.
+    constexpr uint32_t kTD1 = 0, kTD3 = 128, kTD2 = 256, kTUh = 384;
 
     if (warp == 0) {
         if (lane == 0) {
             // Each operand pair is refilled as soon as the MMAs that read it have completed:
-            // W and Qt of chunk c once the first group of chunk c - 1 is done (d1done), Aqk
-            // and Kt^T once its second group is done (d23done), so the loads overlap the
-            // rest of the chunk instead of its epilogue alone.
+            // W and Qt of chunk c once chunk c - 1's D1 and S^T Qt^T are done (wqfree), Aqk and
+            // Kt^T once its D3 and U^T Aqk^T are done (d2done).
             for (int c = 0; c < NC; ++c) {
                 const int cix = bh * NC + c;
-                if (c > 0) mbar_wait(d1done, (c - 1) & 1, wd, 1u);
+                if (c > 0) mbar_wait(wqfree, (c - 1) & 1, wd, 1u);
                 mbar_arrive_expect_tx(opfull, tc::kOpWQ);
                 for (int kb = 0; kb < 4; ++kb) {
                     tma_load_2d(sm + tc::kW + kb * 8192, &tm_w, opfull, kb * 32, cix * 64);
                     tma_load_2d(sm + tc::kQ + kb * 8192, &tm_q, opfull, kb * 32, cix * 64);
                 }
-                if (c > 0) mbar_wait(d23done, (c - 1) & 1, wd, 1u);
+                if (c > 0) mbar_wait(d2done, (c - 1) & 1, wd, 1u);
                 mbar_arrive_expect_tx(opfull2, tc::kOpAK);
                 for (int kb = 0; kb < 2; ++kb) {
                     tma_load_2d(sm + tc::kA + kb * 8192, &tm_a, opfull2, kb * 32, cix * 64);
@@ -421,37 +442,51 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
                            qq = smem_u32(sm + tc::kQ), aq = smem_u32(sm + tc::kA),
                            kq = smem_u32(sm + tc::kK), uq = smem_u32(sm + tc::kU);
             constexpr uint32_t id64 = idesc_tf32_f32(128, 64), id128 = idesc_tf32_f32(128, 128);
-            const uint32_t tD1 = tmem, tD2 = tmem + 64, tD3 = tmem + 128;
+            const uint32_t tD1 = tmem + kTD1, tD3 = tmem + kTD3;
+            // The chain that carries the state is S -> D1 -> U -> D3 -> S; the output's MMAs
+            // (S^T Qt^T, U^T Aqk^T) follow the chain's MMA of their group in the in-order
+            // tensor pipe, and o^T leaves TMEM through its own warps.
             for (int c = 0; c < NC; ++c) {
                 const uint32_t ph = c & 1;
+                const uint32_t tD2 = tmem + kTD2 + 64 * ph;
                 mbar_wait(stready, ph, wd, 2u);
                 mbar_wait(opfull, ph, wd, 4u);
                 tc_fence_after();
-                // D1 = S^T W^T, D2 = S^T Qt^T   (K = dk = 128: 4 blocks x 4 steps)
+                // D1 = S^T W^T   (K = dk = 128: 4 blocks x 4 steps)
                 for (int kb = 0; kb < 4; ++kb)
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = sdesc_kmajor_sw128(st + kb * 16384 + kk * 32);
-                        const uint32_t acc = (kb | kk) ? 1u : 0u;
-                        mma_tf32(tD1, ad, sdesc_kmajor_sw128(wq + kb * 8192 + kk * 32), id64, acc);
-                        mma_tf32(tD2, ad, sdesc_kmajor_sw128(qq + kb * 8192 + kk * 32), id64, acc);
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_tf32(tD1, sdesc_kmajor_sw128(st + kb * 16384 + kk * 32),
+                                 sdesc_kmajor_sw128(wq + kb * 8192 + kk * 32), id64, (kb | kk) ? 1u : 0u);
                 mma_commit(d1done);
+                // D2 = S^T Qt^T, into the buffer chunk c - 2's o^T has left
+                if (c >= 2) mbar_wait(&ofree[ph], ((c - 2) >> 1) & 1, wd, 4u);
+                tc_fence_after();
+                for (int kb = 0; kb < 4; ++kb)
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_tf32(tD2, sdesc_kmajor_sw128(st + kb * 16384 + kk * 32),
+                                 sdesc_kmajor_sw128(qq + kb * 8192 + kk * 32), id64, (kb | kk) ? 1u : 0u);
+                mma_commit(wqfree);
                 mbar_wait(utready, ph, wd, 8u);
                 mbar_wait(opfull2, ph, wd, 4u);
                 tc_fence_after();
-                // D2 += U^T Aqk^T, D3 = U^T Kt   (K = tok = 64: 2 blocks x 4 steps)
+                // D3 = U^T Kt   (K = tok = 64: 2 blocks x 4 steps)
                 for (int kb = 0; kb < 2; ++kb)
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = sdesc_kmajor_sw128(uq + kb * 16384 + kk * 32);
-                        mma_tf32(tD2, ad, sdesc_kmajor_sw128(aq + kb * 8192 + kk * 32), id64, 1u);
-                        mma_tf32(tD3, ad, sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32), id128,
-                                 (kb | kk) ? 1u : 0u);
-                    }
-                mma_commit(d23done);
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_tf32(tD3, sdesc_kmajor_sw128(uq + kb * 16384 + kk * 32),
+                                 sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32), id128, (kb | kk) ? 1u : 0u);
+                mma_commit(d3done);
+                // D2 += U^T Aqk^T
+                for (int kb = 0; kb < 2; ++kb)
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_tf32(tD2, sdesc_kmajor_sw128(uq + kb * 16384 + kk * 32),
+                                 sdesc_kmajor_sw128(aq + kb * 8192 + kk * 32), id64, 1u);
+                mma_commit(d2done);
+                mma_commit(&d2out[ph]);
             }
         }
         __syncwarp();
-    } else {
+    } else if (warp < 6) {
+        // the state chain: one thread per state row v (its TMEM lane)
         const int quad = warp & 3, v = quad * 32 + lane;
         const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
         float *ST = (float *)(sm + tc::kSt);
@@ -469,51 +504,46 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(stready);
-        Tout *o = (Tout *)a.o;
         for (int c = 0; c < NC; ++c) {
             const uint32_t ph = c & 1;
-            const int t0 = c * kC, L = min(kC, a.T - t0);
             const size_t cix = (size_t)bh * NC + c;
-            // ---- E1: U^T = Uh^T - S^T W^T
-            const float *Uh = a.U + cix * kC * tc::kD + v;
-            float uh[kC];
-#pragma unroll
-            for (int t = 0; t < kC; ++t) uh[t] = a.transition ? 0.f : Uh[t * tc::kD];
+            const float gl = __expf(a.G[cix * kC + kC - 1]);
+            // ---- E1: U^T = Uh^T - S^T W^T, both from TMEM
+            mbar_wait(&uhready[ph], (c >> 1) & 1, wd, 16u);
             mbar_wait(d1done, ph, wd, 16u);
             tc_fence_after();
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
-                float d[32];
-                tmem_ld32(trow + half * 32, d);
+                uint32_t d[32], u[32];
+                tmem_ld32_issue(trow + kTD1 + half * 32, d);
+                tmem_ld32_issue(trow + kTUh + 64 * ph + half * 32, u);
+                tmem_ld_wait(d);
+                tmem_ld_wait(u);
 #pragma unroll
                 for (int j = 0; j < 32; j += 4) {
                     const int t = half * 32 + j;
-                    *(float4 *)(UT + sw128_f32(128, v, t)) =
-                        make_float4(uh[t] - d[j], uh[t + 1] - d[j + 1], uh[t + 2] - d[j + 2],
-                                    uh[t + 3] - d[j + 3]);
+                    *(float4 *)(UT + sw128_f32(128, v, t)) = make_float4(
+                        __uint_as_float(u[j]) - __uint_as_float(d[j]),
+                        __uint_as_float(u[j + 1]) - __uint_as_float(d[j + 1]),
+                        __uint_as_float(u[j + 2]) - __uint_as_float(d[j + 2]),
+                        __uint_as_float(u[j + 3]) - __uint_as_float(d[j + 3]));
                 }
             }
             fence_proxy_async();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(utready);
-            // ---- E2: o^T = D2, S^T = e^{G_last} S^T + D3
-            const float gl = __expf(a.G[cix * kC + kC - 1]);
-            mbar_wait(d23done, ph, wd, 32u);
+            if (lane == 0) {
+                mbar_arrive(utready);
+                mbar_arrive(&uhfree[ph]);
+            }
+            // ---- E2: S^T = e^{G_last} S^T + D3
+            mbar_wait(d3done, ph, wd, 32u);
             tc_fence_after();
-            // o^T leaves TMEM first (the next chunk's MMAs overwrite it once S is released),
-            // then S (it gates those MMAs), then the o stores; TMEM loads are issued in pairs
-            // and the state is read ahead of the FMAs
-            uint32_t ro0[32], ro1[32];
-            tmem_ld32_issue(trow + 64, ro0);
-            tmem_ld32_issue(trow + 96, ro1);
-            tmem_ld_wait(ro0);
-            tmem_ld_wait(ro1);
 #pragma unroll
             for (int q = 0; q < 4; q += 2) {
                 uint32_t r0[32], r1[32];
-                tmem_ld32_issue(trow + 128 + q * 32, r0);
-                tmem_ld32_issue(trow + 128 + (q + 1) * 32, r1);
+                tmem_ld32_issue(trow + kTD3 + q * 32, r0);
+                tmem_ld32_issue(trow + kTD3 + (q + 1) * 32, r1);
                 float4 x[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -535,26 +565,73 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(stready);
+        }
+        // the final state once the last chunk's MMAs (which read S) have completed
+        mbar_wait(d2done, (NC - 1) & 1, wd, 64u);
+        if (a.sT) {
+            float *sT = a.sT + (size_t)gbh * tc::kD * tc::kD + v;
+            for (int k = 0; k < tc::kD; ++k)
+                sT[(size_t)k * tc::kD] = *(float *)((unsigned char *)ST + sw128_f32(128, v, k));
+        }
+    } else {
+        // output and prefetch warps (same TMEM lane quarters): Uh^T of chunk c + 2 into the
+        // TMEM buffer chunk c has used, and o^T of chunk c out to global memory
+        const int quad = warp & 3, v = quad * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+        Tout *o = (Tout *)a.o;
+        const size_t tstride = (size_t)a.H * tc::kD;
+        auto put_uh = [&](int c) {  // Uh^T[v][t] of chunk c into buffer c & 1
             if (!a.transition) {
+                const float *Uh = a.U + ((size_t)bh * NC + c) * kC * tc::kD + v;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    float u[32];
+#pragma unroll
+                    for (int t = 0; t < 32; ++t) u[t] = Uh[(half * 32 + t) * tc::kD];
+                    tmem_st32(trow + kTUh + 64 * (c & 1) + half * 32, u);
+                }
+            } else {  // the transition scan takes v as zero: Uh = 0
+                float u[32];
+#pragma unroll
+                for (int t = 0; t < 32; ++t) u[t] = 0.f;
+                tmem_st32(trow + kTUh + 64 * (c & 1), u);
+                tmem_st32(trow + kTUh + 64 * (c & 1) + 32, u);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&uhready[c & 1]);
+        };
+        put_uh(0);
+        if (NC > 1) put_uh(1);
+        for (int c = 0; c < NC; ++c) {
+            const uint32_t ph = c & 1;
+            const int t0 = c * kC, L = min(kC, a.T - t0);
+            // E1 of chunk c has read its Uh: chunk c + 2's goes into the same buffer
+            mbar_wait(&uhfree[ph], (c >> 1) & 1, wd, 128u);
+            tc_fence_after();
+            if (c + 2 < NC) put_uh(c + 2);
+            mbar_wait(&d2out[ph], (c >> 1) & 1, wd, 64u);
+            tc_fence_after();
+            if (!a.transition) {
+                uint32_t ro0[32], ro1[32];
+                tmem_ld32_issue(trow + kTD2 + 64 * ph, ro0);
+                tmem_ld32_issue(trow + kTD2 + 64 * ph + 32, ro1);
+                tmem_ld_wait(ro0);
+                tmem_ld_wait(ro1);
                 Tout *op = o + (((size_t)b * a.T + t0) * a.H + h) * tc::kD + v;
-                const size_t tstride = (size_t)a.H * tc::kD;
 #pragma unroll
                 for (int t = 0; t < kC; ++t)
                     if (t < L) op[t * tstride] = from_f32<Tout>(__uint_as_float(t < 32 ? ro0[t] : ro1[t - 32]));
             }
             tc_fence_before();
             __syncwarp();
-        }
-        if (a.sT) {
-            float *sT = a.sT + (size_t)gbh * tc::kD * tc::kD + v;
-            for (int k = 0; k < tc::kD; ++k)
-                sT[(size_t)k * tc::kD] = *(float *)((unsigned char *)ST + sw128_f32(128, v, k));
+            if (lane == 0) mbar_arrive(&ofree[ph]);
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, 256);
+    if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ---- tensor-core prep (bf16 inputs, D = 128, no sparse write) --------------
@@ -893,7 +970,7 @@ cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
         e = launched();
         if (e != cudaSuccess) return e;
     }
-    scan<<<a.nbh, 192, tc::kSmem, st>>>(a, mw, mq, ma, mk);
+    scan<<<a.nbh, 320, tc::kSmem, st>>>(a, mw, mq, ma, mk);
     return launched();
 }
 
