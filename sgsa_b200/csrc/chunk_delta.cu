@@ -324,24 +324,27 @@ cudaError_t run(const ChunkArgs &a, cudaStream_t st) {
 
 // ---- tensor-core scan (bf16 inputs, D = 128, no sparse write) ---------------
 //
-// One CTA per (b, h); the 128x128 fp32 state is kept transposed (S^T[v][dk]) in
-// shared memory as a K-major, 128-byte-swizzled tf32 operand, and every
-// contraction of a chunk runs as tcgen05.mma.kind::tf32 with M = 128 (state
-// rows), fp32 accumulation in TMEM:
-//   D1 = S^T W^T            (U^T = Uh^T - D1)       [v x tok]
-//   D2 = S^T Qt^T + U^T Aqk^T                        [v x t]   -> o^T
-//   D3 = U^T Kt             (S^T <- e^{G_last} S^T + D3)  [v x dk]
+// One CTA per (b, h); the 128x128 fp32 state lives transposed (S^T[v][dk], row v = TMEM
+// lane v) in tensor memory for the whole scan: it is the A operand of the chunk's first
+// MMA and the accumulator of its last, so it never passes through shared memory.  Every
+// contraction runs as tcgen05.mma.kind::tf32 with M = 128 (state rows), fp32 in TMEM:
+//   [D1 | D2] = S^T [W; Qt]^T     (U^T = Uh^T - D1)        [v x (tok | t)]
+//   S^T <- e^{G_last} S^T          (the epilogue, in place in TMEM)
+//   S^T += U^T Kt                  (the state update: MMA accumulate)
+//   D2 += U^T Aqk^T                -> o^T                   [v x t]
 // W, Qt, Aqk and Kt^T come from the prep kernel's workspace through TMA.
-// Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; warps 2-5: one
-// thread per state row v (TMEM lane), the two epilogues.
+// Warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; warps 2-5: one thread per
+// state row v, the chain's epilogue (U, the decay); warps 6-9: Uh^T into TMEM ahead of
+// its chunk and o^T out to global memory.
 static __device__ unsigned int g_scan_watchdog;
 
 namespace tc {
 constexpr int kD = 128;
-constexpr int kSt = 0;                       // S^T  [128 v][128 dk]   64 KB
-constexpr int kW = kSt + 65536;              // W    [64 tok][128 dk]  32 KB
-constexpr int kQ = kW + 32768;               // Qt   [64 t][128 dk]    32 KB
-constexpr int kA = kQ + 32768;               // Aqk  [64 t][64 tok]    16 KB
+// W and Qt interleaved by 32-column block (block kb at kW + 16 KB kb: 64 rows of W, then
+// 64 rows of Qt): one N = 128 K-major operand [W; Qt], so S^T W^T and S^T Qt^T are one MMA
+constexpr int kW = 0;                        // [W; Qt] [128 rows][128 dk]  64 KB
+constexpr int kQ = kW + 8192;                // Qt rows inside each 16 KB block
+constexpr int kA = kW + 65536;               // Aqk  [64 t][64 tok]    16 KB
 constexpr int kK = kA + 16384;               // Kt^T [128 dk][64 tok]  32 KB
 constexpr int kU = kK + 32768;               // U^T  [128 v][64 tok]   32 KB
 constexpr int kBar = kU + 32768;
@@ -370,8 +373,9 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
     uint64_t *bars = (uint64_t *)(sm + tc::kBar);
     // opfull / opfull2: W, Qt / Aqk, Kt^T of the chunk landed; d1done: D1 = S^T W^T in TMEM;
     // wqfree: the MMAs reading W and Qt completed; utready: U^T in shared memory (and this
-    // chunk's Uh read); d3done: D3 = U^T Kt in TMEM; d2done: o^T = D2 complete (and U^T, Aqk,
-    // Kt^T read); stready: the updated state in shared memory; uhready: the chunk's Uh^T in
+    // chunk's Uh read, S^T decayed); d3done: the state update S^T += U^T Kt; d2done: o^T = D2
+    // complete (and U^T, Aqk,
+    // Kt^T read); stready: the initial state in TMEM; uhready: the chunk's Uh^T in
     // TMEM; ofree: the chunk's o^T read out of its TMEM buffer.
     uint64_t *opfull = bars + 0, *d1done = bars + 1, *utready = bars + 2, *d3done = bars + 3,
              *stready = bars + 4, *opfull2 = bars + 5, *wqfree = bars + 6, *d2done = bars + 7,
@@ -410,22 +414,36 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    // TMEM columns: D1 [0, 64), D3 [128, 256), D2 (o^T) [256 + 64 p, 320 + 64 p) and
-    // Uh^T [384 + 64 p, 448 + 64 p) for chunk parity p.
-    constexpr uint32_t kTD1 = 0, kTD3 = 128, kTD2 = 256, kTUh = 384;
+    // TMEM columns: S^T [0, 128); D1 | D2 (o^T) [128 + 128 p, 192 + 128 p) |
+    // [192 + 128 p, 256 + 128 p) and Uh^T [384 + 64 p, 448 + 64 p) for chunk parity p.
+    constexpr uint32_t kTS = 0, kTD12 = 128, kTUh = 384;
 
     if (warp == 0) {
         if (lane == 0) {
             // Each operand pair is refilled as soon as the MMAs that read it have completed:
             // W and Qt of chunk c once chunk c - 1's D1 and S^T Qt^T are done (wqfree), Aqk and
             // Kt^T once its D3 and U^T Aqk^T are done (d2done).
+            auto prefetch = [&](int c) {  // chunk c's operand tiles into L2
+                if (c >= NC) return;
+                const int cix = bh * NC + c;
+                for (int kb = 0; kb < 4; ++kb) {
+                    tma_prefetch_2d(&tm_w, kb * 32, cix * 64);
+                    tma_prefetch_2d(&tm_q, kb * 32, cix * 64);
+                }
+                for (int kb = 0; kb < 2; ++kb) {
+                    tma_prefetch_2d(&tm_a, kb * 32, cix * 64);
+                    tma_prefetch_2d(&tm_k, kb * 32, cix * 128);
+                }
+            };
+            prefetch(1);
             for (int c = 0; c < NC; ++c) {
                 const int cix = bh * NC + c;
+                prefetch(c + 2);  // two chunks ahead: the loads below then hit L2
                 if (c > 0) mbar_wait(wqfree, (c - 1) & 1, wd, 1u);
                 mbar_arrive_expect_tx(opfull, tc::kOpWQ);
                 for (int kb = 0; kb < 4; ++kb) {
-                    tma_load_2d(sm + tc::kW + kb * 8192, &tm_w, opfull, kb * 32, cix * 64);
-                    tma_load_2d(sm + tc::kQ + kb * 8192, &tm_q, opfull, kb * 32, cix * 64);
+                    tma_load_2d(sm + tc::kW + kb * 16384, &tm_w, opfull, kb * 32, cix * 64);
+                    tma_load_2d(sm + tc::kQ + kb * 16384, &tm_q, opfull, kb * 32, cix * 64);
                 }
                 if (c > 0) mbar_wait(d2done, (c - 1) & 1, wd, 1u);
                 mbar_arrive_expect_tx(opfull2, tc::kOpAK);
@@ -438,42 +456,38 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t st = smem_u32(sm + tc::kSt), wq = smem_u32(sm + tc::kW),
-                           qq = smem_u32(sm + tc::kQ), aq = smem_u32(sm + tc::kA),
+            const uint32_t wq = smem_u32(sm + tc::kW), aq = smem_u32(sm + tc::kA),
                            kq = smem_u32(sm + tc::kK), uq = smem_u32(sm + tc::kU);
             constexpr uint32_t id64 = idesc_tf32_f32(128, 64), id128 = idesc_tf32_f32(128, 128);
-            const uint32_t tD1 = tmem + kTD1, tD3 = tmem + kTD3;
+            const uint32_t tS = tmem + kTS;
             // The chain that carries the state is S -> D1 -> U -> D3 -> S; the output's MMAs
             // (S^T Qt^T, U^T Aqk^T) follow the chain's MMA of their group in the in-order
             // tensor pipe, and o^T leaves TMEM through its own warps.
             for (int c = 0; c < NC; ++c) {
                 const uint32_t ph = c & 1;
-                const uint32_t tD2 = tmem + kTD2 + 64 * ph;
-                mbar_wait(stready, ph, wd, 2u);
+                const uint32_t tD12 = tmem + kTD12 + 128 * ph, tD2 = tD12 + 64;
+                // the state: initial (written by the epilogue) or after chunk c - 1's update
+                if (c == 0) mbar_wait(stready, 0, wd, 2u);
+                else mbar_wait(d3done, (c - 1) & 1, wd, 2u);
                 mbar_wait(opfull, ph, wd, 4u);
-                tc_fence_after();
-                // D1 = S^T W^T   (K = dk = 128: 4 blocks x 4 steps)
-                for (int kb = 0; kb < 4; ++kb)
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_tf32(tD1, sdesc_kmajor_sw128(st + kb * 16384 + kk * 32),
-                                 sdesc_kmajor_sw128(wq + kb * 8192 + kk * 32), id64, (kb | kk) ? 1u : 0u);
-                mma_commit(d1done);
-                // D2 = S^T Qt^T, into the buffer chunk c - 2's o^T has left
+                // the buffer chunk c - 2's o^T has left
                 if (c >= 2) mbar_wait(&ofree[ph], ((c - 2) >> 1) & 1, wd, 4u);
                 tc_fence_after();
+                // [D1 | D2] = S^T [W; Qt]^T   (N = 128, K = dk = 128: 16 steps of 8)
                 for (int kb = 0; kb < 4; ++kb)
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_tf32(tD2, sdesc_kmajor_sw128(st + kb * 16384 + kk * 32),
-                                 sdesc_kmajor_sw128(qq + kb * 8192 + kk * 32), id64, (kb | kk) ? 1u : 0u);
+                        mma_tf32_ts(tD12, tS + kb * 32 + kk * 8,
+                                    sdesc_kmajor_sw128(wq + kb * 16384 + kk * 32), id128, (kb | kk) ? 1u : 0u);
+                mma_commit(d1done);
                 mma_commit(wqfree);
                 mbar_wait(utready, ph, wd, 8u);
                 mbar_wait(opfull2, ph, wd, 4u);
                 tc_fence_after();
-                // D3 = U^T Kt   (K = tok = 64: 2 blocks x 4 steps)
+                // S^T += U^T Kt   (the epilogue scaled S^T by e^{G_last}; K = tok = 64)
                 for (int kb = 0; kb < 2; ++kb)
                     for (int kk = 0; kk < 4; ++kk)
-                        mma_tf32(tD3, sdesc_kmajor_sw128(uq + kb * 16384 + kk * 32),
-                                 sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32), id128, (kb | kk) ? 1u : 0u);
+                        mma_tf32(tS, sdesc_kmajor_sw128(uq + kb * 16384 + kk * 32),
+                                 sdesc_kmajor_sw128(kq + kb * 16384 + kk * 32), id128, 1u);
                 mma_commit(d3done);
                 // D2 += U^T Aqk^T
                 for (int kb = 0; kb < 2; ++kb)
@@ -489,33 +503,32 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
         // the state chain: one thread per state row v (its TMEM lane)
         const int quad = warp & 3, v = quad * 32 + lane;
         const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-        float *ST = (float *)(sm + tc::kSt);
         unsigned char *UT = sm + tc::kU;
-        // initial state, transposed: S^T[v][dk] = S0[dk][v]
-        for (int k4 = 0; k4 < tc::kD; k4 += 4) {
-            float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (a.s0) {
-                const float *s0 = a.s0 + (size_t)gbh * tc::kD * tc::kD + v;
-                x = make_float4(s0[(k4 + 0) * tc::kD], s0[(k4 + 1) * tc::kD],
-                                s0[(k4 + 2) * tc::kD], s0[(k4 + 3) * tc::kD]);
-            }
-            *(float4 *)((unsigned char *)ST + sw128_f32(128, v, k4)) = x;
+        // initial state, transposed into TMEM: S^T[v][dk] = S0[dk][v]
+#pragma unroll 1
+        for (int k0 = 0; k0 < tc::kD; k0 += 32) {
+            float x[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                x[i] = a.s0 ? a.s0[(size_t)gbh * tc::kD * tc::kD + (size_t)(k0 + i) * tc::kD + v] : 0.f;
+            tmem_st32(trow + kTS + k0, x);
         }
-        fence_proxy_async();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(stready);
         for (int c = 0; c < NC; ++c) {
             const uint32_t ph = c & 1;
             const size_t cix = (size_t)bh * NC + c;
             const float gl = __expf(a.G[cix * kC + kC - 1]);
-            // ---- E1: U^T = Uh^T - S^T W^T, both from TMEM
+            // ---- U^T = Uh^T - S^T W^T, both from TMEM, into shared memory (the A operand
+            // of the last two MMAs)
             mbar_wait(&uhready[ph], (c >> 1) & 1, wd, 16u);
             mbar_wait(d1done, ph, wd, 16u);
             tc_fence_after();
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t d[32], u[32];
-                tmem_ld32_issue(trow + kTD1 + half * 32, d);
+                tmem_ld32_issue(trow + kTD12 + 128 * ph + half * 32, d);
                 tmem_ld32_issue(trow + kTUh + 64 * ph + half * 32, u);
                 tmem_ld_wait(d);
                 tmem_ld_wait(u);
@@ -529,49 +542,44 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
                         __uint_as_float(u[j + 3]) - __uint_as_float(d[j + 3]));
                 }
             }
-            fence_proxy_async();
+            // ---- the decay, in place: S^T <- e^{G_last} S^T (the first MMA of the chunk,
+            // which read S^T, has completed)
+#pragma unroll
+            for (int q = 0; q < 4; q += 2) {
+                uint32_t r0[32], r1[32];
+                tmem_ld32_issue(trow + kTS + q * 32, r0);
+                tmem_ld32_issue(trow + kTS + (q + 1) * 32, r1);
+                tmem_ld_wait(r0);
+                tmem_ld_wait(r1);
+                float x0[32], x1[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    x0[i] = gl * __uint_as_float(r0[i]);
+                    x1[i] = gl * __uint_as_float(r1[i]);
+                }
+                tmem_st32(trow + kTS + q * 32, x0);
+                tmem_st32(trow + kTS + (q + 1) * 32, x1);
+            }
+            fence_proxy_async();  // U^T: generic-proxy stores, read by the tensor core
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(utready);
                 mbar_arrive(&uhfree[ph]);
             }
-            // ---- E2: S^T = e^{G_last} S^T + D3
-            mbar_wait(d3done, ph, wd, 32u);
-            tc_fence_after();
-#pragma unroll
-            for (int q = 0; q < 4; q += 2) {
-                uint32_t r0[32], r1[32];
-                tmem_ld32_issue(trow + kTD3 + q * 32, r0);
-                tmem_ld32_issue(trow + kTD3 + (q + 1) * 32, r1);
-                float4 x[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    x[j] = *(const float4 *)((unsigned char *)ST + sw128_f32(128, v, q * 32 + 4 * j));
-                tmem_ld_wait(r0);
-                tmem_ld_wait(r1);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const uint32_t *r = j < 8 ? r0 : r1;
-                    const int jj = (j & 7) * 4;
-                    x[j].x = fmaf(gl, x[j].x, __uint_as_float(r[jj]));
-                    x[j].y = fmaf(gl, x[j].y, __uint_as_float(r[jj + 1]));
-                    x[j].z = fmaf(gl, x[j].z, __uint_as_float(r[jj + 2]));
-                    x[j].w = fmaf(gl, x[j].w, __uint_as_float(r[jj + 3]));
-                    *(float4 *)((unsigned char *)ST + sw128_f32(128, v, q * 32 + 4 * j)) = x[j];
-                }
-            }
-            fence_proxy_async();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(stready);
         }
-        // the final state once the last chunk's MMAs (which read S) have completed
-        mbar_wait(d2done, (NC - 1) & 1, wd, 64u);
+        // the final state once the last update has completed
+        mbar_wait(d3done, (NC - 1) & 1, wd, 64u);
+        tc_fence_after();
         if (a.sT) {
             float *sT = a.sT + (size_t)gbh * tc::kD * tc::kD + v;
-            for (int k = 0; k < tc::kD; ++k)
-                sT[(size_t)k * tc::kD] = *(float *)((unsigned char *)ST + sw128_f32(128, v, k));
+#pragma unroll 1
+            for (int k0 = 0; k0 < tc::kD; k0 += 32) {
+                float x[32];
+                tmem_ld32(trow + kTS + k0, x);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sT[(size_t)(k0 + i) * tc::kD] = x[i];
+            }
         }
     } else {
         // output and prefetch warps (same TMEM lane quarters): Uh^T of chunk c + 2 into the
@@ -614,8 +622,8 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
             tc_fence_after();
             if (!a.transition) {
                 uint32_t ro0[32], ro1[32];
-                tmem_ld32_issue(trow + kTD2 + 64 * ph, ro0);
-                tmem_ld32_issue(trow + kTD2 + 64 * ph + 32, ro1);
+                tmem_ld32_issue(trow + kTD12 + 128 * ph + 64, ro0);
+                tmem_ld32_issue(trow + kTD12 + 128 * ph + 96, ro1);
                 tmem_ld_wait(ro0);
                 tmem_ld_wait(ro1);
                 Tout *op = o + (((size_t)b * a.T + t0) * a.H + h) * tc::kD + v;
