@@ -236,6 +236,7 @@ constexpr int kEpiThreads = 256;
 constexpr int kBins = kLinTop + 1;  // histogram bins per row (32-bit counters)
 constexpr int kDigit = 7;           // bits per digit of the plain radix fallback
 constexpr int kCap = kBins;         // candidate slots of a row: its whole histogram column
+constexpr int kLongRow = 16384;     // rows this long get the narrower first window
 constexpr int kMaxPasses = 8;
 
 struct RowSel {
@@ -795,7 +796,8 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                             if (jb + i < nvalid) dr[jb + i] = v[i];
                     }
                     if (pass == 0 && kt == 0 && ci == 0) {
-                        // sample of the first key tile: place every row's window
+                        // sample of the first key tile (the row's 128 scores, both of this
+                        // thread's chunks): place every row's window
                         uint32_t amax = 0u;
                         int np = 0, nv = 0;
 #pragma unroll
@@ -804,6 +806,18 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                             amax = max(amax, ok ? (__float_as_uint(v[i]) & 0x7fffffffu) : 0u);
                             np += ok && v[i] > 0.f;
                             nv += ok;
+                        }
+                        if (C::kN > 64) {
+                            float w2[32];
+                            tmem_ld32(taddr + (c + 2) * 32, w2);
+                            const int jb2 = jb + 64;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                const bool ok = active && jb2 + i < nvalid;
+                                amax = max(amax, ok ? (__float_as_uint(w2[i]) & 0x7fffffffu) : 0u);
+                                np += ok && w2[i] > 0.f;
+                                nv += ok;
+                            }
                         }
                         s_xch[0][half][row] = (uint32_t)np | ((uint32_t)nv << 16);
                         s_xch[1][half][row] = amax;
@@ -818,6 +832,12 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                         const float p = nval ? (float)npos / (float)nval : 0.5f;
                         const float q = (float)s.need / (float)max(nvalid, 1);
                         const float lo = p > q + 0.15f ? 0.f : p < q - 0.15f ? -W : -0.5f * W;
+                        // Long rows selecting from the upper tail: the k-th score lies well
+                        // inside [0, max|s| of the sample), and a window of about that width
+                        // keeps its bin under the candidate capacity where 2 max|s| would
+                        // need the refine pass (a k-th score beyond the window restarts the
+                        // row exactly, with the plain digits, so this only trades passes).
+                        if (lo == 0.f && nvalid >= kLongRow) W *= 0.525f;
                         s.a0 = 1.0f / W;
                         s.b0 = -lo * s.a0;
                     }
