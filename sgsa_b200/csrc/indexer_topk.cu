@@ -237,6 +237,8 @@ constexpr int kBins = kLinTop + 1;  // histogram bins per row (32-bit counters)
 constexpr int kDigit = 7;           // bits per digit of the plain radix fallback
 constexpr int kCap = kBins;         // candidate slots of a row: its whole histogram column
 constexpr int kLongRow = 16384;     // rows this long get the narrower first window
+constexpr int kSampleFrom = 8192;   // query tiles from here on start with a sampled pass
+constexpr int kSampleStride = 8;    // ... over every 8th key tile
 constexpr int kMaxPasses = 8;
 
 struct RowSel {
@@ -509,6 +511,36 @@ __device__ __forceinline__ void lin_choose(const uint32_t *hist, int col, int ne
     }
 }
 
+// After a sampled window pass (every kSampleStride-th key tile, nsamp of the row's keys):
+// the window of the full pass, placed on the sample's own counts.  In a sample of nsamp
+// keys the k-th key of the row has rank about need_s = need nsamp / nvalid, within a few
+// sqrt(need_s); the window spans the bins holding the sample ranks need_s -+ R, R =
+// 6 sqrt(need_s) + 8, so the full pass's chosen bin holds few keys and goes straight to
+// the candidate pass.  The window only steers the work: a k-th key outside it restarts the
+// row with the plain digits, exactly.
+__device__ __forceinline__ void lin_resample(RowSel &s, const uint32_t *hist, int col, int nvalid,
+                                             int nsamp) {
+    if (nsamp <= 0 || nvalid <= 0) return;
+    const float need_s = (float)s.need * (float)nsamp / (float)nvalid;
+    const float R = 6.f * sqrtf(need_s) + 8.f;
+    const int r_top = (int)(need_s - R), r_bot = (int)ceilf(need_s + R);
+    const float a = s.a0, b = s.b0;
+    float lo = -b / a, hi = lo + 1.f / a;  // the sampled pass's window
+    int c, cum, cnt;
+    if (r_bot <= nsamp) {
+        lin_choose(hist, col, r_bot, c, cum, cnt);
+        if (c > 0) lo = ((c - 0.5f) / (float)kLinTop - b) / a;  // lower edge of bin c
+    }
+    if (r_top >= 1) {
+        lin_choose(hist, col, r_top, c, cum, cnt);
+        if (c < kLinTop) hi = ((c + 0.5f) / (float)kLinTop - b) / a;  // upper edge of bin c
+    }
+    if (hi > lo && hi - lo < INFINITY) {
+        s.a0 = 1.0f / (hi - lo);
+        s.b0 = -lo * s.a0;
+    }
+}
+
 // After the window pass: the chosen bin, with exact key edges by bisection.
 __device__ __forceinline__ void lin_after0(RowSel &s, const uint32_t *hist, int col, int K,
                                            unsigned long long *stats, bool count) {
@@ -658,6 +690,9 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
     const int row = quad * 32 + lane;
     const int t = q0 + row;
     const int nvalid = (epi && t < T) ? t + 1 : 0;
+    // long query tiles: pass 0 bins a sample (every kSampleStride-th key tile) to place the
+    // window of the full pass (CTA-uniform: every role strides its tile loop the same way)
+    const bool sampled = q0 >= kSampleFrom;
     const bool has_row = epi && t < T;
     const bool stat_thread = has_row && half == 0;
     int32_t *out_row = (has_row && idx) ? idx + ((size_t)bh * T + t) * K : nullptr;
@@ -723,7 +758,8 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
     for (int pass = 0;; ++pass) {
         if (warp == 0) {
             if (lane == 0) {
-                for (int kt = 0; kt < nkt; ++kt, ++it_p) {
+                const int kstep = (sampled && pass == 0) ? kSampleStride : 1;
+                for (int kt = 0; kt < nkt; kt += kstep, ++it_p) {
                     const uint32_t st = it_p % C::kStages, ph = (it_p / C::kStages) & 1;
                     mbar_wait(&empty[st], ph ^ 1, wd, 1u);
                     mbar_arrive_expect_tx(&full[st], C::kKBytes);
@@ -738,7 +774,8 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
             if (lane == 0) {
                 constexpr uint32_t idesc = idesc_bf16_f32(128, C::kN);
                 const uint32_t tq = tmem + C::kTIQ;  // A operand in tensor memory
-                for (int kt = 0; kt < nkt; ++kt, ++it_m) {
+                const int kstep = (sampled && pass == 0) ? kSampleStride : 1;
+                for (int kt = 0; kt < nkt; kt += kstep, ++it_m) {
                     const uint32_t st = it_m % C::kStages, ph = (it_m / C::kStages) & 1;
                     const uint32_t buf = it_m % C::kAcc, bph = (it_m / C::kAcc) & 1;
                     mbar_wait(&tempty[buf], bph ^ 1, wd, 4u);
@@ -775,7 +812,8 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
             // candidate slots: half 0 from the front of the row's column, half 1 from the back
             uint32_t cslot = (uint32_t)__cvta_generic_to_shared(hcol + (half ? (kCap - 1) * kRows : 0));
             const int cstep = half ? -(int)(kRows * 4) : (int)(kRows * 4);
-            for (int kt = 0; kt < nkt; ++kt, ++it_e) {
+            const int kstep = (sampled && pass == 0) ? kSampleStride : 1;
+            for (int kt = 0; kt < nkt; kt += kstep, ++it_e) {
                 const uint32_t buf = it_e % C::kAcc, bph = (it_e / C::kAcc) & 1;
                 mbar_wait(&tfull[buf], bph, wd, 16u);
                 tc_fence_after();
@@ -904,6 +942,11 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                             s.cand = true;
                             if (stat_thread) atomicAdd(&g_index_stats[2], 1ull);
                         }
+                    } else if (s.lvl == 0 && sampled && pass == 0) {
+                        int nsamp = 0;  // this row's keys in the sampled tiles
+                        for (int kt = 0; kt < nkt; kt += kSampleStride)
+                            nsamp += max(0, min(C::kN, nvalid - kt * C::kN));
+                        lin_resample(s, hist, row, nvalid, nsamp);
                     } else if (s.lvl == 0) {
                         lin_after0(s, hist, row, K, g_index_stats, stat_thread);
                     } else {
