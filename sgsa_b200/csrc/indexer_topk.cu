@@ -818,6 +818,47 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                 mbar_wait(&tfull[buf], bph, wd, 16u);
                 tc_fence_after();
                 const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + buf * C::kN;
+                if (!collecting && pass == 0 && kt == 0) {
+                    // sample of the first key tile (the row's 128 scores: this thread's two
+                    // chunks, 16 columns at a time): place every row's window
+                    uint32_t amax = 0u;
+                    int np = 0, nv = 0;
+#pragma unroll 1
+                    for (int q4 = 0; q4 < C::kN / 32; ++q4) {
+                        const int c = half + 2 * (q4 >> 1);
+                        float w2[16];
+                        tmem_ld16(taddr + c * 32 + (q4 & 1) * 16, w2);
+                        const int jb2 = c * 32 + (q4 & 1) * 16;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const bool ok = active && jb2 + i < nvalid;
+                            amax = max(amax, ok ? (__float_as_uint(w2[i]) & 0x7fffffffu) : 0u);
+                            np += ok && w2[i] > 0.f;
+                            nv += ok;
+                        }
+                    }
+                    s_xch[0][half][row] = (uint32_t)np | ((uint32_t)nv << 16);
+                    s_xch[1][half][row] = amax;
+                    epi_bar();
+                    const uint32_t o = s_xch[0][half ^ 1][row];
+                    amax = max(amax, s_xch[1][half ^ 1][row]);
+                    const int npos = np + (int)(o & 0xffffu), nval = nv + (int)(o >> 16);
+                    // window 2 max|s| wide; by the sample's share of positive scores
+                    // against the share to select: [0, W), [-W/2, W/2) or [-W, 0)
+                    float W = 2.0f * __uint_as_float(min(amax, 0x7f000000u));
+                    W = W > 1e-30f ? W : 1.0f;
+                    const float p = nval ? (float)npos / (float)nval : 0.5f;
+                    const float q = (float)s.need / (float)max(nvalid, 1);
+                    const float lo = p > q + 0.15f ? 0.f : p < q - 0.15f ? -W : -0.5f * W;
+                    // Long rows selecting from the upper tail: the k-th score lies well
+                    // inside [0, max|s| of the sample), and a window of about that width
+                    // keeps its bin under the candidate capacity where 2 max|s| would
+                    // need the refine pass (a k-th score beyond the window restarts the
+                    // row exactly, with the plain digits, so this only trades passes).
+                    if (lo == 0.f && nvalid >= kLongRow) W *= 0.525f;
+                    s.a0 = 1.0f / W;
+                    s.b0 = -lo * s.a0;
+                }
                 if (!collecting) {
 #pragma unroll 1
                   for (int ci = 0; ci < C::kN / 64; ++ci) {  // chunks half, half + 2 of the tile
@@ -832,52 +873,6 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             if (jb + i < nvalid) dr[jb + i] = v[i];
-                    }
-                    if (pass == 0 && kt == 0 && ci == 0) {
-                        // sample of the first key tile (the row's 128 scores, both of this
-                        // thread's chunks): place every row's window
-                        uint32_t amax = 0u;
-                        int np = 0, nv = 0;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const bool ok = active && jb + i < nvalid;
-                            amax = max(amax, ok ? (__float_as_uint(v[i]) & 0x7fffffffu) : 0u);
-                            np += ok && v[i] > 0.f;
-                            nv += ok;
-                        }
-                        if (C::kN > 64) {
-                            float w2[32];
-                            tmem_ld32(taddr + (c + 2) * 32, w2);
-                            const int jb2 = jb + 64;
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) {
-                                const bool ok = active && jb2 + i < nvalid;
-                                amax = max(amax, ok ? (__float_as_uint(w2[i]) & 0x7fffffffu) : 0u);
-                                np += ok && w2[i] > 0.f;
-                                nv += ok;
-                            }
-                        }
-                        s_xch[0][half][row] = (uint32_t)np | ((uint32_t)nv << 16);
-                        s_xch[1][half][row] = amax;
-                        epi_bar();
-                        const uint32_t o = s_xch[0][half ^ 1][row];
-                        amax = max(amax, s_xch[1][half ^ 1][row]);
-                        const int npos = np + (int)(o & 0xffffu), nval = nv + (int)(o >> 16);
-                        // window 2 max|s| wide; by the sample's share of positive scores
-                        // against the share to select: [0, W), [-W/2, W/2) or [-W, 0)
-                        float W = 2.0f * __uint_as_float(min(amax, 0x7f000000u));
-                        W = W > 1e-30f ? W : 1.0f;
-                        const float p = nval ? (float)npos / (float)nval : 0.5f;
-                        const float q = (float)s.need / (float)max(nvalid, 1);
-                        const float lo = p > q + 0.15f ? 0.f : p < q - 0.15f ? -W : -0.5f * W;
-                        // Long rows selecting from the upper tail: the k-th score lies well
-                        // inside [0, max|s| of the sample), and a window of about that width
-                        // keeps its bin under the candidate capacity where 2 max|s| would
-                        // need the refine pass (a k-th score beyond the window restarts the
-                        // row exactly, with the plain digits, so this only trades passes).
-                        if (lo == 0.f && nvalid >= kLongRow) W *= 0.525f;
-                        s.a0 = 1.0f / W;
-                        s.b0 = -lo * s.a0;
                     }
                     if (active && jb < nvalid) {
                         if (do_cand) {
