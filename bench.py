@@ -80,8 +80,9 @@ def algorithmic_counts(cfg):
 # launch at T = 8192, from ncu captures of the launches at B1 T8192 H16 (the command
 # of each is in TRAFFIC_SOURCE); the traffic of these kernels grows in proportion to
 # the (batch, head) pairs a launch processes.
-TRAFFIC_PER_BH = {"sparse_attn_tc": (417.96e6 + 25.08e6) / 16, "indexer_thresholds": 32.65e6 / 16,
-                  "delta": (101.80e6 + 243.43e6 + 302.32e6 + 53.64e6) / 16}
+TRAFFIC_PER_BH = {"sparse_attn_tc": (417.96e6 + 25.08e6) / 16,
+                  "indexer_thresholds": (32.64e6 + 23.81e6) / 16,
+                  "delta": (101.74e6 + 242.67e6 + 302.36e6 + 52.37e6) / 16}
 TRAFFIC_SOURCE = ("ncu dram bytes of one launch at B1 T8192 H16 (python bench.py --only <stage> "
                   "--steps 1 --B 1 --H 16), scaled by the launch's (b, h) count")
 
