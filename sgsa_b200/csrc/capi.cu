@@ -401,6 +401,8 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
         e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
                                      initial_state, od, final_state, B, T, H, D, dtype, flags, w,
                                      side, layer_delta_cap());
+        // the attention's per-head norm bound, memory-bound, also beside the indexer
+        if (e == cudaSuccess) e = sgsa::launch_qk_norm_max(q, k, qkmax, B, T, H, side);
         cudaError_t ej = cudaSuccess;
         if (side != st) ej = cudaEventRecord(ss->join, side);
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
@@ -412,7 +414,7 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
         if (ej != cudaSuccess) return fail_cuda(ej);
         e = sgsa::launch_sparse_attn_tc(q, k, v, iq, ik, thr, od, mix, out, B, T, H, scale,
                                         mix_per_channel, nullptr, 0, dtype == SGSA_DTYPE_F32,
-                                        idx_heads, qkmax, st);
+                                        idx_heads, qkmax, st, nullptr, /*norms_ready=*/true);
         return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
     }
     e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr, initial_state,

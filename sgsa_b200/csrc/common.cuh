@@ -91,7 +91,11 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
                                   int HI, uint32_t *qkmax, cudaStream_t st,
-                                  float *dbg_scores = nullptr);
+                                  float *dbg_scores = nullptr, bool norms_ready = false);
+// max|q|^2, max|k|^2 per (b, h) into qkmax[2 (b H + h) + {0, 1}] (bf16, D = 128): the bound the
+// tensor-core attention's softmax uses (launch_sparse_attn_tc runs it unless norms_ready).
+cudaError_t launch_qk_norm_max(const void *q, const void *k, uint32_t *qkmax, int B, int T, int H,
+                               cudaStream_t st);
 cudaError_t launch_sparse_retrieve(const void *q, const void *k, const void *v, const int32_t *idx,
                                    void *khat, void *vhat, int B, int T, int H, int D, int K,
                                    float scale, int HI, int dtype, cudaStream_t st);

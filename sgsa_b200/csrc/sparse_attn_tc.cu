@@ -535,6 +535,16 @@ __global__ void __launch_bounds__(256) qk_norm_max_kernel(const __nv_bfloat16 *_
 
 }  // namespace
 
+cudaError_t launch_qk_norm_max(const void *q, const void *k, uint32_t *qkmax, int B, int T, int H,
+                               cudaStream_t st) {
+    if (B * H > 65535) return cudaSuccess;  // the attention then keeps a running maximum
+    cudaError_t e = cudaMemsetAsync(qkmax, 0, (size_t)B * H * 2 * sizeof(uint32_t), st);
+    if (e != cudaSuccess) return e;
+    qk_norm_max_kernel<<<dim3(ceil_div(T, kNormRows), B * H), 256, 0, st>>>(
+        (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, qkmax, T, H);
+    return launched();
+}
+
 bool sparse_attn_tc_eligible(int T, int D, int DI, int dtype) {
     (void)T;
     return dtype == SGSA_DTYPE_BF16 && D == 128 && DI == 64;
@@ -544,7 +554,8 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
                                   const void *ik, const uint32_t *thr, const float *od,
                                   const void *mix, void *out, int B, int T, int H, float scale,
                                   int mix_pc, const int32_t *q_tiles, int n_tiles, bool out_f32,
-                                  int HI, uint32_t *qkmax, cudaStream_t st, float *dbg_scores) {
+                                  int HI, uint32_t *qkmax, cudaStream_t st, float *dbg_scores,
+                                  bool norms_ready) {
     CUtensorMap mk, mv, mik;
     if (!make_tmap_rows_bf16(&mk, k, B, T, H, 128, kBlk) ||
         !make_tmap_rows_bf16(&mv, v, B, T, H, 128, kBlk) ||
@@ -555,12 +566,8 @@ cudaError_t launch_sparse_attn_tc(const void *q, const void *k, const void *v, c
     if (ntiles <= 0) return cudaSuccess;
     const float sl = scale * 1.4426950408889634f;
     if (B * H > 65535) qkmax = nullptr;  // grid limit of the norm pass: running maximum instead
-    if (qkmax) {
-        cudaError_t e = cudaMemsetAsync(qkmax, 0, (size_t)B * H * 2 * sizeof(uint32_t), st);
-        if (e != cudaSuccess) return e;
-        qk_norm_max_kernel<<<dim3(ceil_div(T, kNormRows), B * H), 256, 0, st>>>(
-            (const __nv_bfloat16 *)q, (const __nv_bfloat16 *)k, qkmax, T, H);
-        e = launched();
+    if (qkmax && !norms_ready) {
+        cudaError_t e = launch_qk_norm_max(q, k, qkmax, B, T, H, st);
         if (e != cudaSuccess) return e;
     }
     if (out_f32) {
