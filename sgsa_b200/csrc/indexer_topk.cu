@@ -239,6 +239,7 @@ constexpr int kCap = kBins;         // candidate slots of a row: its whole histo
 constexpr int kLongRow = 16384;     // rows this long get the narrower first window
 constexpr int kSampleFrom = 8192;   // query tiles from here on start with a sampled pass
 constexpr int kSampleStride = 8;    // ... over every 8th key tile
+constexpr int kSmallGridWaves = 4;  // grids of at most this many CTAs per SM: one CTA per SM
 constexpr int kMaxPasses = 8;
 
 struct RowSel {
@@ -635,7 +636,11 @@ __device__ __forceinline__ void collect_chunk(const float (&v)[32], uint32_t *ri
     }
 }
 
-template <int DI>
+// ACC = 1: one 128-column accumulator, 256 TMEM columns, two CTAs per SM (the pipeline's
+// MMA and epilogue alternate within a CTA; the other CTA fills the gaps).  ACC = 2: two
+// accumulators, 512 columns, one CTA per SM whose next tile's MMA overlaps the epilogue of
+// the current one: faster per CTA, for grids too small to fill the SMs twice over.
+template <int DI, int ACC = 1>
 struct TcCfg {
     static constexpr int kKB = DI / 64;                // 128-byte K blocks
     // 128-key tiles: the tensor-core attention recomputes these scores with the
@@ -645,24 +650,24 @@ struct TcCfg {
     static constexpr int kKBytes = kN * DI * 2;
     static constexpr int kStages = 2;
     static constexpr int kHistBytes = kBins * kRows * 4;
-    static constexpr int kAcc = 1;                     // TMEM accumulator buffers
+    static constexpr int kAcc = ACC;                   // TMEM accumulator buffers
     static constexpr int kBars = 2 * kStages + 2 * kAcc;
     static constexpr size_t kSmem = 1024 + kStages * kKBytes + kHistBytes + kBars * 8;
     // TMEM: the accumulators, then the query tile (the MMA's A operand: row = lane,
     // two bf16 per 32-bit column)
     static constexpr int kTIQ = kAcc * kN;
-    static constexpr int kTmemCols = 256;
+    static constexpr int kTmemCols = ACC == 1 ? 256 : 512;
     static_assert(kTIQ + DI / 2 <= kTmemCols, "tensor memory");
     static constexpr int kThreads = 64 + kEpiThreads;
 };
 
-template <int DI>
-__global__ void __launch_bounds__(TcCfg<DI>::kThreads, 2)
+template <int DI, int ACC>
+__global__ void __launch_bounds__(TcCfg<DI, ACC>::kThreads, ACC == 1 ? 2 : 1)
 indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
                        const __grid_constant__ CUtensorMap tm_k, int32_t *__restrict__ idx,
                        uint4 *__restrict__ thr, int B, int T, int H, int K, int nqt,
                        const int32_t *__restrict__ q_tiles, float *__restrict__ dbg_scores) {
-    using C = TcCfg<DI>;
+    using C = TcCfg<DI, ACC>;
     using namespace sm100;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned char *base = (unsigned char *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -989,19 +994,26 @@ template <int DI>
 cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T, int H,
                    int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st,
                    float *dbg_scores = nullptr) {
-    using C = TcCfg<DI>;
     CUtensorMap mk;
-    if (!make_tmap_rows_bf16(&mk, ik, B, T, H, DI, C::kN)) return cudaErrorInvalidValue;
-    auto kern = indexer_topk_tc_kernel<DI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::kSmem);
-    if (e != cudaSuccess) return e;
+    if (!make_tmap_rows_bf16(&mk, ik, B, T, H, DI, TcCfg<DI>::kN)) return cudaErrorInvalidValue;
     const int nqt = ceil_div(T, kRows);
     const int ntiles = q_tiles ? n_tiles : nqt;
     if (ntiles <= 0) return cudaSuccess;
-    kern<<<ntiles * B * H, C::kThreads, C::kSmem, st>>>((const __nv_bfloat16 *)iq, mk, idx, thr, B,
-                                                      T, H, K, nqt, q_tiles, dbg_scores);
-    return launched();
+    const long long ctas = (long long)ntiles * B * H;
+    int dev = 0, nsm = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    // Grids that do not fill the SMs several times over: one CTA per SM with two accumulators
+    auto go = [&](auto kern, size_t smem, int threads) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        kern<<<(unsigned)ctas, threads, smem, st>>>((const __nv_bfloat16 *)iq, mk, idx, thr, B, T, H, K,
+                                                    nqt, q_tiles, dbg_scores);
+        return launched();
+    };
+    if (ctas <= (long long)kSmallGridWaves * nsm)
+        return go(indexer_topk_tc_kernel<DI, 2>, TcCfg<DI, 2>::kSmem, TcCfg<DI, 2>::kThreads);
+    return go(indexer_topk_tc_kernel<DI, 1>, TcCfg<DI, 1>::kSmem, TcCfg<DI, 1>::kThreads);
 }
 
 template <int DI>
