@@ -407,7 +407,7 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
         if (side != st) ej = cudaEventRecord(ss->join, side);
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
             e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, idx_heads, DI, top_k,
-                                              nullptr, 0, st);
+                                              nullptr, 0, st, /*shares_sms=*/side != st);
         // always join, so that the caller's stream never runs ahead of the side stream
         if (side != st && ej == cudaSuccess) ej = cudaStreamWaitEvent(st, ss->join, 0);
         if (e != cudaSuccess) return fail_cuda(e);

@@ -78,7 +78,7 @@ cudaError_t launch_indexer_topk_debug(const void *iq, const void *ik, int32_t *i
 bool indexer_tc_eligible(int DI, int dtype);
 cudaError_t launch_indexer_topk_thr(const void *iq, const void *ik, int32_t *idx, uint32_t *thr,
                                     int B, int T, int H, int DI, int K, const int32_t *q_tiles,
-                                    int n_tiles, cudaStream_t st);
+                                    int n_tiles, cudaStream_t st, bool shares_sms = false);
 cudaError_t launch_topk_select(const float *scores, const int32_t *valid, int32_t *idx, int R,
                                int S, int K, cudaStream_t st);
 cudaError_t launch_sparse_attn_mix(const void *q, const void *k, const void *v,

@@ -993,7 +993,7 @@ indexer_topk_tc_kernel(const __nv_bfloat16 *__restrict__ iq,
 template <int DI>
 cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T, int H,
                    int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st,
-                   float *dbg_scores = nullptr) {
+                   float *dbg_scores = nullptr, bool shares_sms = false) {
     CUtensorMap mk;
     if (!make_tmap_rows_bf16(&mk, ik, B, T, H, DI, TcCfg<DI>::kN)) return cudaErrorInvalidValue;
     const int nqt = ceil_div(T, kRows);
@@ -1011,15 +1011,17 @@ cudaError_t run_tc(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int
                                                     nqt, q_tiles, dbg_scores);
         return launched();
     };
-    if (ctas <= (long long)kSmallGridWaves * nsm)
+    // (not while other kernels run beside it: its 512 TMEM columns would keep them off the SM)
+    if (!shares_sms && ctas <= (long long)kSmallGridWaves * nsm)
         return go(indexer_topk_tc_kernel<DI, 2>, TcCfg<DI, 2>::kSmem, TcCfg<DI, 2>::kThreads);
     return go(indexer_topk_tc_kernel<DI, 1>, TcCfg<DI, 1>::kSmem, TcCfg<DI, 1>::kThreads);
 }
 
 template <int DI>
 cudaError_t run_tc_t(const void *iq, const void *ik, int32_t *idx, uint4 *thr, int B, int T,
-                     int H, int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st) {
-    return run_tc<DI>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st);
+                     int H, int K, const int32_t *q_tiles, int n_tiles, cudaStream_t st,
+                     bool shares_sms = false) {
+    return run_tc<DI>(iq, ik, idx, thr, B, T, H, K, q_tiles, n_tiles, st, nullptr, shares_sms);
 }
 
 template <typename Tin, int DI>
@@ -1054,9 +1056,11 @@ bool indexer_tc_eligible(int DI, int dtype) {
 
 cudaError_t launch_indexer_topk_thr(const void *iq, const void *ik, int32_t *idx, uint32_t *thr,
                                     int B, int T, int H, int DI, int K, const int32_t *q_tiles,
-                                    int n_tiles, cudaStream_t st) {
-    if (DI == 64) return run_tc_t<64>(iq, ik, idx, (uint4 *)thr, B, T, H, K, q_tiles, n_tiles, st);
-    if (DI == 128) return run_tc_t<128>(iq, ik, idx, (uint4 *)thr, B, T, H, K, q_tiles, n_tiles, st);
+                                    int n_tiles, cudaStream_t st, bool shares_sms) {
+    if (DI == 64)
+        return run_tc_t<64>(iq, ik, idx, (uint4 *)thr, B, T, H, K, q_tiles, n_tiles, st, shares_sms);
+    if (DI == 128)
+        return run_tc_t<128>(iq, ik, idx, (uint4 *)thr, B, T, H, K, q_tiles, n_tiles, st, shares_sms);
     return cudaErrorInvalidValue;
 }
 
