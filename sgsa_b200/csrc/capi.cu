@@ -41,13 +41,14 @@ bool head_dim_ok(int D) { return D == 32 || D == 64 || D == 128; }
 bool dtype_ok(int dt) { return dt == SGSA_DTYPE_F32 || dt == SGSA_DTYPE_BF16; }
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// The layer's concurrent delta stage runs on a non-blocking side stream with a
-// fork and a join event.  They are created once per (host thread, device) and
-// reused, so callers on different host threads never share them and a call
+// The layer's concurrent delta stage runs on a non-blocking side stream (the highest
+// priority, so that its few long-lived scan CTAs find SMs first) with a fork and a join
+// event, and an event after its prep kernel.  They are created once per (host thread,
+// device) and reused, so callers on different host threads never share them and a call
 // creates or destroys nothing after the first on its thread.
 struct SideStream {
     cudaStream_t stream = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr, prep = nullptr;
     bool ok = false;
 };
 
@@ -57,13 +58,18 @@ SideStream *side_stream() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
     SideStream &s = per_dev[dev];
     if (!s.ok) {
-        if (!s.stream && cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess)
+        int lo = 0, hi = 0;
+        if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess) hi = 0;
+        if (!s.stream &&
+            cudaStreamCreateWithPriority(&s.stream, cudaStreamNonBlocking, hi) != cudaSuccess)
             s.stream = nullptr;
         if (!s.fork && cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess)
             s.fork = nullptr;
         if (!s.join && cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess)
             s.join = nullptr;
-        s.ok = s.stream && s.fork && s.join;
+        if (!s.prep && cudaEventCreateWithFlags(&s.prep, cudaEventDisableTiming) != cudaSuccess)
+            s.prep = nullptr;
+        s.ok = s.stream && s.fork && s.join && s.prep;
         if (!s.ok) cudaGetLastError();
     }
     return s.ok ? &s : nullptr;
@@ -398,16 +404,26 @@ int sgsa_layer_fwd(const void *q, const void *k, const void *v, const void *beta
             if ((e = cudaEventRecord(ss->fork, st)) != cudaSuccess) return fail_cuda(e);
             if ((e = cudaStreamWaitEvent(side, ss->fork, 0)) != cudaSuccess) return fail_cuda(e);
         }
+        // A small indexer grid runs one CTA per SM (faster per CTA, but its tensor memory
+        // keeps other kernels off the SM): it then starts after the delta stage's prep and
+        // beside its few scan CTAs, which the side stream's priority places first.
+        int dev = 0, nsm = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess)
+            cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        const bool small_idx = side != st &&
+                               (long long)((T + 127) / 128) * B * idx_heads <= 4LL * nsm;
         e = sgsa::launch_chunk_delta(q, k, v, beta, gamma, nullptr, nullptr, nullptr,
                                      initial_state, od, final_state, B, T, H, D, dtype, flags, w,
-                                     side, layer_delta_cap());
+                                     side, layer_delta_cap(), small_idx ? ss->prep : nullptr);
         // the attention's per-head norm bound, memory-bound, also beside the indexer
         if (e == cudaSuccess) e = sgsa::launch_qk_norm_max(q, k, qkmax, B, T, H, side);
         cudaError_t ej = cudaSuccess;
         if (side != st) ej = cudaEventRecord(ss->join, side);
+        if (e == cudaSuccess && small_idx) e = cudaStreamWaitEvent(st, ss->prep, 0);
         if (e == cudaSuccess)  // selection as per-row thresholds; indices only if asked for
             e = sgsa::launch_indexer_topk_thr(iq, ik, indices, thr, B, T, idx_heads, DI, top_k,
-                                              nullptr, 0, st, /*shares_sms=*/side != st);
+                                              nullptr, 0, st,
+                                              /*shares_sms=*/side != st && !small_idx);
         // always join, so that the caller's stream never runs ahead of the side stream
         if (side != st && ej == cudaSuccess) ej = cudaStreamWaitEvent(st, ss->join, 0);
         if (e != cudaSuccess) return fail_cuda(e);

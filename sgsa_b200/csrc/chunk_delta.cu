@@ -955,7 +955,8 @@ static bool scan_use_tc() {
 }
 
 template <typename Tout>
-cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
+cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st,
+                        cudaEvent_t prep_done = nullptr) {
     const long long nch = (long long)a.nbh * a.NC;
     CUtensorMap mw, mq, ma, mk, mkin, mqin, mvin;
     if (!make_tmap_2d_f32(&mw, a.W, 128, nch * 64, 64) ||
@@ -977,6 +978,7 @@ cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st) {
         prep<<<dim3((a.NC + 1) / 2, a.nbh), 256, ptc::kSmem, st>>>(a, mkin, mqin, mvin);
         e = launched();
         if (e != cudaSuccess) return e;
+        if (prep_done && (e = cudaEventRecord(prep_done, st)) != cudaSuccess) return e;
     }
     scan<<<a.nbh, 320, tc::kSmem, st>>>(a, mw, mq, ma, mk);
     return launched();
@@ -1034,7 +1036,7 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
                                const void *gamma, const void *sk, const void *sv,
                                const void *alpha, const float *s0, void *o, float *sT, int B,
                                int T, int H, int D, int dtype, int flags, void *ws,
-                               cudaStream_t st, size_t ws_cap) {
+                               cudaStream_t st, size_t ws_cap, cudaEvent_t prep_done) {
     const bool sparse = flags & SGSA_FLAG_HAS_SPARSE;
     const int M = sparse ? 2 * kC : kC;
     const int group = chunk_delta_group_pairs(B, T, H, D, flags, ws_cap);
@@ -1068,8 +1070,9 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
             a.Qt = tail;
             a.KtT = a.Qt + nchunk * kC * D;
             const bool reuse = (flags & SGSA_FLAG_REUSE_PREP);
-            e = (flags & SGSA_FLAG_OUT_F32) ? run_tc_scan<float>(a, reuse, st)
-                                            : run_tc_scan<__nv_bfloat16>(a, reuse, st);
+            cudaEvent_t pd = g0 == 0 ? prep_done : nullptr;  // after the first group's prep
+            e = (flags & SGSA_FLAG_OUT_F32) ? run_tc_scan<float>(a, reuse, st, pd)
+                                            : run_tc_scan<__nv_bfloat16>(a, reuse, st, pd);
         } else if (dtype == SGSA_DTYPE_F32) {
             e = sparse ? run_d<float, float, true>(D, a, st) : run_d<float, float, false>(D, a, st);
         } else if (of32) {

@@ -58,7 +58,10 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
                                const void *gamma, const void *sk, const void *sv,
                                const void *alpha, const float *s0, void *o, float *sT, int B,
                                int T, int H, int D, int dtype, int flags, void *ws,
-                               cudaStream_t st, size_t ws_cap = 0);
+                               cudaStream_t st, size_t ws_cap = 0,
+                               cudaEvent_t prep_done = nullptr);
+// prep_done (optional): recorded on st after the first tensor-core prep launch (a
+// scheduling point for work that should follow it; nothing depends on it for correctness)
 size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags);
 size_t chunk_delta_ws_bytes_pairs(long long pairs, int T, int D, int flags);
 int chunk_delta_group_pairs(int B, int T, int H, int D, int flags, size_t cap);
