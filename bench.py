@@ -343,6 +343,28 @@ def stage_times(cfg, d, reps=3, only=None):
                                             1.0 / math.sqrt(D), 1, _lib.DTYPE_BF16,
                                             st.cuda_stream), "attn")
 
+    sw = {}
+
+    def delta_sw():
+        # the delta stage with the sparse write (row f3): 2 virtual samples per token; the
+        # retrieval's k_hat / v_hat stand-ins are the token's own k / v, alpha = beta
+        fl = _lib.FLAG_OUT_F32 | _lib.FLAG_HAS_SPARSE
+        if "ws" not in sw:
+            sw["ws"] = torch.empty(lib.sgsa_chunk_fwd_workspace_size(B, T, H, D, fl),
+                                   device="cuda", dtype=torch.uint8)
+        w = sw["ws"]
+        _lib.check(lib.sgsa_chunk_fwd(P(d["q"]), P(d["k"]), P(d["v"]), P(d["beta"]), P(d["gamma"]),
+                                      P(d["k"]), P(d["v"]), P(d["beta"]), None, P(od), None, B, T,
+                                      H, D, _lib.DTYPE_BF16, 64, fl, P(w), w.numel(),
+                                      st.cuda_stream), "chunk")
+
+    def delta_sw_simt():
+        os.environ["SGSA_SCAN_SIMT"] = "1"
+        try:
+            delta_sw()
+        finally:
+            del os.environ["SGSA_SCAN_SIMT"]
+
     thr = torch.empty(B, H, T, 4, device="cuda", dtype=torch.int32)
     norms = torch.empty(2 * B * H, device="cuda", dtype=torch.int32)
 
@@ -362,7 +384,8 @@ def stage_times(cfg, d, reps=3, only=None):
     res = {}
     # the stages as the layer runs them (fused) and the standalone index/gather pair
     stages = (("delta", delta), ("indexer_thresholds", index_thr), ("sparse_attn_tc", attn_tc),
-              ("indexer_topk", index), ("sparse_attn_mix", attn))
+              ("indexer_topk", index), ("sparse_attn_mix", attn),
+              ("delta_sparse_write", delta_sw), ("delta_sparse_write_cuda_core", delta_sw_simt))
     if only == "sparse_attn_mix":
         index()  # the attention stage reads the indexer's output
     if only == "sparse_attn_tc":
@@ -861,7 +884,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["delta", "indexer_topk", "sparse_attn_mix", "indexer_thresholds",
+    ap.add_argument("--only", default=None, choices=["delta", "delta_sparse_write", "indexer_topk", "sparse_attn_mix", "indexer_thresholds",
                              "sparse_attn_tc"],
                     help="profiling aid: run one stage --steps times on a (scaled) config, no JSON")
     ap.add_argument("--workload", default="layer", choices=["layer", "decode", "long", "hybrid"],

@@ -164,6 +164,7 @@ int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta
         return SGSA_OK;
     }
     if (!q || !k || !v || !beta || !gamma || !o) return SGSA_ERR_NULL;
+    flags &= 63;  // the public SGSA_FLAG_* bits; the rest are internal to the kernels
     if ((flags & SGSA_FLAG_HAS_SPARSE) && (!sparse_k || !sparse_v || !alpha)) return SGSA_ERR_NULL;
     if ((flags & SGSA_FLAG_HAS_INIT) && !initial_state) return SGSA_ERR_NULL;
     if ((flags & SGSA_FLAG_STORE_FINAL) && !final_state) return SGSA_ERR_NULL;

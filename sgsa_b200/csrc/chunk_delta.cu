@@ -37,6 +37,10 @@ constexpr int kC = 64;
 constexpr int kThreads = 256;
 constexpr int kBV = 32;
 
+// Internal flag of launch_chunk_delta: the inputs are the sparse write's interleaved virtual
+// samples (ChunkArgs::pairs).  Outside the public SGSA_FLAG_* bits.
+constexpr int kFlagPairs = 1 << 30;
+
 struct ChunkArgs {
     const void *q, *k, *v, *beta, *gamma, *sk, *sv, *alpha;
     const float *s0;
@@ -47,6 +51,11 @@ struct ChunkArgs {
     float *W, *U, *Aqk, *G;
     float *Qt, *KtT;  // tensor-core scan only: exp(G_t) q_t [C x D] and Kap~^T [D x C]
     int transition;   // tensor-core scan only: v taken as zero, o not written
+    // tensor-core kernels only: the rows are the sparse write's virtual samples, two per token
+    // (local sample at 2t, sparse sample at 2t + 1, decay 1 on the second); the sparse sample
+    // does not see its own token's local sample, and only the odd rows are read out, into
+    // row t of an o of a.T / 2 tokens
+    int pairs;
 };
 
 template <int D, bool SPARSE>
@@ -626,10 +635,17 @@ chunk_scan_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_w,
                 tmem_ld32_issue(trow + kTD12 + 128 * ph + 96, ro1);
                 tmem_ld_wait(ro0);
                 tmem_ld_wait(ro1);
-                Tout *op = o + (((size_t)b * a.T + t0) * a.H + h) * tc::kD + v;
+                if (a.pairs) {  // odd virtual rows only: sample 2t+1 holds token t's output
+                    Tout *op = o + (((size_t)b * (a.T >> 1) + (t0 >> 1)) * a.H + h) * tc::kD + v;
 #pragma unroll
-                for (int t = 0; t < kC; ++t)
-                    if (t < L) op[t * tstride] = from_f32<Tout>(__uint_as_float(t < 32 ? ro0[t] : ro1[t - 32]));
+                    for (int t = 1; t < kC; t += 2)
+                        if (t < L) op[(t >> 1) * tstride] = from_f32<Tout>(__uint_as_float(t < 32 ? ro0[t] : ro1[t - 32]));
+                } else {
+                    Tout *op = o + (((size_t)b * a.T + t0) * a.H + h) * tc::kD + v;
+#pragma unroll
+                    for (int t = 0; t < kC; ++t)
+                        if (t < L) op[t * tstride] = from_f32<Tout>(__uint_as_float(t < 32 ? ro0[t] : ro1[t - 32]));
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -772,8 +788,11 @@ chunk_prep_tc_kernel(ChunkArgs a, const __grid_constant__ CUtensorMap tm_k,
                     // branch-free: the exponent is clamped at 0 (its value only matters where
                     // m <= tau, where G_i <= G_j) and the mask selects
                     const float e = __expf(fminf(sG[i] - sG[j], 0.f)) * d[jj + u];
+                    // pairs: sample 2t+1 predicts from the state before token t's local
+                    // sample 2t (both samples of a token read the same decayed state)
+                    const bool dep = m < tau && !(a.pairs && (tau & 1) && m == tau - 1);
                     if (warp < 4)
-                        r[u] = (vi && vj && m < tau) ? lam_i * e : 0.f;
+                        r[u] = (vi && vj && dep) ? lam_i * e : 0.f;
                     else
                         r[u] = (vi && vj && m <= tau) ? e : 0.f;
                 }
@@ -984,6 +1003,40 @@ cudaError_t run_tc_scan(const ChunkArgs &a, bool reuse_prep, cudaStream_t st,
     return launched();
 }
 
+// The sparse write's virtual samples as a plain sequence of 2T rows for the tensor-core
+// kernels (chunk_fwd.py:49-56 builds the same interleave: kappa = (k_t, sparse_k_t),
+// nu = (v_t, sparse_v_t), lam = (beta_t, alpha_t), both samples at token t's decay):
+// row 2t = (k, v, beta, gamma, q = 0), row 2t+1 = (sparse_k, sparse_v, alpha, 1, q).
+// One thread per 8 bf16 values (16 bytes) of one token row of one head.
+__global__ void __launch_bounds__(256)
+pair_interleave_kernel(const uint4 *q, const uint4 *k, const uint4 *v, const uint4 *sk,
+                       const uint4 *sv, const __nv_bfloat16 *beta, const __nv_bfloat16 *gamma,
+                       const __nv_bfloat16 *alpha, uint4 *qv, uint4 *kv, uint4 *vv,
+                       __nv_bfloat16 *bv, __nv_bfloat16 *gv, long long rows, int H, int vec) {
+    const long long n = rows * vec;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (long long)gridDim.x * blockDim.x) {
+        // e = r*vec + x with token row r = (b*T + t)*H + h; the virtual rows of (b, t) are
+        // 2(b*T + t) and 2(b*T + t) + 1 of a [B, 2T, H] layout
+        const long long r = e / vec, bt = r / H;
+        const int h = (int)(r - bt * H), x = (int)(e - r * vec);
+        const long long r0 = (2 * bt) * H + h, r1 = r0 + H;
+        const long long e0 = r0 * vec + x, e1 = r1 * vec + x;
+        kv[e0] = k[e];
+        kv[e1] = sk[e];
+        vv[e0] = v[e];
+        vv[e1] = sv[e];
+        qv[e0] = make_uint4(0u, 0u, 0u, 0u);
+        qv[e1] = q[e];
+        if (x == 0) {
+            bv[r0] = beta[r];
+            bv[r1] = alpha[r];
+            gv[r0] = gamma[r];
+            gv[r1] = __float2bfloat16(1.f);
+        }
+    }
+}
+
 template <typename Tin, typename Tout, bool SPARSE>
 cudaError_t run_d(int D, const ChunkArgs &a, cudaStream_t st) {
     switch (D) {
@@ -1009,6 +1062,21 @@ unsigned int read_scan_watchdog(cudaStream_t st) {
     return v;
 }
 
+// The sparse write on the tensor-core kernels: bf16, D = 128, a plain forward (the transition
+// and prep-reuse passes of the sequence-parallel path stay on the single-sample layout).
+static bool chunk_tc_pairs_eligible(int D, int dtype, int flags) {
+    return dtype == SGSA_DTYPE_BF16 && D == 128 && (flags & SGSA_FLAG_HAS_SPARSE) &&
+           !(flags & (SGSA_FLAG_TRANSITION | SGSA_FLAG_REUSE_PREP)) && scan_use_tc();
+}
+
+static size_t align256z(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Interleaved virtual inputs of the sparse write (q, k, v rows; beta, gamma scalars), bf16.
+static size_t pair_inputs_bytes(int B, int T, int H, int D) {
+    const size_t rows = (size_t)B * 2 * T * H;
+    return 3 * align256z(rows * D * 2) + 2 * align256z(rows * 2);
+}
+
 size_t chunk_delta_ws_bytes_pairs(long long pairs, int T, int D, int flags) {
     const int M = (flags & SGSA_FLAG_HAS_SPARSE) ? 2 * kC : kC;
     const size_t NC = (size_t)ceil_div(T, kC);
@@ -1022,7 +1090,16 @@ size_t chunk_delta_ws_bytes_pairs(long long pairs, int T, int D, int flags) {
 }
 
 size_t chunk_delta_ws_bytes(int B, int T, int H, int D, int flags) {
-    return chunk_delta_ws_bytes_pairs((long long)B * H, T, D, flags);
+    const size_t simt = chunk_delta_ws_bytes_pairs((long long)B * H, T, D, flags);
+    if (!((flags & SGSA_FLAG_HAS_SPARSE) && D == 128 &&
+          !(flags & (SGSA_FLAG_TRANSITION | SGSA_FLAG_REUSE_PREP))))
+        return simt;
+    // the size does not know the dtype: room for either the CUDA-core sparse layout or the
+    // tensor-core one (interleaved inputs + the single-sample operands of 2T rows)
+    const size_t tc = pair_inputs_bytes(B, T, H, D) +
+                      chunk_delta_ws_bytes_pairs((long long)B * H, 2 * T, D,
+                                                 flags & ~SGSA_FLAG_HAS_SPARSE);
+    return std::max(simt, tc);
 }
 
 int chunk_delta_group_pairs(int B, int T, int H, int D, int flags, size_t cap) {
@@ -1037,6 +1114,34 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
                                const void *alpha, const float *s0, void *o, float *sT, int B,
                                int T, int H, int D, int dtype, int flags, void *ws,
                                cudaStream_t st, size_t ws_cap, cudaEvent_t prep_done) {
+    if (chunk_tc_pairs_eligible(D, dtype, flags)) {
+        // the sparse write as 2T virtual samples on the tensor-core kernels: interleave, then
+        // the single-sample prep / scan with the pair mask; the scan writes token rows of o
+        const size_t rows = (size_t)B * T * H, vrows = 2 * rows, ib = pair_inputs_bytes(B, T, H, D);
+        if (ws_cap && ws_cap <= ib) return cudaErrorInvalidValue;
+        unsigned char *p = (unsigned char *)ws;
+        __nv_bfloat16 *qv = (__nv_bfloat16 *)p;
+        __nv_bfloat16 *kv = (__nv_bfloat16 *)(p += align256z(vrows * D * 2));
+        __nv_bfloat16 *vv = (__nv_bfloat16 *)(p += align256z(vrows * D * 2));
+        __nv_bfloat16 *bv = (__nv_bfloat16 *)(p += align256z(vrows * D * 2));
+        __nv_bfloat16 *gv = (__nv_bfloat16 *)(p += align256z(vrows * 2));
+        p += align256z(vrows * 2);
+        const int vec = D / 8;
+        const long long n = (long long)rows * vec;
+        const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+        pair_interleave_kernel<<<grid, 256, 0, st>>>(
+            (const uint4 *)q, (const uint4 *)k, (const uint4 *)v, (const uint4 *)sk,
+            (const uint4 *)sv, (const __nv_bfloat16 *)beta, (const __nv_bfloat16 *)gamma,
+            (const __nv_bfloat16 *)alpha, (uint4 *)qv, (uint4 *)kv, (uint4 *)vv, bv, gv,
+            (long long)rows, H, vec);
+        cudaError_t e = launched();
+        if (e != cudaSuccess) return e;
+        return launch_chunk_delta(qv, kv, vv, bv, gv, nullptr, nullptr, nullptr, s0, o, sT, B,
+                                  2 * T, H, D, dtype, (flags & ~SGSA_FLAG_HAS_SPARSE) | kFlagPairs,
+                                  p, st, ws_cap ? ws_cap - ib : 0, prep_done);
+    }
+    const bool pairs = flags & kFlagPairs;
+    flags &= ~kFlagPairs;
     const bool sparse = flags & SGSA_FLAG_HAS_SPARSE;
     const int M = sparse ? 2 * kC : kC;
     const int group = chunk_delta_group_pairs(B, T, H, D, flags, ws_cap);
@@ -1048,6 +1153,7 @@ cudaError_t launch_chunk_delta(const void *q, const void *k, const void *v, cons
     a.sT = (flags & SGSA_FLAG_STORE_FINAL) ? sT : nullptr;
     a.B = B; a.T = T; a.H = H; a.NC = ceil_div(T, kC);
     a.transition = (flags & SGSA_FLAG_TRANSITION) ? 1 : 0;
+    a.pairs = pairs ? 1 : 0;
     const bool tc = chunk_tc_eligible(D, dtype, flags);
     const bool of32 = (flags & SGSA_FLAG_OUT_F32) || dtype == SGSA_DTYPE_F32;
     // The (batch, head) pairs in groups whose per-chunk operands fit the workspace cap; the

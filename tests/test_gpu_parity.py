@@ -63,6 +63,32 @@ def test_chunk_matches_oracle(dtype, D, sparse, init):
     assert oracle.rel_l2(s, rs) < TOL[dtype]
 
 
+@pytest.mark.parametrize("T,out_f32", [(1, False), (33, True), (1000, False), (1000, True)])
+def test_sparse_write_tensor_core_path(T, out_f32, monkeypatch):
+    """bf16, D=128 with the sparse write runs the tensor-core chunk kernels on the
+    2T interleaved virtual samples (chunk_fwd.py:49-56) with the same-token mask
+    (dep_mask = tau_j < tau_i).  Checked against the float64 oracle at the bf16
+    tolerance and, with float32 outputs (two bf16-rounded outputs would carry two
+    roundings), against the CUDA-core sparse path on the same inputs."""
+    x = rand_case(2, T, 2, 128, torch.bfloat16, seed=T + 7, sparse=True, init=True)
+    d = dev(x)
+    o, s = ops.chunk_sgsa_fp32_state(d["q"], d["k"], d["v"], d["beta"], d["gamma"],
+                                     d["initial_state"], d["sparse_k"], d["sparse_v"], d["alpha"],
+                                     out_f32=out_f32)
+    ro, rs = oracle_chunk(x)
+    assert oracle.rel_l2(o.float().cpu().numpy(), ro) < 2e-3
+    assert oracle.rel_l2(s.float().cpu().numpy(), rs) < 2e-3
+    if not out_f32:
+        return
+    monkeypatch.setenv("SGSA_SCAN_SIMT", "1")  # the CUDA-core chunk kernels
+    o2, s2 = ops.chunk_sgsa_fp32_state(d["q"], d["k"], d["v"], d["beta"], d["gamma"],
+                                       d["initial_state"], d["sparse_k"], d["sparse_v"],
+                                       d["alpha"], out_f32=out_f32)
+    torch.cuda.synchronize()
+    assert oracle.rel_l2(o.float().cpu().numpy(), o2.float().cpu().numpy()) < 2e-3
+    assert oracle.rel_l2(s.float().cpu().numpy(), s2.float().cpu().numpy()) < 2e-3
+
+
 @pytest.mark.parametrize("T", [1, 63, 64, 65, 130])
 def test_chunk_ragged_lengths(T):
     x = rand_case(1, T, 2, 64, torch.float32, seed=T, sparse=True, init=True)
