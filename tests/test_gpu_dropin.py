@@ -72,3 +72,59 @@ def test_sgsa_state_layer_with_swapped_chunk_op(ref, monkeypatch, mode, hidden, 
     rel = lambda a, b: float((a.double() - b).norm() / b.norm())
     assert rel(out, want_out) < 1e-5
     assert rel(state, want_state) < 1e-5
+
+
+@pytest.mark.parametrize("mode", ["none", "direct", "residual"])
+def test_sgsa_state_layer_bf16_head_dim_128(ref, monkeypatch, mode):
+    """The reference layer in bfloat16 with head dim 128: the swapped op takes the
+    tensor-core chunk kernels (with the sparse write for "direct" / "residual").
+    The bf16 layer's own projections differ from a float64 layer by more than the op's
+    tolerance, so the op is checked on the exact tensors the layer hands it: its
+    output and final state against the float64 oracle at the bf16 bar (2e-3)."""
+    import inspect
+
+    from oracle import oracle
+
+    torch.manual_seed(1)
+    B, T, hidden, heads = 2, 300, 512, 4
+    cfg = ref.SGSAConfig(hidden_size=hidden, num_attention_heads=heads, num_kv_heads=heads,
+                         sgsa_write_mode=mode, linear_backend="torch_chunk")
+    layer = ref.SGSAStateLayer(cfg).cuda().eval().to(torch.bfloat16)
+    D = cfg.head_dim
+    bf = lambda t: t.to(torch.bfloat16)
+    hs = bf(torch.randn(B, T, hidden, device="cuda"))
+    q = bf(torch.nn.functional.normalize(torch.randn(B, T, heads, D, device="cuda"), dim=-1))
+    k = bf(torch.nn.functional.normalize(torch.randn(B, T, heads, D, device="cuda"), dim=-1))
+    v = bf(torch.randn(B, T, heads, D, device="cuda"))
+    k_hat = bf(torch.nn.functional.normalize(torch.randn(B, T, heads, D, device="cuda"), dim=-1))
+    v_hat = bf(torch.randn(B, T, heads, D, device="cuda"))
+    diag = {"concentration": bf(torch.rand(B, heads, T, device="cuda")),
+            "novelty": bf(torch.rand(B, heads, T, device="cuda"))}
+    seen = []
+    sig = inspect.signature(sgsa_b200.chunk_sgsa)
+
+    def ours(*a, **kw):
+        r = sgsa_b200.chunk_sgsa(*a, **kw)
+        args = sig.bind(*a, **kw)
+        args.apply_defaults()
+        seen.append((dict(args.arguments), r))
+        return r
+
+    monkeypatch.setattr(ref, "chunk_sgsa", ours)
+    with torch.no_grad():
+        out, state, stats = layer(hs, q, k, v, k_hat, v_hat, diag)
+    torch.cuda.synchronize()
+    assert seen and float(stats["used_torch_chunk"]) == 1.0
+    assert torch.isfinite(out.float()).all()
+    args, (o, st) = seen[-1]
+    assert args["q"].dtype == torch.bfloat16 and args["q"].shape[-1] == 128
+    sparse = args.get("sparse_k") is not None
+    assert sparse == (mode != "none")
+    c = lambda t: None if t is None else t.detach().float().cpu()
+    ro, rs = oracle.sgsa_recurrent(c(args["q"]), c(args["k"]), c(args["v"]), c(args["beta"]),
+                                   c(args["gamma"]), c(args.get("sparse_k")),
+                                   c(args.get("sparse_v")), c(args.get("alpha")),
+                                   c(args.get("initial_state")))
+    assert oracle.rel_l2(o.float().cpu().numpy(), ro) < 2e-3
+    if st is not None:
+        assert oracle.rel_l2(st.float().cpu().numpy(), rs) < 2e-3
