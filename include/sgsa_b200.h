@@ -106,6 +106,10 @@ int sgsa_check_status(unsigned int *word, int reset);
  * naive_recurrent_sgsa (modelings/sgsa_ops/naive.py:39-55): no query scale,
  * o_t = S_t^T q_t.  d_k == d_v == D, D in {32, 64, 128}; chunk_size == 64.
  * sparse_k/sparse_v/alpha may be NULL unless SGSA_FLAG_HAS_SPARSE is set.
+ * bf16 with D == 128 runs on the tensor cores, the sparse write included (its
+ * two samples per token as 2T interleaved rows); the workspace size covers
+ * that layout and the CUDA-core one, since it does not take the dtype.  Flag
+ * bits outside SGSA_FLAG_* are ignored.
  */
 size_t sgsa_chunk_fwd_workspace_size(int B, int T, int H, int D, int flags);
 int sgsa_chunk_fwd(const void *q, const void *k, const void *v, const void *beta,
