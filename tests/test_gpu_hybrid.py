@@ -97,3 +97,62 @@ def test_tiny_model_logits_match_oracle(dtype, tol):
     assert oracle.rel_l2(logits.numpy(), ref.numpy()) < tol
     last = m(ids.cuda(), last_only=True).float().cpu()
     assert oracle.rel_l2(last.numpy(), logits[:, -1].numpy()) < (1e-6 if dtype == torch.float32 else 1e-2)
+
+
+def test_bf16_model_blocks_match_oracle_one_at_a_time():
+    """The bf16 model pinned block by block, tighter than the whole-model bar.
+
+    Each layer's attention increment and MLP increment (the residual left out, so the
+    residual stream's size does not hide their errors) are computed on the device from the
+    device's own bf16 residual stream, and by the oracle in float64 from the same bf16
+    values (for the SGSA core, from the device's own bf16 projections, which are pinned
+    against the oracle's separately: top-k sets chosen from differently rounded indexer
+    scores legitimately differ at near ties).  One block chains a handful of bf16 roundings (norm, projection, core, output
+    projection), so the bar is 1e-2 per increment instead of the whole model's 4e-2."""
+    cfg = hybrid.TINY
+    m = HybridSGSAModel(cfg, device="cuda", dtype=torch.bfloat16, seed=3)
+    ids = torch.randint(1, cfg.vocab_size, (2, 256), generator=torch.Generator().manual_seed(5))
+    B, T = ids.shape
+    N, I = cfg.hidden_size, cfg.intermediate_size
+    H, D, DI = cfg.num_heads, cfg.head_dim, cfg.indexer_dim
+    f64 = lambda t: t.detach().double().cpu()
+    with torch.no_grad():
+        x = hybrid.embed(ids.cuda(), m.weights["embed"])
+        for li, lw in enumerate(m.weights["layers"]):
+            w = {n: f64(t) for n, t in lw.items()}
+            # attention increment
+            h = hybrid.rmsnorm(x, lw["norm1"], cfg.eps)
+            zero = torch.zeros_like(x)
+            if cfg.is_dense(li):
+                inc = m.dense_attention(h, lw, zero)
+                hr = ohybrid.rmsnorm(f64(x), w["norm1"], cfg.eps)
+                wq, wk, wv = w["w_qkv"].chunk(3, 0)
+                want = ohybrid.dense_attention(hr, wq, wk, wv, w["w_o"], H, cfg.rope_theta)
+            else:
+                inc = m.sgsa_attention(h, lw, zero)
+                # the projection pinned on its own; the core and the output projection then
+                # on the device's own bf16 projections, so that top-k sets are chosen from
+                # the same rounded indexer scores on both sides (as in the layer tests)
+                hr = ohybrid.rmsnorm(f64(x), w["norm1"], cfg.eps)
+                a = ohybrid.sgsa_projection(hr, w["w_in"], w["b_in"], H, D, DI)
+                P = torch.addmm(lw["b_in"], h.view(B * T, N), lw["w_in"].T).view(B, T, -1)
+                ad = {n: f64(t) for n, t in hybrid.layer_proj(P, H, D, DI).items()}
+                for n in a:
+                    e = oracle.rel_l2(ad[n].numpy(), a[n].double().numpy())
+                    assert e < 1e-2, (li, n, e)
+                out, _, _, _ = oracle.sgsa_layer(ad["q"], ad["k"], ad["v"], ad["beta"], ad["gamma"],
+                                                 ad["iq"], ad["ik"], ad["mix"], cfg.top_k)
+                want = torch.from_numpy(np.asarray(out)).double().reshape(B, T, -1) @ w["w_o"].T
+            e_att = oracle.rel_l2(f64(inc).numpy(), want.numpy())
+            x = (x + inc).to(x.dtype)
+            # MLP increment
+            h2 = hybrid.rmsnorm(x, lw["norm2"], cfg.eps)
+            gu = torch.matmul(h2.view(B * T, N), lw["w_gu"].T)
+            inc2 = torch.matmul(hybrid.swiglu(gu), lw["w_down"].T).view(B, T, N)
+            hr2 = ohybrid.rmsnorm(f64(x), w["norm2"], cfg.eps)
+            want2 = ohybrid.swiglu(hr2, w["w_gu"][:I], w["w_gu"][I:], w["w_down"])
+            e_mlp = oracle.rel_l2(f64(inc2).numpy(), want2.numpy())
+            print(f"layer {li} ({'dense' if cfg.is_dense(li) else 'sgsa'}): "
+                  f"attention {e_att:.2e}, mlp {e_mlp:.2e}")
+            assert e_att < 1e-2 and e_mlp < 1e-2, (li, e_att, e_mlp)
+            x = (x + inc2).to(x.dtype)
