@@ -86,6 +86,21 @@ def test_noalloc_tensor_core_path_near_the_limit():
         assert _rel(ns, rs) <= 2e-3
 
 
+def test_noalloc_sparse_write_on_the_tensor_cores():
+    """bf16, D=128 with the sparse write: the tensor-core chunk kernels on the 2T
+    interleaved samples, whose interleaved inputs also live in the scratch array."""
+    lib = _lib.load()
+    B, T, H, D = 1, 1000, 4, 128
+    flags = _lib.FLAG_HAS_SPARSE | _lib.FLAG_HAS_INIT | _lib.FLAG_STORE_FINAL
+    assert lib.sgsa_chunk_fwd_workspace_size(B, T, H, D, flags) <= (64 << 20)
+    for seed in (4, 5):
+        x = _inputs(torch.bfloat16, B=B, T=T, H=H, D=D, seed=seed)
+        ro, rs = _call(lib, "regular", x, torch.bfloat16, flags)
+        no, ns = _call(lib, "noalloc", x, torch.bfloat16, flags)
+        assert _rel(no, ro) <= 2e-3
+        assert _rel(ns, rs) <= 2e-3
+
+
 def test_noalloc_refuses_prep_reuse():
     """Reusing prep operands would read whatever an earlier call left in the shared
     scratch, so the flag is refused before anything is launched."""
