@@ -122,17 +122,40 @@ __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
     }
     if (tid < DI) s_q[tid] = to_f32(iq[(size_t)bh * DI + tid]);
     __syncthreads();
-    for (int j = tid; j < n; j += kTopkThreads) {
-        const Tin *kr = ikc + (((size_t)b * Tc + j) * H + h) * DI;
-        float s = 0.f;
+    {
+        // Scores: DI / 8 lanes per cached row, one 16-byte load each (a row's DI values
+        // in one coalesced request; rows of one head are H * DI elements apart), the
+        // partial dots summed by xor shuffles; kU rows per lane group in flight.
+        constexpr int G = DI / 8, RPW = 32 / G, kU = 8;
+        const int warp = tid >> 5, lane = tid & 31, sub = lane % G, r0 = lane / G;
+        constexpr int step = (kTopkThreads / 32) * RPW;
+        float qv[8];
 #pragma unroll
-        for (int d0 = 0; d0 < DI; d0 += 8) {
-            float x[8];
-            load8(kr + d0, x);
+        for (int i = 0; i < 8; ++i) qv[i] = s_q[sub * 8 + i];
+        const Tin *base = ikc + ((size_t)b * Tc * H + h) * DI + sub * 8;
+        for (int jb = warp * RPW; jb < n; jb += step * kU) {  // warp-uniform
+            float x[kU][8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s = fmaf(s_q[d0 + i], x[i], s);
+            for (int u = 0; u < kU; ++u) {
+                const int j = jb + u * step + r0;
+                if (j < n) {
+                    load8(base + (size_t)j * H * DI, x[u]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) x[u][i] = 0.f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                float s = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s = fmaf(qv[i], x[u][i], s);
+#pragma unroll
+                for (int off = G / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+                const int j = jb + u * step + r0;
+                if (sub == 0 && j < n) keys[j] = float_key(s);
+            }
         }
-        keys[j] = float_key(s);
     }
     if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = K; s_done = 0; }
     __syncthreads();
