@@ -168,17 +168,43 @@ __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
             if ((u & msk) == pre) atomicAdd(&hist[(u >> shift) & 0xffu], 1u);
         }
         __syncthreads();
-        if (tid == 0) {
-            int cum = 0, chosen = 0, cnt = 0;
-            for (int bin = 255; bin >= 0; --bin) {
-                cnt = (int)hist[bin];
-                if (cum + cnt >= s_need) { chosen = bin; break; }
-                cum += cnt;
+        if (tid < 32) {
+            const int lane = tid;
+            // the bin that holds the need-th largest key: lane l sums bins 255-8l .. 248-8l,
+            // an inclusive scan over lanes from the top, the first lane that reaches
+            // `need` walks its eight bins
+            const int need = s_need;
+            uint32_t c[8];
+            int tot = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { c[i] = hist[255 - 8 * lane - i]; tot += (int)c[i]; }
+            int incl = tot;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += y;
             }
-            s_need -= cum;
-            s_prefix |= (uint32_t)chosen << shift;
-            s_mask |= 0xffu << shift;
-            if (cnt == s_need) s_done = 1;
+            const uint32_t hit = __ballot_sync(0xffffffffu, incl >= need);
+            const int total = __shfl_sync(0xffffffffu, incl, 31);
+            const int L = hit ? __ffs(hit) - 1 : -1;
+            if (L < 0) {  // not reached (the active keys number at least `need`): bin 0
+                if (lane == 0) {
+                    s_need = need - total;
+                    s_mask |= 0xffu << shift;
+                    if ((int)hist[0] == s_need) s_done = 1;
+                }
+            } else if (lane == L) {
+                int cum = incl - tot, chosen = 0, cnt = 0;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if (cum + (int)c[i] >= need) { chosen = 255 - 8 * lane - i; cnt = (int)c[i]; break; }
+                    cum += (int)c[i];
+                }
+                s_need = need - cum;
+                s_prefix |= (uint32_t)chosen << shift;
+                s_mask |= 0xffu << shift;
+                if (cnt == s_need) s_done = 1;
+            }
         }
         __syncthreads();
     }
