@@ -308,7 +308,7 @@ int sgsa_recurrent_fwd(const void *q, const void *k, const void *v, const void *
  * Decode-time indexer: for each (b, h), the top-k of iq[b,h] . ik_cache[b,j,h]
  * over the cache positions j < n (the current token included), ties to the
  * lowest j, ascending, -1 padded.  iq [B,H,DI]; ik_cache [B,Tc,H,DI] (Tc the
- * allocated cache length, n <= Tc and n <= 57344).  The decode form of the
+ * allocated cache length, n <= Tc and n <= 55296).  The decode form of the
  * selection of modelings/hybrid_dense_delta_topk.py:343-349, which the
  * reference re-scores against the whole cache at every step (:343-349 with
  * the cache of :226-230).

@@ -386,7 +386,7 @@ cudaError_t run_dattn(const void *q, const void *kc, const void *vc, const int32
 
 }  // namespace
 
-constexpr int kDecodeMaxCache = 56 * 1024;  // scores of one row in shared memory
+constexpr int kDecodeMaxCache = 54 * 1024;  // scores of one row in shared memory (+ static, <= 227 KB)
 
 int decode_max_cache() { return kDecodeMaxCache; }
 

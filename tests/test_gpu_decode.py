@@ -119,3 +119,30 @@ def test_decode_cache_steps_match_oracle(reuse):
             idx = oracle.decode_topk(iq, ikc_o, n + 1, K)
         want = oracle.decode_attn_mix(q, kc_o, vc_o, idx, od[:, 0], mix)
         assert oracle.rel_l2(got.float().cpu().numpy(), want) < 2e-3
+
+
+def test_decode_topk_at_the_longest_cache():
+    """The longest cache the refresh accepts (every score of a row in shared memory)
+    runs and matches the oracle; one more row is refused."""
+    import ctypes
+
+    from sgsa_b200 import _lib
+
+    lib = _lib.load()
+    n = 54 * 1024
+    r = _gen(7)
+    iq = r(1, 1, 64).to(torch.bfloat16)
+    ikc = r(1, n, 1, 64).to(torch.bfloat16)
+    got = ops.decode_topk(iq.cuda(), ikc.cuda(), n, 256).cpu().numpy()
+    want, kth = oracle.decode_topk(iq, ikc, n, 256, return_kth=True)
+    if not np.array_equal(got, want):
+        s = np.einsum("bhd,bjhd->bhj", iq.double().numpy(), ikc.double().numpy())
+        a, w = set(got[0, 0].tolist()), set(want[0, 0].tolist())
+        for j in a ^ w:
+            assert abs(s[0, 0, j] - kth[0, 0]) <= 1e-5 * max(1.0, abs(kth[0, 0]))
+    big = torch.zeros(1, n + 1, 1, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(1, 1, 256, dtype=torch.int32, device="cuda")
+    rc = lib.sgsa_decode_topk(iq.cuda().data_ptr(), big.data_ptr(), out.data_ptr(), 1, 1, n + 1,
+                              n + 1, 64, 256, _lib.DTYPE_BF16,
+                              torch.cuda.current_stream().cuda_stream)
+    assert rc == -6  # SGSA_ERR_UNSUPPORTED
