@@ -208,44 +208,45 @@ __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
         }
         __syncthreads();
     }
-    // ordered compaction: thread tid owns the contiguous index segment [lo, hi)
-    const uint32_t pre = s_prefix, msk = s_mask;
-    const int need = s_need;
-    const int seg = (n + kTopkThreads - 1) / kTopkThreads;
-    const int lo = min(n, tid * seg), hi = min(n, lo + seg);
-    int gt = 0, eq = 0;
-    for (int j = lo; j < hi; ++j) {
-        const uint32_t m = keys[j] & msk;
-        gt += m > pre;
-        eq += m == pre;
-    }
-    // exclusive scan of the equal counts, then of the output counts
-    s_scan[tid] = eq;
-    __syncthreads();
-    for (int off = 1; off < kTopkThreads; off <<= 1) {
-        const int x = (tid >= off) ? s_scan[tid - off] : 0;
+    // Ordered compaction: warp w owns the contiguous index segment [lo, hi) and reads it
+    // 32 consecutive keys at a time (lane i the i-th: no bank conflicts).  Pass 1 counts the
+    // keys above the threshold prefix (gt) and equal to it (eq) per warp; after one exchange
+    // of the warp totals, pass 2 emits in index order, the equal keys by rank (lowest
+    // indices first) while fewer than `need` have been taken.
+    {
+        constexpr int kWarps = kTopkThreads / 32;
+        const uint32_t pre = s_prefix, msk = s_mask;
+        const int need = s_need;
+        const int warp = tid >> 5, lane = tid & 31;
+        const uint32_t lt = (1u << lane) - 1u;
+        const int seg = (n + kWarps - 1) / kWarps;
+        const int lo = min(n, warp * seg), hi = min(n, lo + seg);
+        int gt = 0, eq = 0;
+        for (int j0 = lo; j0 < hi; j0 += 32) {
+            const int j = j0 + lane;
+            const uint32_t m = j < hi ? (keys[j] & msk) : 0u;
+            gt += __popc(__ballot_sync(0xffffffffu, j < hi && m > pre));
+            eq += __popc(__ballot_sync(0xffffffffu, j < hi && m == pre));
+        }
+        if (lane == 0) { s_scan[2 * warp] = gt; s_scan[2 * warp + 1] = eq; }
         __syncthreads();
-        s_scan[tid] += x;
-        __syncthreads();
-    }
-    const int eq_before = s_scan[tid] - eq;
-    const int take_eq = max(0, min(eq, need - eq_before));
-    __syncthreads();
-    s_scan[tid] = gt + take_eq;
-    __syncthreads();
-    for (int off = 1; off < kTopkThreads; off <<= 1) {
-        const int x = (tid >= off) ? s_scan[tid - off] : 0;
-        __syncthreads();
-        s_scan[tid] += x;
-        __syncthreads();
-    }
-    int pos = s_scan[tid] - (gt + take_eq);
-    int taken = 0;
-    for (int j = lo; j < hi; ++j) {
-        const uint32_t m = keys[j] & msk;
-        if (m > pre || (m == pre && taken < take_eq)) {
-            if (m == pre) ++taken;
-            out[pos++] = j;
+        int eq_before = 0, out_before = 0;
+        for (int w = 0; w < warp; ++w) {
+            const int g = s_scan[2 * w], e = s_scan[2 * w + 1];
+            out_before += g + max(0, min(e, need - eq_before));
+            eq_before += e;
+        }
+        int pos = out_before, eq_rank = eq_before;
+        for (int j0 = lo; j0 < hi; j0 += 32) {
+            const int j = j0 + lane;
+            const uint32_t m = j < hi ? (keys[j] & msk) : 0u;
+            const bool is_gt = j < hi && m > pre, is_eq = j < hi && m == pre;
+            const uint32_t eqb = __ballot_sync(0xffffffffu, is_eq);
+            const bool take = is_gt || (is_eq && eq_rank + __popc(eqb & lt) < need);
+            const uint32_t tb = __ballot_sync(0xffffffffu, take);
+            if (take) out[pos + __popc(tb & lt)] = j;
+            pos += __popc(tb);
+            eq_rank += __popc(eqb);
         }
     }
 }
