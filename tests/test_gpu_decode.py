@@ -22,9 +22,10 @@ def _gen(seed):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("D", [32, 64, 128])
 @pytest.mark.parametrize("sparse", [False, True])
-def test_fused_recurrent_matches_oracle(dtype, D, sparse):
+@pytest.mark.parametrize("T", [97, 1])  # T == 1 is the decode step's kernel
+def test_fused_recurrent_matches_oracle(dtype, D, sparse, T):
     r = _gen(D + sparse)
-    B, T, H = 2, 97, 3
+    B, H = 2, 3
     x = dict(q=torch.nn.functional.normalize(r(B, T, H, D), dim=-1),
              k=torch.nn.functional.normalize(r(B, T, H, D), dim=-1), v=r(B, T, H, D),
              beta=torch.sigmoid(r(B, T, H)),
