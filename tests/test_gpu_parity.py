@@ -388,14 +388,15 @@ def test_sparse_retrieve_reference_fixture():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_sparse_write_block_matches_oracle(dtype):
+@pytest.mark.parametrize("D", [64, 128])  # bf16 at 128: the tensor-core chunk kernels
+def test_sparse_write_block_matches_oracle(dtype, D):
     """Retrieval (q . k top-k), k_hat / v_hat, then the delta rule with the sparse write.
 
     The two halves are pinned separately at the plain tolerance: the retrieval
     against the oracle's k_hat / v_hat, and the recurrence with the sparse write
     against the oracle fed the device's own (dtype-rounded) k_hat / v_hat, so the
     rounding of k_hat to the input dtype is not charged to the recurrence."""
-    x = rand_case(2, 300, 2, 64, dtype, seed=21, sparse=True, init=True)
+    x = rand_case(2, 300, 2, D, dtype, seed=21, sparse=True, init=True)
     K = 32
     d = dev(x)
     o, st = ops.sgsa_sparse_write_fwd(d["q"], d["k"], d["v"], d["beta"], d["gamma"], d["alpha"],
