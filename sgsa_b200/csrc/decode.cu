@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(D) recurrent_sgsa_kernel(
 }
 
 // ------------------------------------------------------------- decode top-k
-constexpr int kTopkThreads = 512;
+constexpr int kTopkThreads = 1024;
 
 template <typename Tin, int DI>
 __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
         // Scores: DI / 8 lanes per cached row, one 16-byte load each (a row's DI values
         // in one coalesced request; rows of one head are H * DI elements apart), the
         // partial dots summed by xor shuffles; kU rows per lane group in flight.
-        constexpr int G = DI / 8, RPW = 32 / G, kU = 8;
+        constexpr int G = DI / 8, RPW = 32 / G, kU = 4;
         const int warp = tid >> 5, lane = tid & 31, sub = lane % G, r0 = lane / G;
         constexpr int step = (kTopkThreads / 32) * RPW;
         float qv[8];
