@@ -305,6 +305,18 @@ int sgsa_recurrent_fwd(const void *q, const void *k, const void *v, const void *
                        void *stream);
 
 /*
+ * Decode cache append: row `pos` of k_cache / v_cache [B,Tc,H,D] and ik_cache
+ * [B,Tc,H,DI] from this token's k, v [B,H,D] and ik [B,H,DI] (same dtype as the
+ * caches), every batch row in one launch.  Replaces the per-step key/value cache
+ * growth of the reference's decode (torch.cat of the past and new rows,
+ * modelings/hybrid_dense_delta_topk.py:226-230); here the caches are allocated
+ * once at their full length.  All pointers 16-byte aligned; 0 <= pos < Tc.
+ */
+int sgsa_decode_append(void *k_cache, void *v_cache, void *ik_cache, const void *k,
+                       const void *v, const void *ik, int B, int Tc, int H, int D, int DI,
+                       int pos, int dtype, void *stream);
+
+/*
  * Decode-time indexer: for each (b, h), the top-k of iq[b,h] . ik_cache[b,j,h]
  * over the cache positions j < n (the current token included), ties to the
  * lowest j, ascending, -1 padded.  iq [B,H,DI]; ik_cache [B,Tc,H,DI] (Tc the

@@ -51,6 +51,7 @@ SIGNATURES = {
     "sgsa_embed": (_i, [_vp] * 3 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_gate_mix": (_i, [_vp] * 4 + [ctypes.c_longlong, _i, _i, _i, _vp]),
     "sgsa_recurrent_fwd": (_i, [_vp] * 11 + [_i] * 6 + [_vp]),
+    "sgsa_decode_append": (_i, [_vp] * 6 + [_i] * 7 + [_vp]),
     "sgsa_decode_topk": (_i, [_vp] * 3 + [_i] * 7 + [_vp]),
     "sgsa_decode_attn_mix": (_i, [_vp] * 7 + [_i] * 5 + [ctypes.c_float, _i, _i, _vp]),
     "sgsa_layer_fwd_workspace_size": (_sz, [_i] * 8),

@@ -466,6 +466,24 @@ int sgsa_recurrent_fwd(const void *q, const void *k, const void *v, const void *
     return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
 }
 
+int sgsa_decode_append(void *k_cache, void *v_cache, void *ik_cache, const void *k,
+                       const void *v, const void *ik, int B, int Tc, int H, int D, int DI,
+                       int pos, int dtype, void *stream) {
+    if (B < 0 || H < 0 || Tc <= 0 || pos < 0 || pos >= Tc) return SGSA_ERR_SHAPE;
+    if (!head_dim_ok(D) || (DI != 32 && DI != 64 && DI != 128)) return SGSA_ERR_SHAPE;
+    if (!dtype_ok(dtype)) return SGSA_ERR_DTYPE;
+    if ((size_t)B * H == 0) return SGSA_OK;
+    if (!k_cache || !v_cache || !ik_cache || !k || !v || !ik) return SGSA_ERR_NULL;
+    const uintptr_t any = (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)ik_cache |
+                          (uintptr_t)k | (uintptr_t)v | (uintptr_t)ik;
+    if (any & 15) return SGSA_ERR_SHAPE;  // 16-byte vectors
+    if (int s = check_device()) return s;
+    cudaError_t e = sgsa::launch_decode_append(k_cache, v_cache, ik_cache, k, v, ik, B, Tc, H, D,
+                                               DI, pos, dtype == SGSA_DTYPE_F32 ? 4 : 2,
+                                               (cudaStream_t)stream);
+    return e == cudaSuccess ? SGSA_OK : fail_cuda(e);
+}
+
 int sgsa_decode_topk(const void *iq, const void *ik_cache, int32_t *indices, int B, int H,
                      int Tc, int n, int DI, int top_k, int dtype, void *stream) {
     if (B < 0 || H < 0 || Tc < 0 || n < 0 || n > Tc || top_k <= 0) return SGSA_ERR_SHAPE;

@@ -110,6 +110,9 @@ cudaError_t launch_recurrent(const void *q, const void *k, const void *v, const 
                              const void *gamma, const void *sk, const void *sv, const void *alpha,
                              const float *s0, void *o, float *sT, int B, int T, int H, int D,
                              int dtype, bool out_f32, cudaStream_t st);
+cudaError_t launch_decode_append(void *kc, void *vc, void *ikc, const void *k, const void *v,
+                                 const void *ik, int B, int Tc, int H, int D, int DI, int pos,
+                                 int elem_bytes, cudaStream_t st);
 cudaError_t launch_decode_topk(const void *iq, const void *ikc, int32_t *idx, int B, int H,
                                int Tc, int n, int DI, int K, int dtype, cudaStream_t st);
 cudaError_t launch_decode_attn(const void *q, const void *kc, const void *vc, const int32_t *idx,

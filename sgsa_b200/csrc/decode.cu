@@ -14,6 +14,8 @@
 // * decode_attn_kernel: softmax attention of one query over its selected cache
 //   rows plus the gate (one CTA per (b, h), 8 warps split the rows, online
 //   softmax states merged through shared memory).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace sgsa {
@@ -251,6 +253,25 @@ __global__ void __launch_bounds__(kTopkThreads) decode_topk_kernel(
     }
 }
 
+// ------------------------------------------------------------ cache append
+// Row `pos` of the k, v and indexer-key caches from this token's k, v and ik, every batch
+// row, in one launch: 16-byte vectors, 64-bit row offsets (a [B, Tc, H, D] cache passes 2^31
+// elements at configs[4] sizes).
+__global__ void __launch_bounds__(256)
+decode_append_kernel(uint4 *__restrict__ kc, uint4 *__restrict__ vc, uint4 *__restrict__ ikc,
+                     const uint4 *__restrict__ k, const uint4 *__restrict__ v,
+                     const uint4 *__restrict__ ik, int B, long long Tc, int nkv, int nik,
+                     long long pos) {
+    const long long per = 2LL * nkv + nik, n = (long long)B * per;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long b = e / per, x = e - b * per, row = b * Tc + pos;
+        if (x < nkv) kc[row * nkv + x] = k[b * nkv + x];
+        else if (x < 2 * nkv) vc[row * nkv + x - nkv] = v[b * nkv + x - nkv];
+        else ikc[row * nik + x - 2 * nkv] = ik[b * nik + x - 2 * nkv];
+    }
+}
+
 // ------------------------------------------------------- decode attention
 constexpr int kAttnWarps = 4;  // 4 measured faster than 8 or 16 at configs[4]
 static_assert(kAttnWarps * 32 >= 128, "the merge writes output column c from thread c (D <= 128)");
@@ -438,6 +459,18 @@ unsigned int check_word_decode(bool reset) {
     if (cudaMemcpyFromSymbol(&v, g_check, sizeof(v)) != cudaSuccess) return 0xffffffffu;
     if (reset && v) cudaMemcpyToSymbol(g_check, &z, sizeof(z));
     return v;
+}
+
+cudaError_t launch_decode_append(void *kc, void *vc, void *ikc, const void *k, const void *v,
+                                 const void *ik, int B, int Tc, int H, int D, int DI, int pos,
+                                 int elem_bytes, cudaStream_t st) {
+    const int nkv = H * D * elem_bytes / 16, nik = H * DI * elem_bytes / 16;
+    const long long n = (long long)B * (2LL * nkv + nik);
+    const int grid = (int)std::min<long long>((n + 255) / 256, 148LL * 8);
+    decode_append_kernel<<<grid, 256, 0, st>>>((uint4 *)kc, (uint4 *)vc, (uint4 *)ikc,
+                                                (const uint4 *)k, (const uint4 *)v,
+                                                (const uint4 *)ik, B, Tc, nkv, nik, pos);
+    return launched();
 }
 
 }  // namespace sgsa

@@ -500,14 +500,31 @@ class DecodeCache:
         if self.n >= self.k.shape[1]:
             raise ValueError("decode cache is full")
         o_d, self.state = chunk_free_recurrent_step(q, k, v, beta, gamma, self.state)
-        self.k[:, self.n] = k
-        self.v[:, self.n] = v
-        self.ik[:, self.n] = ik
+        decode_append(self.k, self.v, self.ik, k, v, ik, self.n)
         self.n += 1
         if self.indices is None or self.steps % self.reuse == 0:
             self.indices = decode_topk(iq, self.ik, self.n, self.top_k)
         self.steps += 1
         return decode_attn_mix(q, self.k, self.v, self.indices, o_d, mix)
+
+
+def decode_append(k_cache: Tensor, v_cache: Tensor, ik_cache: Tensor, k: Tensor, v: Tensor,
+                  ik: Tensor, pos: int) -> None:
+    """Row ``pos`` of the [B, Tc, H, *] caches from one token's k, v [B, H, D] and ik
+    [B, H, DI], in one launch (the reference grows its caches by torch.cat,
+    hybrid_dense_delta_topk.py:226-230)."""
+    B, Tc, H, D = k_cache.shape
+    DI = ik_cache.shape[-1]
+    for n, t in (("k_cache", k_cache), ("v_cache", v_cache), ("ik_cache", ik_cache)):
+        _dev(t, n)
+        if not t.is_contiguous() or t.dtype != k_cache.dtype:
+            raise ValueError(f"{n} must be contiguous and of the caches' dtype")
+    cast = lambda t: t.to(k_cache.dtype).contiguous()
+    k, v, ik = cast(k), cast(v), cast(ik)
+    st = _lib.load().sgsa_decode_append(_ptr(k_cache), _ptr(v_cache), _ptr(ik_cache), _ptr(k),
+                                        _ptr(v), _ptr(ik), B, Tc, H, D, DI, pos,
+                                        _dtype_code(k_cache), _stream(k_cache))
+    _lib.check(st, "sgsa_decode_append", k_cache)
 
 
 def chunk_free_recurrent_step(q, k, v, beta, gamma, state):

@@ -147,3 +147,29 @@ def test_decode_topk_at_the_longest_cache():
                               n + 1, 64, 256, _lib.DTYPE_BF16,
                               torch.cuda.current_stream().cuda_stream)
     assert rc == -6  # SGSA_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_append_matches_indexing(dtype):
+    """sgsa_decode_append writes exactly row `pos` of the three caches (the same result as
+    tensor indexing) and refuses a position outside the cache."""
+    from sgsa_b200 import _lib
+
+    r = _gen(11)
+    B, Tc, H, D, DI = 3, 50, 4, 128, 64
+    kc, vc, ikc = (r(B, Tc, H, D).to(dtype).cuda(), r(B, Tc, H, D).to(dtype).cuda(),
+                   r(B, Tc, H, DI).to(dtype).cuda())
+    want = [t.clone() for t in (kc, vc, ikc)]
+    k, v, ik = r(B, H, D).to(dtype).cuda(), r(B, H, D).to(dtype).cuda(), r(B, H, DI).to(dtype).cuda()
+    for pos in (0, 17, Tc - 1):
+        ops.decode_append(kc, vc, ikc, k, v, ik, pos)
+        want[0][:, pos], want[1][:, pos], want[2][:, pos] = k, v, ik
+    torch.cuda.synchronize()
+    for got, w in zip((kc, vc, ikc), want):
+        assert torch.equal(got, w)
+    lib = _lib.load()
+    rc = lib.sgsa_decode_append(kc.data_ptr(), vc.data_ptr(), ikc.data_ptr(), k.data_ptr(),
+                                v.data_ptr(), ik.data_ptr(), B, Tc, H, D, DI, Tc,
+                                _lib.DTYPE_F32 if dtype == torch.float32 else _lib.DTYPE_BF16,
+                                torch.cuda.current_stream().cuda_stream)
+    assert rc != 0
