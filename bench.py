@@ -814,10 +814,11 @@ def run_ours(args, ws, rank, local):
     def e2e_step():
         ops.sgsa_layer_fwd_from_host(*(pinned[n] for n in names), cfg.top_k, out=out_host)
 
-    for _ in range(2):
+    for _ in range(3):
         e2e_step()
     barrier(ws)
-    e2e_steps = max(1, min(args.steps, 5))
+    # the host link's time varies from call to call: average over up to 20 steps (~0.3 s)
+    e2e_steps = max(1, min(2 * args.steps, 20))
     e0.record(st)
     for _ in range(e2e_steps):
         e2e_step()
