@@ -296,42 +296,57 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attn_kernel(
     float m = -INFINITY, l = 0.f, acc[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) acc[e] = 0.f;
-    // slot s is handled by warp (s / 2) % kAttnWarps, half s % 2; both halves of a
-    // warp run the same number of iterations (the shuffles need the whole warp)
-    for (int base = 2 * warp; base < K; base += 2 * kAttnWarps) {
-        const int s = base + half;
-        int j = (s < K) ? ix[s] : -1;
-        if (kCheckBuild && s < K && (j < -1 || j >= Tc)) SGSA_CHECK_FAIL(g_check, kChkDecodeIndex);
-        if ((unsigned)j >= (unsigned)Tc) j = -1;  // out-of-range rows count as padding
-        float d0 = 0.f;
-        float kr[EPL], vr[EPL];
-        if (j >= 0) {
-            if constexpr (EPL == 8) {
-                load8(kb + (size_t)j * stride, kr);
-                load8(vb + (size_t)j * stride, vr);
+    // slot s is handled by warp (s / 2) % kAttnWarps, half s % 2, in increasing order; each
+    // iteration takes kRowsU of a half's slots, their index loads first, then all their k and
+    // v rows, so that the gathers of kRowsU rows are in flight together.  Both halves of a
+    // warp run the same number of iterations (the shuffles need the whole warp).
+    constexpr int kRowsU = 2, kStep = 2 * kAttnWarps;
+    for (int base = 2 * warp; base < K; base += kStep * kRowsU) {
+        int js[kRowsU];
+#pragma unroll
+        for (int u = 0; u < kRowsU; ++u) {
+            const int s = base + u * kStep + half;
+            int j = (s < K) ? ix[s] : -1;
+            if (kCheckBuild && s < K && (j < -1 || j >= Tc)) SGSA_CHECK_FAIL(g_check, kChkDecodeIndex);
+            if ((unsigned)j >= (unsigned)Tc) j = -1;  // out-of-range rows count as padding
+            js[u] = j;
+        }
+        float kr[kRowsU][EPL], vr[kRowsU][EPL];
+#pragma unroll
+        for (int u = 0; u < kRowsU; ++u) {
+            const int j = js[u];
+            if (j >= 0) {
+                if constexpr (EPL == 8) {
+                    load8(kb + (size_t)j * stride, kr[u]);
+                    load8(vb + (size_t)j * stride, vr[u]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < EPL; ++e) {
+                        kr[u][e] = to_f32(kb[(size_t)j * stride + e]);
+                        vr[u][e] = to_f32(vb[(size_t)j * stride + e]);
+                    }
+                }
             } else {
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) {
-                    kr[e] = to_f32(kb[(size_t)j * stride + e]);
-                    vr[e] = to_f32(vb[(size_t)j * stride + e]);
-                }
+                for (int e = 0; e < EPL; ++e) kr[u][e] = vr[u][e] = 0.f;
             }
-        } else {
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) kr[e] = vr[e] = 0.f;
         }
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) d0 = fmaf(qv[e], kr[e], d0);
+        for (int u = 0; u < kRowsU; ++u) {
+            float d0 = 0.f;
 #pragma unroll
-        for (int off = 8; off > 0; off >>= 1) d0 += __shfl_xor_sync(0xffffffffu, d0, off);
-        if (j >= 0) {
-            const float mn = fmaxf(m, d0);
-            const float c = (m == -INFINITY) ? 0.f : exp2f(m - mn);
-            const float p = exp2f(d0 - mn);
-            l = l * c + p;
+            for (int e = 0; e < EPL; ++e) d0 = fmaf(qv[e], kr[u][e], d0);
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) acc[e] = fmaf(p, vr[e], acc[e] * c);
-            m = mn;
+            for (int off = 8; off > 0; off >>= 1) d0 += __shfl_xor_sync(0xffffffffu, d0, off);
+            if (js[u] >= 0) {
+                const float mn = fmaxf(m, d0);
+                const float c = (m == -INFINITY) ? 0.f : exp2f(m - mn);
+                const float p = exp2f(d0 - mn);
+                l = l * c + p;
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) acc[e] = fmaf(p, vr[u][e], acc[e] * c);
+                m = mn;
+            }
         }
     }
     const int slot = warp * 2 + half;
